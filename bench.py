@@ -1,0 +1,356 @@
+"""Benchmark of the B200 Qwen3 forward path (config 0 of the benchmark set).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl soc|reference]
+
+Workload: Qwen3-0.6B architecture, random fp16 weights
+N(0, 0.02) seed 0 in the reference bundle format, batch 1, a 16-token prompt of
+ids uniform in [0, 151936) seed 1, prefill + 32 greedy decode steps.  One
+"step" = that whole generation job (prefill 16 + 32 decode steps, 33 generated
+ids).  Metric: decode tokens/s = generated ids per second of job time.
+
+* value        device-timed (CUDA events on the library stream) with the prompt
+               already resident in HBM (soc_b200_generate_device);
+* e2e          the same job through the public C ABI with host buffers
+               (soc_b200_generate: pinned prompt in, ids out, synchronous);
+* roofline     the decode step, timed as (job - prefill-only job) / 32: algorithmic
+               bytes = every weight byte read once + the KV bytes of the step;
+* cpu_baseline the reference CPU runtime (oracle/_ref) on a bounded sample.
+
+N > 1: one process per GPU (torchrun), each running its own replica of the job
+("replicas only": batch-1 decode of one sequence does not shard); value sums all
+ranks' ids over the max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tokens/s (B=1 & batched) Qwen3-0.6B shape; HBM GB/s vs 8 TB/s"
+PROMPT_LEN, NEW_TOKENS = 16, 33  # 1 id from the prefill + 32 decode steps
+SPEC_HBM_GBS = 8000.0
+
+
+def qwen06_bytes_per_decode_step(cfg: dict, ctx_len: int) -> float:
+    """Algorithmic HBM bytes of one batch-1 decode step at context ctx_len (keys incl. the new one)."""
+    H, I, L, D = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["head_dim"]
+    hq, hkv, V = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["vocab_size"]
+    lin = L * (H * (hq + 2 * hkv) * D + H * hq * D + 3 * H * I)
+    weights = 2 * (lin + V * H)                       # fp16 linears + tied lm_head
+    norms = 4 * (L * (2 * H + 2 * D) + H)              # fp32 norm vectors
+    kv_token = L * 2 * hkv * D * 2                     # fp16 K and V of one position, all layers
+    return float(weights + norms + kv_token * ctx_len + kv_token)
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="clocks", suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self) -> dict:
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(parts)
+            except ValueError:
+                pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def config0_bundle(rank: int, world: int, barrier):
+    from soc_b200.bundle import QWEN3_0_6B, cached_bundle
+    if rank == 0:
+        p = cached_bundle("config0", QWEN3_0_6B, seed=0, dtype="float16")
+    barrier()
+    if rank != 0:
+        p = cached_bundle("config0", QWEN3_0_6B, seed=0, dtype="float16")
+    return p
+
+
+def prompt_ids(cfg) -> np.ndarray:
+    return np.random.default_rng(1).integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.int32)
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args, rank, world):
+    """The reference CPU runtime (its sources compiled unchanged, oracle/_ref) on
+    this host's cores: one independent sequence per thread, one decode token per
+    thread per step; each thread first prefills a bounded 2-token prompt."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    from soc_b200.bundle import QWEN3_0_6B, cached_bundle
+    if not O.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libsocref.so was not built"}))
+        return
+    p = cached_bundle("config0", QWEN3_0_6B, seed=0, dtype="float16")
+    cores = O.host_cores()
+    threads = max(1, min(cores, int(os.environ.get("SOC_REF_THREADS", "32"))))
+    models = [O.RefModel(p, 64) for _ in range(threads)]
+    ids = prompt_ids(QWEN3_0_6B)[:2]
+    toks = [0] * threads
+    pos = [2] * threads
+
+    def prefill(i):
+        lg = models[i].forward(ids, 0)
+        toks[i] = models[i].sample(lg[-1])
+
+    def step(i):
+        lg = models[i].forward([toks[i]], pos[i])
+        toks[i] = models[i].sample(lg[0])
+        pos[i] += 1
+
+    def parallel(fn):
+        ts = [threading.Thread(target=fn, args=(i,)) for i in range(threads)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+
+    parallel(prefill)
+    for _ in range(args.warmup):
+        parallel(step)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        parallel(step)
+    dt = time.perf_counter() - t0
+    value = threads * args.steps / dt
+    sample = (f"{threads} threads x {args.steps} timed decode steps (after {args.warmup} warm-up) of independent "
+              f"Qwen3-0.6B sequences, each after a 2-token prefill (a bounded sample of config 0)")
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1000, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config0: Qwen3-0.6B fp16 batch-1 greedy decode", "host_threads": threads},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def cpu_baseline_sample() -> dict:
+    """Reference CPU runtime, 1 thread (it is single-threaded), on a bounded sample of
+    the config-0 workload: 2-token prompt, then 3 timed decode steps."""
+    from oracle import oracle as O
+    from soc_b200.bundle import QWEN3_0_6B, cached_bundle
+    if not O.ref_available():
+        return {"value": None, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                "sample": "unavailable: oracle/_ref not built"}
+    p = cached_bundle("config0", QWEN3_0_6B, seed=0, dtype="float16")
+    rm = O.RefModel(p, 64)
+    ids = prompt_ids(QWEN3_0_6B)[:2]
+    tok = rm.sample(rm.forward(ids, 0)[-1])
+    steps = 3
+    t0 = time.perf_counter()
+    for i in range(steps):
+        tok = rm.sample(rm.forward([tok], 2 + i)[0])
+    dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": "tokens/s", "cores": 1, "kind": "reference",
+            "sample": f"{steps} decode steps after a 2-token prefill, 1 thread of {O.host_cores()} host cores "
+                      f"(the reference runtime is single-threaded)"}
+
+
+# ----------------------------------------------------------------------- our arm
+def run_soc(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+    from soc_b200 import runtime as R
+    from soc_b200.bundle import QWEN3_0_6B
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    p = config0_bundle(rank, world, barrier)
+    ctx = R.Context(local)
+    model = R.Model(ctx, p)
+    kv = R.KVCache(model, 1, 256)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    prompt = prompt_ids(QWEN3_0_6B)
+    d_prompt = torch.from_numpy(prompt).cuda()
+    d_out = torch.zeros(NEW_TOKENS, dtype=torch.int32, device="cuda")
+
+    def job(max_new=NEW_TOKENS):
+        model.generate_device(kv, 0, d_prompt.data_ptr(), PROMPT_LEN, max_new, d_out.data_ptr())
+
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        job()
+        job(1)
+    ctx.synchronize()
+
+    def timed(fn, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        ctx.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        ctx.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        return e0.elapsed_time(e1)
+
+    launches0 = R.kernel_launches()
+    with ClockSampler(local) as clk:
+        ms_total = timed(job, args.steps)
+    launches = R.kernel_launches() - launches0
+    ms_prefill = timed(lambda: job(1), args.steps)
+    if world > 1:
+        t = torch.tensor([ms_total, ms_prefill], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total, ms_prefill = t.tolist()
+    greedy = d_out.cpu().tolist()
+
+    # e2e through the public ABI with host buffers (pinned prompt in, ids out).
+    h_prompt = torch.from_numpy(prompt).pin_memory()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = model.generate(kv, 0, h_prompt.numpy(), NEW_TOKENS)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = t.item()
+    assert out == greedy[: len(out)], "e2e and device runs disagree"
+
+    step_ms = ms_total / args.steps
+    decode_ms = (ms_total - ms_prefill) / args.steps / (NEW_TOKENS - 1)
+    cfg = QWEN3_0_6B
+    ctx_lens = [PROMPT_LEN + i for i in range(NEW_TOKENS - 1)]
+    alg_bytes = float(np.mean([qwen06_bytes_per_decode_step(cfg, c) for c in ctx_lens]))
+    peaks = load_peaks()
+    achieved = alg_bytes / (decode_ms * 1e-3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "decode_step_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_decode_step")
+
+    result = None
+    if rank == 0:
+        cpu = cpu_baseline_sample() if world == 1 and not args.no_cpu_baseline else None
+        result = {
+            "metric": METRIC,
+            "value": NEW_TOKENS * args.steps * world / (ms_total * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": step_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16w-f32a",
+            "data": "synthetic",
+            "impl": "soc_b200",
+            "config": {"workload": "config0: Qwen3-0.6B fp16 weights, batch 1, 16-token prompt + 32 greedy "
+                                   "decode steps (33 ids/job), ids seed 1, weights seed 0",
+                       "global_batch": world, "seq_len": PROMPT_LEN + NEW_TOKENS - 1,
+                       "parallelism": f"replicas{world}",
+                       "l2": "weights 1.19 GB per token > 126 MB L2; no flush needed"},
+            "decode_ms_per_token": decode_ms,
+            "prefill_ms": ms_prefill / args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                         "frac_of_8TBs": achieved / SPEC_HBM_GBS, "traffic": traffic,
+                         "unit_of_work": "one batch-1 decode step (all 28 layers + lm_head + argmax)",
+                         "algorithmic_bytes_per_step": alg_bytes},
+            "e2e": {"value": NEW_TOKENS * args.steps * world / e2e_s, "unit": "tokens/s",
+                    "h2d_bytes_per_step": PROMPT_LEN * 4, "d2h_bytes_per_step": NEW_TOKENS * 4},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "greedy_ids_head": greedy[:8],
+        }
+        if cpu is not None:
+            result["cpu_baseline"] = cpu
+    kv.free()
+    model.free()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="soc", choices=["soc", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_soc(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,146 @@
+/*
+ * soc_b200 -- C ABI of the B200-native Qwen3 forward path.
+ *
+ * Drop-in boundary for the reference runtime's hot path (SongWooYoung/SoC):
+ * the entry points below replace, one for one, what a host runtime calls on
+ * the reference's model objects.  Plain pointers and sizes only; every call
+ * returns 0 (SOC_B200_OK) or a negative status, with a thread-local message
+ * in soc_b200_last_error() (the reference throws std::runtime_error, e.g.
+ * Mac/cpu/src/linear.cpp:9-11, or returns bool + std::string*,
+ * Mac/gpu/src/runtime/generation_context.cpp:97-101).
+ *
+ * Ownership: the library owns all device memory it allocates; host buffers
+ * passed in are copied before the call returns.  Threading: one CUDA stream
+ * per context; calls on one context (and on the models and caches made from
+ * it) must be serialised by the caller, as with the reference's
+ * GenerationContext (not thread-safe).
+ */
+#ifndef SOC_B200_H
+#define SOC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SOC_B200_API __attribute__((visibility("default")))
+#else
+#define SOC_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SOC_B200_OK 0
+#define SOC_B200_ERR_INVALID (-1)   /* bad argument, shape or state */
+#define SOC_B200_ERR_CUDA (-2)      /* CUDA runtime failure */
+#define SOC_B200_ERR_IO (-3)        /* file missing / short */
+#define SOC_B200_ERR_FORMAT (-4)    /* manifest or tensor record rejected */
+#define SOC_B200_ERR_CAPACITY (-5)  /* KV cache or workspace exhausted */
+#define SOC_B200_ERR_RANGE (-6)     /* token id outside [0, vocab) */
+#define SOC_B200_ERR_DEVICE (-7)    /* a kernel reported an error status */
+
+/* Weight formats for soc_b200_load_bundle / soc_b200_linear. */
+#define SOC_B200_WEIGHTS_NATIVE 0   /* whatever the bundle stores */
+#define SOC_B200_WEIGHTS_F16 1
+#define SOC_B200_WEIGHTS_BF16 2
+#define SOC_B200_WEIGHTS_INT8_G64 3 /* group 64 along in_features, fp16 scales */
+#define SOC_B200_WEIGHTS_INT4_G32 4 /* group 32, two per byte (low nibble first), fp16 scales */
+
+typedef struct soc_ctx soc_ctx;
+typedef struct soc_model soc_model;
+typedef struct soc_kv soc_kv;
+
+typedef struct {
+    int layers, hidden, intermediate, q_heads, kv_heads, head_dim, vocab;
+    int tied_embeddings;   /* lm_head aliases the embedding table */
+    int weight_format;     /* SOC_B200_WEIGHTS_* of the block linears */
+    int max_position;      /* rows of the RoPE table */
+    float rms_norm_eps;
+    double rope_theta;
+} soc_model_info;
+
+/* Message of the last failed call on this thread ("" if none). */
+SOC_B200_API const char* soc_b200_last_error(void);
+
+/* Kernels launched by this library in this process so far (a CUDA-graph
+ * replay counts every kernel node).  No counterpart in the reference, which
+ * has no device kernels; used to attribute device work in benchmarks. */
+SOC_B200_API long long soc_b200_kernel_launches(void);
+
+/* Open device `device` (one stream).  Replaces MetalContext::CreateDefault
+ * (Mac/gpu/src/metal/metal_context.mm:78). */
+SOC_B200_API int soc_b200_open(int device, soc_ctx** out);
+SOC_B200_API void soc_b200_close(soc_ctx* ctx);
+/* Wait for all work queued on the context's stream. */
+SOC_B200_API int soc_b200_synchronize(soc_ctx* ctx);
+/* The context's cudaStream_t (for event timing by the caller). */
+SOC_B200_API void* soc_b200_stream(soc_ctx* ctx);
+
+/* Load a soc.cpp.llm_export v2 bundle into device memory.  Validation and
+ * error text follow ManifestLoader::LoadFromFile + StartupValidator::
+ * ValidateManifest + QwenModelLoader::LoadModel (Mac/cpu/src/runtime_assets.cpp:
+ * 138-168, startup_validator.cpp:5-23, qwen_model_loader.cpp:35-93) and
+ * WeightLoader::LoadTensor (weight_loader.cpp:17-30).  tp_size must be 1 in
+ * this version (tp_rank 0, nccl_comm NULL). */
+SOC_B200_API int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_format, int tp_rank, int tp_size,
+                         void* nccl_comm, soc_model** out);
+SOC_B200_API int soc_b200_model_info(const soc_model* model, soc_model_info* out);
+SOC_B200_API void soc_b200_free_model(soc_model* model);
+
+/* Paged fp16 KV cache for up to max_seqs sequences and max_tokens cached
+ * tokens in total, page_tokens per page (16).  Replaces TensorKVCache
+ * (Mac/cpu/src/kv_cache.cpp:20-44) and the Metal KVCache::CreateShared. */
+SOC_B200_API int soc_b200_kv_create(soc_model* model, int max_seqs, int max_tokens, int page_tokens, soc_kv** out);
+SOC_B200_API void soc_b200_free_kv(soc_kv* kv);
+/* Drop a sequence's cached tokens (TensorKVCache::ClearSequence, kv_cache.cpp:112-115). */
+SOC_B200_API int soc_b200_kv_reset(soc_kv* kv, int seq);
+/* Cached length of a sequence (TensorKVCache::length), or a negative status. */
+SOC_B200_API int soc_b200_kv_length(const soc_kv* kv, int seq);
+/* Positions [start, end) of one layer as float32 [end-start, kv_heads, head_dim]
+ * K and V (TensorKVCache::Read, kv_cache.cpp:80-110). */
+SOC_B200_API int soc_b200_kv_read(soc_kv* kv, int seq, int layer, int start, int end, float* k, float* v);
+/* Write positions [start, end) of one layer from float32 host rows (rounded to
+ * fp16); extends the sequence length to `end` (TensorKVCache::Write, kv_cache.cpp:50-78). */
+SOC_B200_API int soc_b200_kv_write(soc_kv* kv, int seq, int layer, int start, int end, const float* k, const float* v);
+
+/* Append n tokens to sequence `seq` at its current length and run them
+ * through the model (QwenCausalLM::ForwardLogitsCached with position_offset =
+ * cached length, Mac/cpu/src/qwen_causal_lm.cpp:74-80).  logits_last (nullable)
+ * receives the vocab logits of the last token; next_id (nullable) its greedy
+ * id (Sampler::SampleFromLogits, top_k 1). */
+SOC_B200_API int soc_b200_prefill(soc_model* model, soc_kv* kv, int seq, const int32_t* ids, int n, float* logits_last,
+                     int32_t* next_id);
+
+/* One decode step for n_seqs distinct sequences, each appending last_ids[i]
+ * (GenerationContext::DecodeNextToken, Mac/gpu/src/runtime/generation_context.cpp:
+ * 61-116, batched and ragged).  logits (nullable) receives [n_seqs, vocab]. */
+SOC_B200_API int soc_b200_decode(soc_model* model, soc_kv* kv, int n_seqs, const int* seq_ids, const int32_t* last_ids,
+                    float* logits, int32_t* next_ids);
+
+/* Reset `seq`, prefill the prompt and decode greedily up to max_new tokens,
+ * stopping after eos_token_id when it is >= 0 (GenerationContext::Generate,
+ * generation_context.cpp:118-172).  out_ids must hold max_new ids; *n_out
+ * receives the count.  The decode steps run back to back on the device. */
+SOC_B200_API int soc_b200_generate(soc_model* model, soc_kv* kv, int seq, const int32_t* prompt, int n_prompt, int max_new,
+                      int eos_token_id, int32_t* out_ids, int* n_out);
+
+/* As soc_b200_generate with DEVICE pointers for the prompt and the max_new
+ * output ids, no EOS stop and no host synchronisation (work is queued on the
+ * context stream). */
+SOC_B200_API int soc_b200_generate_device(soc_model* model, soc_kv* kv, int seq, const int32_t* d_prompt, int n_prompt,
+                             int max_new, int32_t* d_out);
+
+/* Kernel-level linear: y[r, :] = W x[r, :] for r < rows, all DEVICE pointers,
+ * W [out_features, in_features] in `weight_format` (scales [out, in/group] fp16
+ * for the int formats, else NULL), x [rows, in] fp32, y [rows, out] fp32.
+ * Restates Linear::Forward (Mac/cpu/src/linear.cpp:51-84).  stream may be NULL
+ * (the context stream). */
+SOC_B200_API int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* scales, int out_features,
+                    int in_features, const float* x, int rows, float* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SOC_B200_H */

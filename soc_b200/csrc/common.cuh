@@ -1,0 +1,100 @@
+// Shared definitions of the soc_b200 CUDA library (host + device).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace socb {
+
+// Library error with a C-ABI status code.
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define SOCB_CUDA(expr)                                                                            \
+    do {                                                                                           \
+        cudaError_t e_ = (expr);                                                                   \
+        if (e_ != cudaSuccess)                                                                     \
+            throw ::socb::Error(-2, std::string("CUDA error: ") + cudaGetErrorString(e_) + " at " + \
+                                    __FILE__ + ":" + std::to_string(__LINE__) + " (" #expr ")");  \
+    } while (0)
+
+// Weight element formats of the linear layers.
+enum WFmt : int { WF_F16 = 1, WF_BF16 = 2, WF_I8G64 = 3, WF_I4G32 = 4 };
+
+// Linear epilogues.
+enum LinMode : int {
+    LIN_STORE = 0,     // y = W x
+    LIN_RESIDUAL = 1,  // y += W x            (o_proj / down_proj into the residual stream)
+    LIN_SWIGLU = 2,    // rows (2j, 2j+1) = (gate_j, up_j): y[j] = silu(gate) * up
+};
+
+// Device-side error bits (kernels never trap; they record and skip).
+enum DevErr : int {
+    DERR_TOKEN_RANGE = 1,
+    DERR_KV_RANGE = 2,
+    DERR_WAIT_TIMEOUT = 4,
+};
+
+// ------------------------------------------------------------------ device helpers
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// 16-byte streaming load that bypasses L1 (weights are read exactly once per pass).
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float2 h2_to_f2(uint32_t u) {
+    __half2 h = *reinterpret_cast<__half2*>(&u);
+    return __half22float2(h);
+}
+
+__device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
+    // bf16 -> f32 is a 16-bit shift (exact).
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+template <typename T>
+struct WTraits;
+template <>
+struct WTraits<__half> {
+    static __device__ __forceinline__ float2 pair(uint32_t u) { return h2_to_f2(u); }
+};
+template <>
+struct WTraits<__nv_bfloat16> {
+    static __device__ __forceinline__ float2 pair(uint32_t u) { return bf2_to_f2(u); }
+};
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+// Orderable key for (value, index) argmax with the lowest index winning ties.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(b) << 32) | static_cast<uint32_t>(0x7fffffff - idx);
+}
+__device__ __forceinline__ int argmax_key_index(unsigned long long k) {
+    return 0x7fffffff - static_cast<int>(static_cast<uint32_t>(k & 0xffffffffull));
+}
+
+}  // namespace socb

@@ -1,0 +1,562 @@
+// Modular sm_100a kernels of the Qwen3 forward (prefill and batched decode).
+//
+// Reference arithmetic they restate (SongWooYoung/SoC, Mac/cpu/src):
+//   embedding gather      embedding.cpp:51-77
+//   RMSNorm               rms_norm_module.cpp:52-66   (x * (1/sqrt(mean(x^2)+eps)) * w)
+//   Linear                linear.cpp:69-81            (fp32 accumulate of fp32 x times decoded weight)
+//   q/k norm + RoPE       qwen_attention.cpp:168-171, rope.cpp:54-89 (rotate-half, double angle)
+//   KV write              qwen_attention.cpp:180-193  (post-RoPE K, raw V)
+//   GQA attention         grouped_query_attention.cpp:59-142 (scale 1/sqrt(D), causal, kv = h / group)
+//   SwiGLU                qwen_mlp.cpp:20-74          (g / (1 + exp(-g)) * up)
+//   greedy sampler        sampler.cpp:26-62           (first strict maximum)
+// The B200 layout differs from the reference: the KV cache is paged fp16, q/k/v are one
+// fused matrix, gate/up rows are interleaved so one warp owns a (gate, up) pair.
+#include <atomic>
+
+#include "kernels.h"
+
+namespace socb {
+
+static std::atomic<long long> g_launches{0};
+void count_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+long long launches_so_far() { return g_launches.load(std::memory_order_relaxed); }
+
+// ------------------------------------------------------------------------ helpers
+__device__ __forceinline__ uint4 ld_nc16(const void* p) {
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p));
+    return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&w)[8]) {
+    float2 a = WTraits<T>::pair(u.x), b = WTraits<T>::pair(u.y), c = WTraits<T>::pair(u.z),
+           d = WTraits<T>::pair(u.w);
+    w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y;
+    w[4] = c.x; w[5] = c.y; w[6] = d.x; w[7] = d.y;
+}
+
+// --------------------------------------------------------------------- embedding
+template <typename T>
+__global__ void k_embed(const T* __restrict__ table, int H, int V, const int* __restrict__ tokens,
+                        float* __restrict__ h, int* err) {
+    const int row = blockIdx.x;
+    const int tok = tokens[row];
+    float* out = h + static_cast<size_t>(row) * H;
+    if (tok < 0 || tok >= V) {
+        if (threadIdx.x == 0) atomicOr(err, DERR_TOKEN_RANGE);
+        for (int i = threadIdx.x; i < H; i += blockDim.x) out[i] = 0.0f;
+        return;
+    }
+    const T* src = table + static_cast<size_t>(tok) * H;
+    for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+        float w[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(src + i), w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) out[i + j] = w[j];
+    }
+}
+
+void launch_embed(int wfmt, const void* table, int hidden, int vocab, const int* tokens, int rows, float* h,
+                  int* err, cudaStream_t st) {
+    if (rows <= 0) return;
+    if (wfmt == WF_BF16)
+        k_embed<__nv_bfloat16><<<rows, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(table), hidden, vocab,
+                                                      tokens, h, err);
+    else
+        k_embed<__half><<<rows, 128, 0, st>>>(static_cast<const __half*>(table), hidden, vocab, tokens, h, err);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+// ----------------------------------------------------------------------- RMSNorm
+__global__ void k_rmsnorm(const float* __restrict__ x, int n, const float* __restrict__ w, float eps,
+                          float* __restrict__ y) {
+    __shared__ float red[32];
+    const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
+    float* yr = y + static_cast<size_t>(blockIdx.x) * n;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float s = 1.0f / sqrtf(red[0] / static_cast<float>(n) + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = xr[i] * s * w[i];
+}
+
+void launch_rmsnorm(const float* x, int rows, int n, const float* w, float eps, float* y, cudaStream_t st) {
+    if (rows <= 0) return;
+    k_rmsnorm<<<rows, 256, 0, st>>>(x, n, w, eps, y);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+// ------------------------------------------------------------------------ linear
+// One CTA = 8 warps = 16 output rows (a warp owns a row pair) x RB input rows staged in
+// shared memory.  Every lane streams 16-byte weight vectors (8 elements) with the
+// loads of UNR iterations issued before their FMAs, fp32 accumulation, warp-shuffle
+// reduction.  The RMSNorm of the input rows (when norm_w != nullptr) is computed in
+// the prologue, so the normalised activations never touch HBM.
+constexpr int LIN_WARPS = 8;
+constexpr int LIN_THREADS = LIN_WARPS * 32;
+
+template <typename T, int RB>
+__global__ void __launch_bounds__(LIN_THREADS) k_linear(const T* __restrict__ W, int out_f, int in_f,
+                                                        const float* __restrict__ x, int ldx, int rows,
+                                                        const float* __restrict__ norm_w, float eps,
+                                                        float* __restrict__ y, int ldy, int mode) {
+    extern __shared__ float4 xs4[];
+    float* xs = reinterpret_cast<float*>(xs4);
+    __shared__ float red[RB][LIN_WARPS];
+    __shared__ float scale_s[RB];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int r0 = blockIdx.y * RB;
+    const int nr = min(RB, rows - r0);
+
+    // Stage the input rows (fp32) in shared memory.
+    for (int r = 0; r < RB; ++r) {
+        float ss = 0.0f;
+        for (int i = tid * 4; i < in_f; i += LIN_THREADS * 4) {
+            float4 v = r < nr ? *reinterpret_cast<const float4*>(x + static_cast<size_t>(r0 + r) * ldx + i)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            xs4[(r * in_f + i) >> 2] = v;
+        }
+        if (norm_w != nullptr) {
+            ss = warp_sum(ss);
+            if (lane == 0) red[r][warp] = ss;
+        }
+    }
+    if (norm_w != nullptr) {
+        __syncthreads();
+        if (tid < RB) {
+            float t = 0.0f;
+            for (int wi = 0; wi < LIN_WARPS; ++wi) t += red[tid][wi];
+            scale_s[tid] = 1.0f / sqrtf(t / static_cast<float>(in_f) + eps);
+        }
+        __syncthreads();
+        for (int r = 0; r < RB; ++r) {
+            const float s = scale_s[r];
+            for (int i = tid; i < in_f; i += LIN_THREADS) xs[r * in_f + i] = xs[r * in_f + i] * s * norm_w[i];
+        }
+    }
+    __syncthreads();
+
+    const int pair = blockIdx.x * LIN_WARPS + warp;
+    const int o0 = 2 * pair;
+    if (o0 >= out_f) return;
+    const bool has1 = (o0 + 1) < out_f;
+    const T* w0 = W + static_cast<size_t>(o0) * in_f;
+    const T* w1 = has1 ? w0 + in_f : w0;
+
+    float acc0[RB], acc1[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) acc0[r] = acc1[r] = 0.0f;
+
+    constexpr int UNR = 4;
+    const int step = 32 * 8;
+    int k = lane * 8;
+    for (; k + (UNR - 1) * step < in_f; k += UNR * step) {
+        uint4 ua[UNR], ub[UNR];
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+            ua[u] = ld_nc16(w0 + k + u * step);
+            ub[u] = ld_nc16(w1 + k + u * step);
+        }
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+            float wa[8], wb[8];
+            unpack8<T>(ua[u], wa);
+            unpack8<T>(ub[u], wb);
+            const int kk = k + u * step;
+#pragma unroll
+            for (int r = 0; r < RB; ++r) {
+                const float4 xa = xs4[(r * in_f + kk) >> 2];
+                const float4 xb = xs4[(r * in_f + kk + 4) >> 2];
+                acc0[r] += wa[0] * xa.x + wa[1] * xa.y + wa[2] * xa.z + wa[3] * xa.w + wa[4] * xb.x +
+                           wa[5] * xb.y + wa[6] * xb.z + wa[7] * xb.w;
+                acc1[r] += wb[0] * xa.x + wb[1] * xa.y + wb[2] * xa.z + wb[3] * xa.w + wb[4] * xb.x +
+                           wb[5] * xb.y + wb[6] * xb.z + wb[7] * xb.w;
+            }
+        }
+    }
+    for (; k < in_f; k += step) {
+        float wa[8], wb[8];
+        unpack8<T>(ld_nc16(w0 + k), wa);
+        unpack8<T>(ld_nc16(w1 + k), wb);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+            const float4 xa = xs4[(r * in_f + k) >> 2];
+            const float4 xb = xs4[(r * in_f + k + 4) >> 2];
+            acc0[r] += wa[0] * xa.x + wa[1] * xa.y + wa[2] * xa.z + wa[3] * xa.w + wa[4] * xb.x + wa[5] * xb.y +
+                       wa[6] * xb.z + wa[7] * xb.w;
+            acc1[r] += wb[0] * xa.x + wb[1] * xa.y + wb[2] * xa.z + wb[3] * xa.w + wb[4] * xb.x + wb[5] * xb.y +
+                       wb[6] * xb.z + wb[7] * xb.w;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+        acc0[r] = warp_sum(acc0[r]);
+        acc1[r] = warp_sum(acc1[r]);
+    }
+    if (lane < nr) {
+        // lane r writes input row r (register arrays indexed by a compile-time loop).
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+            if (r != lane) continue;
+            float* yr = y + static_cast<size_t>(r0 + r) * ldy;
+            if (mode == LIN_SWIGLU) {
+                yr[pair] = silu_f(acc0[r]) * acc1[r];
+            } else if (mode == LIN_RESIDUAL) {
+                yr[o0] += acc0[r];
+                if (has1) yr[o0 + 1] += acc1[r];
+            } else {
+                yr[o0] = acc0[r];
+                if (has1) yr[o0 + 1] = acc1[r];
+            }
+        }
+    }
+}
+
+template <typename T, int RB>
+static void linear_rb(const T* W, int out_f, int in_f, const float* x, int ldx, int rows, const float* norm_w,
+                      float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    const size_t smem = static_cast<size_t>(RB) * in_f * sizeof(float);
+    static bool attr_set = false;  // one attribute set per template instance
+    if (!attr_set) {
+        SOCB_CUDA(cudaFuncSetAttribute(k_linear<T, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr_set = true;
+    }
+    const int pairs = (out_f + 1) / 2;
+    dim3 grid((pairs + LIN_WARPS - 1) / LIN_WARPS, (rows + RB - 1) / RB);
+    k_linear<T, RB><<<grid, LIN_THREADS, smem, st>>>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+template <typename T>
+static void linear_t(const T* W, int out_f, int in_f, const float* x, int ldx, int rows, const float* norm_w,
+                     float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    // Largest row block whose fp32 staging fits in 96 KB of shared memory.
+    const size_t cap = 96 * 1024 / (static_cast<size_t>(in_f) * sizeof(float));
+    if (rows >= 8 && cap >= 8)
+        linear_rb<T, 8>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+    else if (rows >= 4 && cap >= 4)
+        linear_rb<T, 4>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+    else if (rows >= 2 && cap >= 2)
+        linear_rb<T, 2>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+    else
+        linear_rb<T, 1>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+}
+
+void launch_linear(int wfmt, const void* W, const void* scales, int out_f, int in_f, const float* x, int ldx,
+                   int rows, const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    (void)scales;
+    if (rows <= 0 || out_f <= 0) return;
+    if (in_f % 8 != 0 || ldx % 4 != 0) throw Error(-1, "linear: in_features and ldx must be multiples of 8 and 4");
+    if (static_cast<size_t>(in_f) * sizeof(float) > 200 * 1024) throw Error(-1, "linear: in_features too large");
+    if (wfmt == WF_BF16)
+        linear_t(static_cast<const __nv_bfloat16*>(W), out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+    else if (wfmt == WF_F16)
+        linear_t(static_cast<const __half*>(W), out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+    else
+        throw Error(-1, "linear: unsupported weight format");
+}
+
+// ------------------------------------------------- q/k RMSNorm + RoPE + paged KV append
+// One CTA per row; warp w handles heads w, w+8, ... over the (q | k | v) head list.
+// Lane l holds DL = D/32 consecutive dims; the rotate-half partner of dim i < D/2 lives
+// in lane l ^ 16.  cos/sin come from a host table built in double precision exactly as
+// the reference computes them (rope.cpp:74-79), so angles match bit for bit.
+template <int D>
+__global__ void __launch_bounds__(256) k_qk_norm_rope_kv(const float* __restrict__ qkv, int hq, int hkv,
+                                                         const float* __restrict__ qn_w,
+                                                         const float* __restrict__ kn_w, float eps,
+                                                         const float2* __restrict__ rope_cs, int rope_len,
+                                                         const int* __restrict__ row_seq,
+                                                         const int* __restrict__ row_pos, KVLayerView kv,
+                                                         float* __restrict__ q_out, int* err) {
+    constexpr int DL = D / 32;
+    constexpr int HALF = D / 2;
+    const int row = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int pos = row_pos[row];
+    const int seq = row_seq[row];
+    const int nh = hq + 2 * hkv;
+    const float* src_row = qkv + static_cast<size_t>(row) * nh * D;
+    const int page_idx = pos / kv.page_tokens;
+    const bool pos_ok = pos >= 0 && pos < rope_len && page_idx < kv.max_pages;
+    if (!pos_ok) {
+        if (threadIdx.x == 0) atomicOr(err, DERR_KV_RANGE);
+        return;
+    }
+    const int page = kv.page_table[static_cast<size_t>(seq) * kv.max_pages + page_idx];
+    const int slot = pos % kv.page_tokens;
+    for (int h = warp; h < nh; h += 8) {
+        const float* src = src_row + h * D + lane * DL;
+        float v[DL];
+#pragma unroll
+        for (int j = 0; j < DL; ++j) v[j] = src[j];
+        const bool is_v = h >= hq + hkv;
+        if (is_v) {
+            const int kvh = h - hq - hkv;
+            __half* dst = kv.v + ((static_cast<size_t>(page) * hkv + kvh) * kv.page_tokens + slot) * D + lane * DL;
+#pragma unroll
+            for (int j = 0; j < DL; ++j) dst[j] = __float2half_rn(v[j]);
+            continue;
+        }
+        const bool is_q = h < hq;
+        const float* nw = is_q ? qn_w : kn_w;
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < DL; ++j) ss += v[j] * v[j];
+        ss = warp_sum(ss);
+        const float s = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+        for (int j = 0; j < DL; ++j) v[j] = v[j] * s * nw[lane * DL + j];
+        // rotate-half
+        float o[DL];
+        const bool first = lane < 16;
+#pragma unroll
+        for (int j = 0; j < DL; ++j) {
+            const float partner = __shfl_xor_sync(0xffffffffu, v[j], 16);
+            const int i = (lane * DL + j) % HALF;  // pair index
+            const float2 cs = rope_cs[static_cast<size_t>(pos) * HALF + i];
+            o[j] = first ? (v[j] * cs.x - partner * cs.y) : (partner * cs.y + v[j] * cs.x);
+        }
+        if (is_q) {
+            float* dst = q_out + (static_cast<size_t>(row) * hq + h) * D + lane * DL;
+#pragma unroll
+            for (int j = 0; j < DL; ++j) dst[j] = o[j];
+        } else {
+            const int kvh = h - hq;
+            __half* dst = kv.k + ((static_cast<size_t>(page) * hkv + kvh) * kv.page_tokens + slot) * D + lane * DL;
+#pragma unroll
+            for (int j = 0; j < DL; ++j) dst[j] = __float2half_rn(o[j]);
+        }
+    }
+}
+
+void launch_qk_norm_rope_kv(const float* qkv, const Rows& rows, int hq, int hkv, int head_dim, const float* qn_w,
+                            const float* kn_w, float eps, const float2* rope_cs, int rope_len, const KVLayerView& kv,
+                            float* q_out, int* err, cudaStream_t st) {
+    if (rows.n <= 0) return;
+    if (head_dim == 128)
+        k_qk_norm_rope_kv<128><<<rows.n, 256, 0, st>>>(qkv, hq, hkv, qn_w, kn_w, eps, rope_cs, rope_len, rows.seq,
+                                                       rows.pos, kv, q_out, err);
+    else if (head_dim == 64)
+        k_qk_norm_rope_kv<64><<<rows.n, 256, 0, st>>>(qkv, hq, hkv, qn_w, kn_w, eps, rope_cs, rope_len, rows.seq,
+                                                      rows.pos, kv, q_out, err);
+    else
+        throw Error(-1, "head_dim must be 64 or 128");
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+// --------------------------------------------------------------------- attention
+// Split-K causal GQA over the paged fp16 cache.  CTA = (row, kv head, key split);
+// its 4 warps take keys round-robin and keep an online softmax per query head of the
+// group, then merge through shared memory.  With one split the CTA writes the
+// normalised output; otherwise it writes (m, l, o) partials for k_attn_combine.
+constexpr int ATT_WARPS = 4;
+constexpr int ATT_MAXG = 8;
+
+template <int D>
+__global__ void __launch_bounds__(ATT_WARPS * 32) k_attention(const float* __restrict__ q,
+                                                              const int* __restrict__ row_seq,
+                                                              const int* __restrict__ row_pos, int hq, int hkv,
+                                                              KVLayerView kv, int n_splits,
+                                                              float* __restrict__ out, float* __restrict__ part) {
+    constexpr int DL = D / 32;
+    __shared__ float sm_m[ATT_WARPS][ATT_MAXG], sm_l[ATT_WARPS][ATT_MAXG];
+    __shared__ float sm_o[ATT_WARPS][ATT_MAXG][D];
+    const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int G = hq / hkv;
+    const int seq = row_seq[row];
+    const int nvis = row_pos[row] + 1;
+    // Key range of this split, derived per row so a captured graph stays valid as rows grow.
+    const int chunk = ((nvis + n_splits - 1) / n_splits + 15) / 16 * 16;
+    const int kb = split * chunk;
+    const int ke = min(nvis, kb + chunk);
+    const float scale = 1.0f / sqrtf(static_cast<float>(D));
+
+    float qr[ATT_MAXG][DL];
+#pragma unroll
+    for (int g = 0; g < ATT_MAXG; ++g) {
+        if (g < G) {
+            const float* qp = q + (static_cast<size_t>(row) * hq + kvh * G + g) * D + lane * DL;
+#pragma unroll
+            for (int j = 0; j < DL; ++j) qr[g][j] = qp[j];
+        }
+    }
+    float m[ATT_MAXG], l[ATT_MAXG], o[ATT_MAXG][DL];
+#pragma unroll
+    for (int g = 0; g < ATT_MAXG; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < DL; ++j) o[g][j] = 0.0f;
+    }
+    const int* pt = kv.page_table + static_cast<size_t>(seq) * kv.max_pages;
+    for (int p = kb + warp; p < ke; p += ATT_WARPS) {
+        const int page = pt[p / kv.page_tokens];
+        const size_t off = ((static_cast<size_t>(page) * hkv + kvh) * kv.page_tokens + (p % kv.page_tokens)) * D +
+                           lane * DL;
+        float kf[DL], vf[DL];
+#pragma unroll
+        for (int j = 0; j < DL; ++j) {
+            kf[j] = __half2float(kv.k[off + j]);
+            vf[j] = __half2float(kv.v[off + j]);
+        }
+#pragma unroll
+        for (int g = 0; g < ATT_MAXG; ++g) {
+            if (g >= G) break;
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < DL; ++j) s += qr[g][j] * kf[j];
+            s = warp_sum(s) * scale;
+            const float mn = fmaxf(m[g], s);
+            const float corr = expf(m[g] - mn);
+            const float pe = expf(s - mn);
+            l[g] = l[g] * corr + pe;
+#pragma unroll
+            for (int j = 0; j < DL; ++j) o[g][j] = o[g][j] * corr + pe * vf[j];
+            m[g] = mn;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < ATT_MAXG; ++g) {
+        if (g >= G) break;
+        if (lane == 0) {
+            sm_m[warp][g] = m[g];
+            sm_l[warp][g] = l[g];
+        }
+#pragma unroll
+        for (int j = 0; j < DL; ++j) sm_o[warp][g][lane * DL + j] = o[g][j];
+    }
+    __syncthreads();
+    // Merge the warps: thread t handles (g, d) pairs.
+    for (int idx = threadIdx.x; idx < G * D; idx += ATT_WARPS * 32) {
+        const int g = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (int w = 0; w < ATT_WARPS; ++w) M = fmaxf(M, sm_m[w][g]);
+        float L = 0.0f, acc = 0.0f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < ATT_WARPS; ++w) {
+                const float f = sm_m[w][g] == -INFINITY ? 0.0f : expf(sm_m[w][g] - M);
+                L += sm_l[w][g] * f;
+                acc += sm_o[w][g][d] * f;
+            }
+        }
+        const int h = kvh * G + g;
+        if (n_splits == 1) {
+            out[(static_cast<size_t>(row) * hq + h) * D + d] = L > 0.0f ? acc / L : 0.0f;
+        } else {
+            float* pp = part + ((static_cast<size_t>(row) * hq + h) * n_splits + split) * (D + 2);
+            pp[d] = acc;
+            if (d == 0) {
+                pp[D] = M;
+                pp[D + 1] = L;
+            }
+        }
+    }
+}
+
+template <int D>
+__global__ void k_attn_combine(const float* __restrict__ part, int hq, int n_splits, float* __restrict__ out) {
+    const int row = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    const float* pp = part + (static_cast<size_t>(row) * hq + h) * n_splits * (D + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, pp[s * (D + 2) + D]);
+    float L = 0.0f, acc = 0.0f;
+    if (M != -INFINITY) {
+        for (int s = 0; s < n_splits; ++s) {
+            const float ms = pp[s * (D + 2) + D];
+            const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
+            L += pp[s * (D + 2) + D + 1] * f;
+            acc += pp[s * (D + 2) + d] * f;
+        }
+    }
+    out[(static_cast<size_t>(row) * hq + h) * D + d] = L > 0.0f ? acc / L : 0.0f;
+}
+
+int attention_splits(int rows, int hkv, int max_visible) {
+    const int ctas = rows * hkv;
+    int splits = (2 * 148 + ctas - 1) / ctas;
+    const int max_by_len = (max_visible + 63) / 64;
+    if (splits > max_by_len) splits = max_by_len;
+    if (splits < 1) splits = 1;
+    return splits;
+}
+
+void launch_attention(const float* q, const Rows& rows, int splits, int hq, int hkv, int head_dim,
+                      const KVLayerView& kv, float* out, float* scratch, size_t scratch_floats, cudaStream_t st) {
+    if (rows.n <= 0) return;
+    if (hq % hkv != 0 || hq / hkv > ATT_MAXG) throw Error(-1, "attention: unsupported head grouping");
+    if (splits < 1) splits = 1;
+    const size_t need = static_cast<size_t>(rows.n) * hq * splits * (head_dim + 2);
+    if (splits > 1 && (scratch == nullptr || need > scratch_floats)) throw Error(-5, "attention: split-K scratch too small");
+    dim3 grid(rows.n, hkv, splits);
+    if (head_dim == 128) {
+        k_attention<128><<<grid, ATT_WARPS * 32, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out,
+                                                          scratch);
+        if (splits > 1) k_attn_combine<128><<<dim3(rows.n, hq), 128, 0, st>>>(scratch, hq, splits, out);
+    } else if (head_dim == 64) {
+        k_attention<64><<<grid, ATT_WARPS * 32, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out,
+                                                         scratch);
+        if (splits > 1) k_attn_combine<64><<<dim3(rows.n, hq), 64, 0, st>>>(scratch, hq, splits, out);
+    } else {
+        throw Error(-1, "head_dim must be 64 or 128");
+    }
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(splits > 1 ? 2 : 1);
+}
+
+// ------------------------------------------------------------------------ argmax
+// Greedy pick per row: maximum logit, lowest index on ties (the reference's
+// partial_sort with top_k = 1 keeps the first strict maximum).  NaNs never win.
+__global__ void k_argmax(const float* __restrict__ logits, int V, int ld, int* __restrict__ next_ids) {
+    __shared__ unsigned long long red[32];
+    const float* row = logits + static_cast<size_t>(blockIdx.x) * ld;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = row[i];
+        if (v != v) continue;
+        const unsigned long long k = argmax_key(v, i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        unsigned long long b = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+            b = other > b ? other : b;
+        }
+        if (threadIdx.x == 0) next_ids[blockIdx.x] = b == 0ull ? 0 : argmax_key_index(b);
+    }
+}
+
+void launch_argmax(const float* logits, int vocab, int ld, int rows, int* next_ids, cudaStream_t st) {
+    if (rows <= 0) return;
+    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, next_ids);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+}  // namespace socb

@@ -1,0 +1,51 @@
+// Host launchers of the modular Qwen3 kernels (kernels.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace socb {
+
+// Number of kernels this library has launched (graph replays add their kernel count).
+void count_launches(long long n);
+long long launches_so_far();
+
+// Paged KV cache view of one layer: pool [pages][kv_heads][page_tokens][head_dim] fp16.
+struct KVLayerView {
+    __half* k;
+    __half* v;
+    const int* page_table;  // [max_seqs][max_pages]
+    int max_pages;
+    int page_tokens;
+};
+
+// Per-forward row descriptors (one row = one token of some sequence), all device pointers.
+struct Rows {
+    const int* tokens;  // [n]
+    const int* seq;     // [n]
+    const int* pos;     // [n] absolute position of the row's token
+    int n;
+};
+
+void launch_embed(int wfmt, const void* table, int hidden, int vocab, const int* tokens, int rows, float* h,
+                  int* err, cudaStream_t st);
+
+// y[r, o] (mode)= sum_i x'[r, i] * W[o, i], x' = rmsnorm(x[r], norm_w) when norm_w != nullptr.
+void launch_linear(int wfmt, const void* W, const void* scales, int out_f, int in_f, const float* x, int ldx,
+                   int rows, const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st);
+
+void launch_qk_norm_rope_kv(const float* qkv, const Rows& rows, int hq, int hkv, int head_dim, const float* qn_w,
+                            const float* kn_w, float eps, const float2* rope_cs, int rope_len, const KVLayerView& kv,
+                            float* q_out, int* err, cudaStream_t st);
+
+// Causal GQA over the paged cache; visible keys of a row = [0, pos], cut into `splits` key ranges
+// (computed per row on the device).  `scratch` (may be null when splits == 1) holds the split-K
+// partials: rows*hq*splits*(head_dim + 2) floats.
+void launch_attention(const float* q, const Rows& rows, int splits, int hq, int hkv, int head_dim,
+                      const KVLayerView& kv, float* out, float* scratch, size_t scratch_floats, cudaStream_t st);
+int attention_splits(int rows, int hkv, int max_visible);
+
+void launch_argmax(const float* logits, int vocab, int ld, int rows, int* next_ids, cudaStream_t st);
+
+void launch_rmsnorm(const float* x, int rows, int n, const float* w, float eps, float* y, cudaStream_t st);
+
+}  // namespace socb

@@ -1,0 +1,979 @@
+// Host runtime and C ABI of soc_b200: bundle loading into HBM, the paged KV
+// cache, and the prefill / decode / generate drivers.
+//
+// The host side mirrors the reference runtime's objects (SongWooYoung/SoC):
+//   soc_model  <-> QwenModelLoader::LoadModel -> QwenCausalLM   (Mac/cpu/src/qwen_model_loader.cpp:35-93)
+//   soc_kv     <-> TensorKVCache / Metal KVCache                 (Mac/cpu/src/kv_cache.cpp, Mac/gpu/src/runtime/kv_cache.mm)
+//   prefill / decode / generate <-> GenerationContext            (Mac/gpu/src/runtime/generation_context.cpp)
+#include <sys/stat.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/soc_b200.h"
+#include "common.cuh"
+#include "json.hpp"
+#include "kernels.h"
+
+using namespace socb;
+
+namespace {
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        return SOC_B200_OK;
+    } catch (const Error& e) {
+        return fail(e.code, e.what());
+    } catch (const std::exception& e) {
+        return fail(SOC_B200_ERR_INVALID, e.what());
+    }
+}
+
+[[noreturn]] void throw_fmt(const std::string& m) { throw Error(SOC_B200_ERR_FORMAT, m); }
+
+// ------------------------------------------------------------------ manifest
+struct TensorRecord {
+    std::string name, file, dtype;
+    std::vector<size_t> shape;
+    size_t byte_size = 0;
+};
+
+struct Config {
+    size_t hidden = 0, inter = 0, layers = 0, hq = 0, hkv = 0, hd = 0, vocab = 0, max_pos = 40960;
+    double eps = 0, theta = 0;
+    bool tied = true;
+};
+
+std::string read_file(const std::string& path) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) throw Error(SOC_B200_ERR_IO, "failed to open file: " + path);
+    std::stringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+std::string dir_of(const std::string& p) {
+    const auto pos = p.find_last_of('/');
+    return pos == std::string::npos ? std::string(".") : p.substr(0, pos);
+}
+
+size_t dtype_width(const std::string& d) {
+    if (d == "float32" || d == "int32") return 4;
+    if (d == "float16" || d == "bfloat16" || d == "uint16") return 2;
+    if (d == "int64") return 8;
+    if (d == "int8" || d == "uint8" || d == "bool") return 1;
+    throw_fmt("unsupported dtype string: " + d);
+}
+
+struct Manifest {
+    std::string dir;
+    Json config;
+    std::vector<TensorRecord> tensors;
+    const TensorRecord& find(const std::string& n) const {
+        for (auto& t : tensors)
+            if (t.name == n) return t;
+        throw_fmt("missing tensor in manifest: " + n);
+    }
+};
+
+// ManifestLoader::LoadFromFile + StartupValidator::ValidateManifest
+// (Mac/cpu/src/runtime_assets.cpp:138-168, startup_validator.cpp:5-23).
+Manifest load_manifest(const std::string& path) {
+    Json root;
+    try {
+        root = JsonReader(read_file(path)).parse();
+    } catch (const Error&) {
+        throw;
+    } catch (const std::exception& e) {
+        throw_fmt(e.what());
+    }
+    Manifest m;
+    m.dir = dir_of(path);
+    try {
+        if (root.at("format").as_string() != "soc.cpp.llm_export") throw_fmt("manifest format must be soc.cpp.llm_export");
+        if (root.at("format_version").as_int64() < 2) throw_fmt("manifest format_version must be at least 2");
+        root.at("export_dtype").as_string();
+        if (!root.contains("config") || !root.at("config").is_object()) throw_fmt("manifest config must be a JSON object");
+        m.config = root.at("config");
+        for (const Json& t : root.at("tensors").as_array()) {
+            TensorRecord r;
+            r.name = t.at("name").as_string();
+            r.file = m.dir + "/" + t.at("file").as_string();
+            r.dtype = t.at("dtype").as_string();
+            for (const Json& s : t.at("shape").as_array()) r.shape.push_back(static_cast<size_t>(s.as_int64()));
+            r.byte_size = static_cast<size_t>(t.at("byte_size").as_int64());
+            t.at("source_shard").as_string();
+            m.tensors.push_back(std::move(r));
+        }
+        if (m.tensors.empty()) throw_fmt("manifest must contain at least one tensor");
+        if (!root.contains("tokenizer_runtime_file") || root.at("tokenizer_runtime_file").as_string().empty())
+            throw_fmt("manifest must reference tokenizer_runtime_file");
+    } catch (const Error&) {
+        throw;
+    } catch (const std::exception& e) {
+        throw_fmt(e.what());
+    }
+    return m;
+}
+
+// Qwen3Config::FromJson + Validate (Mac/cpu/src/qwen3_config.cpp:20-66).
+Config read_config(const Json& c) {
+    Config k;
+    try {
+        if (c.at("model_type").as_string() != "qwen3") throw_fmt("config model_type must be qwen3");
+        k.hidden = static_cast<size_t>(c.at("hidden_size").as_int64());
+        k.inter = static_cast<size_t>(c.at("intermediate_size").as_int64());
+        k.layers = static_cast<size_t>(c.at("num_hidden_layers").as_int64());
+        k.hq = static_cast<size_t>(c.at("num_attention_heads").as_int64());
+        k.hkv = static_cast<size_t>(c.at("num_key_value_heads").as_int64());
+        k.hd = static_cast<size_t>(c.at("head_dim").as_int64());
+        k.eps = c.at("rms_norm_eps").as_number();
+        k.theta = c.at("rope_theta").as_number();
+        k.tied = c.at("tie_word_embeddings").as_bool();
+        if (c.at("torch_dtype").as_string().empty()) throw_fmt("torch_dtype must not be empty");
+        k.vocab = static_cast<size_t>(c.at("vocab_size").as_int64());
+        if (c.contains("max_position_embeddings")) k.max_pos = static_cast<size_t>(c.at("max_position_embeddings").as_int64());
+    } catch (const Error&) {
+        throw;
+    } catch (const std::exception& e) {
+        throw_fmt(e.what());
+    }
+    if (k.hidden == 0 || k.inter == 0 || k.layers == 0) throw_fmt("qwen3 config dimensions must be non-zero");
+    if (k.hq == 0 || k.hkv == 0 || k.hd == 0) throw_fmt("qwen3 attention dimensions must be non-zero");
+    if (k.hidden % k.hq != 0) throw_fmt("hidden_size must be divisible by num_attention_heads");
+    if (k.hq % k.hkv != 0) throw_fmt("num_attention_heads must be divisible by num_key_value_heads");
+    if (k.eps <= 0.0 || k.theta <= 0.0) throw_fmt("qwen3 normalization and rope parameters must be positive");
+    if (k.vocab == 0) throw_fmt("vocab_size must be non-zero");
+    // Limits of this implementation's kernels.
+    if (k.hd != 64 && k.hd != 128) throw_fmt("soc_b200 supports head_dim 64 or 128");
+    if (k.hq / k.hkv > 8) throw_fmt("soc_b200 supports at most 8 query heads per kv head");
+    if (k.hidden % 256 != 0 || k.inter % 256 != 0 || (k.hq * k.hd) % 256 != 0)
+        throw_fmt("soc_b200 needs hidden, intermediate and q width to be multiples of 256");
+    if (k.max_pos == 0 || k.max_pos > (1u << 20)) k.max_pos = 40960;
+    return k;
+}
+
+// WeightLoader::LoadTensor checks (Mac/cpu/src/weight_loader.cpp:17-30), then reads the bytes.
+std::vector<char> load_record(const TensorRecord& r, const std::vector<size_t>& expect_shape) {
+    if (r.shape != expect_shape) throw_fmt("model loader encountered unexpected shape for: " + r.name);
+    size_t numel = 1;
+    for (size_t s : r.shape) numel *= s;
+    const size_t expect = numel * dtype_width(r.dtype);
+    if (expect != r.byte_size) throw_fmt("tensor record byte_size does not match dtype and shape for: " + r.name);
+    struct stat st {};
+    if (stat(r.file.c_str(), &st) != 0) throw Error(SOC_B200_ERR_IO, "failed to open tensor file: " + r.file);
+    if (static_cast<size_t>(st.st_size) < r.byte_size)
+        throw Error(SOC_B200_ERR_IO, "tensor file is smaller than expected byte_size for: " + r.name);
+    std::vector<char> buf(r.byte_size);
+    FILE* f = std::fopen(r.file.c_str(), "rb");
+    if (!f) throw Error(SOC_B200_ERR_IO, "failed to open tensor file: " + r.file);
+    const size_t got = std::fread(buf.data(), 1, r.byte_size, f);
+    std::fclose(f);
+    if (got != r.byte_size) throw Error(SOC_B200_ERR_IO, "short read for tensor: " + r.name);
+    return buf;
+}
+
+float half_bits_to_float(uint16_t h) {
+    const uint32_t sign = static_cast<uint32_t>(h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1f, m = h & 0x3ff, bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else {
+            int ee = -14;
+            while (!(m & 0x400)) {
+                m <<= 1;
+                --ee;
+            }
+            bits = sign | (static_cast<uint32_t>(ee + 127) << 23) | ((m & 0x3ff) << 13);
+        }
+    } else if (e == 0x1f) {
+        bits = sign | 0x7f800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 112) << 23) | (m << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+// Norm weights are kept in fp32 on the device (exact for fp16 / bf16 sources).
+std::vector<float> to_f32(const TensorRecord& r, const std::vector<char>& b) {
+    size_t n = b.size() / dtype_width(r.dtype);
+    std::vector<float> out(n);
+    if (r.dtype == "float32") {
+        std::memcpy(out.data(), b.data(), n * 4);
+    } else if (r.dtype == "float16") {
+        const uint16_t* p = reinterpret_cast<const uint16_t*>(b.data());
+        for (size_t i = 0; i < n; ++i) out[i] = half_bits_to_float(p[i]);
+    } else if (r.dtype == "bfloat16") {
+        const uint16_t* p = reinterpret_cast<const uint16_t*>(b.data());
+        for (size_t i = 0; i < n; ++i) {
+            uint32_t bits = static_cast<uint32_t>(p[i]) << 16;
+            std::memcpy(&out[i], &bits, 4);
+        }
+    } else {
+        throw_fmt("model loader requires floating-point weights for: " + r.name);
+    }
+    return out;
+}
+
+uint16_t float_to_half_bits(float f) {
+    const __half h = __float2half_rn(f);
+    uint16_t u;
+    std::memcpy(&u, &h, 2);
+    return u;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------- objects
+struct soc_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int sm_count = 0;
+    int* d_err = nullptr;
+};
+
+struct LayerW {
+    void* wqkv = nullptr;  // [(hq + 2 hkv) * hd, hidden]  q rows, then k, then v
+    void* wo = nullptr;    // [hidden, hq * hd]
+    void* wgu = nullptr;   // [2 * inter, hidden] rows (2j, 2j+1) = (gate_j, up_j)
+    void* wd = nullptr;    // [hidden, inter]
+    float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+};
+
+struct soc_model {
+    soc_ctx* ctx = nullptr;
+    Config cfg;
+    int wfmt = WF_F16;  // block linears
+    int efmt = WF_F16;  // embedding / lm_head
+    void* embed = nullptr;
+    void* lm_head = nullptr;  // == embed when tied
+    float* final_norm = nullptr;
+    std::vector<LayerW> layers;
+    float2* rope_cs = nullptr;
+    int rope_len = 0;
+    std::vector<void*> allocs;
+    // workspace (grown on demand)
+    int ws_rows = 0;
+    float *h = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
+    int *d_tokens = nullptr, *d_seq = nullptr, *d_pos = nullptr, *d_next = nullptr;
+    float* logits = nullptr;
+    int logits_rows = 0;
+    float* attn_scratch = nullptr;
+    size_t attn_scratch_floats = 0;
+    // device-fed decode loop (CUDA graph of one step, replayed per token)
+    struct LoopState {
+        int* out;
+        int seq, start, step;
+    };
+    LoopState* d_loop = nullptr;
+    cudaGraphExec_t step_graph = nullptr;
+    const soc_kv* graph_kv = nullptr;
+    int graph_splits = 0;
+    long long graph_kernels = 0;
+
+    void* dmalloc(size_t bytes) {
+        void* p = nullptr;
+        SOCB_CUDA(cudaMalloc(&p, bytes));
+        allocs.push_back(p);
+        return p;
+    }
+    void dfree(void* p) {
+        if (!p) return;
+        cudaFree(p);
+        for (auto& a : allocs)
+            if (a == p) a = nullptr;
+    }
+    size_t qkv_dim() const { return (cfg.hq + 2 * cfg.hkv) * cfg.hd; }
+};
+
+struct soc_kv {
+    soc_model* m = nullptr;
+    int max_seqs = 0, page_tokens = 16, num_pages = 0, max_pages = 0;
+    __half* k = nullptr;  // [layers][num_pages][hkv][page_tokens][hd]
+    __half* v = nullptr;
+    int* d_page_table = nullptr;  // [max_seqs][max_pages]
+    std::vector<int> lengths;
+    std::vector<std::vector<int>> pages;
+    std::vector<int> free_pages;
+    size_t layer_stride() const { return static_cast<size_t>(num_pages) * m->cfg.hkv * page_tokens * m->cfg.hd; }
+    KVLayerView view(int layer) const {
+        return KVLayerView{k + layer * layer_stride(), v + layer * layer_stride(), d_page_table, max_pages,
+                           page_tokens};
+    }
+    void check_seq(int seq) const {
+        if (seq < 0 || seq >= max_seqs) throw Error(SOC_B200_ERR_INVALID, "kv cache sequence index out of range");
+    }
+    // Make room for positions [0, new_len) of `seq` (host page allocator + device page table).
+    void reserve(int seq, int new_len, cudaStream_t st) {
+        if (new_len > max_pages * page_tokens)
+            throw Error(SOC_B200_ERR_CAPACITY, "GenerationContext sequence length would exceed max_sequence_length");
+        const int need = (new_len + page_tokens - 1) / page_tokens;
+        auto& pv = pages[seq];
+        const int before = static_cast<int>(pv.size());
+        if (need <= before) return;
+        if (static_cast<int>(free_pages.size()) < need - before)
+            throw Error(SOC_B200_ERR_CAPACITY, "kv cache out of pages");
+        while (static_cast<int>(pv.size()) < need) {
+            pv.push_back(free_pages.back());
+            free_pages.pop_back();
+        }
+        SOCB_CUDA(cudaMemcpyAsync(d_page_table + static_cast<size_t>(seq) * max_pages + before, pv.data() + before,
+                                  sizeof(int) * (need - before), cudaMemcpyHostToDevice, st));
+    }
+    void reset(int seq) {
+        for (int p : pages[seq]) free_pages.push_back(p);
+        pages[seq].clear();
+        lengths[seq] = 0;
+    }
+};
+
+namespace {
+
+void ensure_workspace(soc_model* m, int rows) {
+    if (rows <= m->ws_rows) return;
+    const Config& c = m->cfg;
+    int r = 16;
+    while (r < rows) r *= 2;
+    for (void* p : {static_cast<void*>(m->h), static_cast<void*>(m->qkv), static_cast<void*>(m->q),
+                    static_cast<void*>(m->att), static_cast<void*>(m->act), static_cast<void*>(m->d_tokens),
+                    static_cast<void*>(m->d_seq), static_cast<void*>(m->d_pos), static_cast<void*>(m->d_next)})
+        m->dfree(p);
+    m->h = static_cast<float*>(m->dmalloc(sizeof(float) * r * c.hidden));
+    m->qkv = static_cast<float*>(m->dmalloc(sizeof(float) * r * m->qkv_dim()));
+    m->q = static_cast<float*>(m->dmalloc(sizeof(float) * r * c.hq * c.hd));
+    m->att = static_cast<float*>(m->dmalloc(sizeof(float) * r * c.hq * c.hd));
+    m->act = static_cast<float*>(m->dmalloc(sizeof(float) * r * c.inter));
+    m->d_tokens = static_cast<int*>(m->dmalloc(sizeof(int) * r));
+    m->d_seq = static_cast<int*>(m->dmalloc(sizeof(int) * r));
+    m->d_pos = static_cast<int*>(m->dmalloc(sizeof(int) * r));
+    m->d_next = static_cast<int*>(m->dmalloc(sizeof(int) * r));
+    m->ws_rows = r;
+}
+
+void ensure_logits(soc_model* m, int rows) {
+    if (rows <= m->logits_rows) return;
+    m->dfree(m->logits);
+    m->logits = static_cast<float*>(m->dmalloc(sizeof(float) * rows * m->cfg.vocab));
+    m->logits_rows = rows;
+}
+
+void ensure_attn_scratch(soc_model* m, size_t floats) {
+    if (floats <= m->attn_scratch_floats) return;
+    m->dfree(m->attn_scratch);
+    m->attn_scratch = static_cast<float*>(m->dmalloc(sizeof(float) * floats));
+    m->attn_scratch_floats = floats;
+}
+
+void check_device_error(soc_model* m) {
+    int e = 0;
+    SOCB_CUDA(cudaMemcpyAsync(&e, m->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, m->ctx->stream));
+    SOCB_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    if (e != 0) {
+        SOCB_CUDA(cudaMemsetAsync(m->ctx->d_err, 0, sizeof(int), m->ctx->stream));
+        if (e & DERR_TOKEN_RANGE) throw Error(SOC_B200_ERR_RANGE, "embedding input token id out of range");
+        if (e & DERR_KV_RANGE) throw Error(SOC_B200_ERR_CAPACITY, "kv cache write position out of range");
+        throw Error(SOC_B200_ERR_DEVICE, "device kernel reported error status " + std::to_string(e));
+    }
+}
+
+// Run rows [0, n) (tokens/seq/pos already in m->d_tokens/d_seq/d_pos) through all layers.
+// Afterwards m->h holds the residual stream; when lm_rows > 0 the logits of rows
+// [lm_first, lm_first + lm_rows) go to m->logits and their greedy ids to m->d_next.
+void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first, int lm_rows, int splits) {
+    const Config& c = m->cfg;
+    cudaStream_t st = m->ctx->stream;
+    const float eps = static_cast<float>(c.eps);
+    const int H = static_cast<int>(c.hidden), I = static_cast<int>(c.inter);
+    const int QW = static_cast<int>(c.hq * c.hd), QKV = static_cast<int>(m->qkv_dim());
+    Rows rows{m->d_tokens, m->d_seq, m->d_pos, n};
+    if (splits < 1) splits = attention_splits(n, static_cast<int>(c.hkv), max_visible);
+    if (splits > 1) ensure_attn_scratch(m, static_cast<size_t>(n) * c.hq * splits * (c.hd + 2));
+    launch_embed(m->efmt, m->embed, H, static_cast<int>(c.vocab), m->d_tokens, n, m->h, m->ctx->d_err, st);
+    for (size_t l = 0; l < c.layers; ++l) {
+        const LayerW& w = m->layers[l];
+        launch_linear(m->wfmt, w.wqkv, nullptr, QKV, H, m->h, H, n, w.in_norm, eps, m->qkv, QKV, LIN_STORE, st);
+        launch_qk_norm_rope_kv(m->qkv, rows, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
+                               w.q_norm, w.k_norm, eps, m->rope_cs, m->rope_len, kv->view(static_cast<int>(l)), m->q,
+                               m->ctx->d_err, st);
+        launch_attention(m->q, rows, splits, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
+                         kv->view(static_cast<int>(l)), m->att, m->attn_scratch, m->attn_scratch_floats, st);
+        launch_linear(m->wfmt, w.wo, nullptr, H, QW, m->att, QW, n, nullptr, eps, m->h, H, LIN_RESIDUAL, st);
+        launch_linear(m->wfmt, w.wgu, nullptr, 2 * I, H, m->h, H, n, w.post_norm, eps, m->act, I, LIN_SWIGLU, st);
+        launch_linear(m->wfmt, w.wd, nullptr, H, I, m->act, I, n, nullptr, eps, m->h, H, LIN_RESIDUAL, st);
+    }
+    if (lm_rows > 0) {
+        ensure_logits(m, lm_rows);
+        launch_linear(m->efmt, m->lm_head, nullptr, static_cast<int>(c.vocab), H, m->h + static_cast<size_t>(lm_first) * H,
+                      H, lm_rows, m->final_norm, eps, m->logits, static_cast<int>(c.vocab), LIN_STORE, st);
+        launch_argmax(m->logits, static_cast<int>(c.vocab), static_cast<int>(c.vocab), lm_rows, m->d_next, st);
+    }
+}
+
+void check_ids(const soc_model* m, const int32_t* ids, int n) {
+    for (int i = 0; i < n; ++i)
+        if (ids[i] < 0 || static_cast<size_t>(ids[i]) >= m->cfg.vocab)
+            throw Error(SOC_B200_ERR_RANGE, "embedding input token id out of range");
+}
+
+constexpr int kPrefillChunk = 4096;
+
+// Prefill `n` host ids at the end of `seq`; leaves the last row's logits/next id on the device.
+void prefill_impl(soc_model* m, soc_kv* kv, int seq, const int32_t* ids, int n, bool ids_on_device) {
+    kv->check_seq(seq);
+    if (n <= 0) throw Error(SOC_B200_ERR_INVALID, "GenerationContext prefill requires at least one token");
+    if (!ids_on_device) check_ids(m, ids, n);
+    cudaStream_t st = m->ctx->stream;
+    const int start = kv->lengths[seq];
+    kv->reserve(seq, start + n, st);
+    for (int off = 0; off < n; off += kPrefillChunk) {
+        const int cn = std::min(kPrefillChunk, n - off);
+        ensure_workspace(m, cn);
+        std::vector<int> sq(cn, seq), ps(cn);
+        for (int i = 0; i < cn; ++i) ps[i] = start + off + i;
+        SOCB_CUDA(cudaMemcpyAsync(m->d_tokens, ids + off, sizeof(int) * cn,
+                                  ids_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+        SOCB_CUDA(cudaMemcpyAsync(m->d_seq, sq.data(), sizeof(int) * cn, cudaMemcpyHostToDevice, st));
+        SOCB_CUDA(cudaMemcpyAsync(m->d_pos, ps.data(), sizeof(int) * cn, cudaMemcpyHostToDevice, st));
+        const bool last = off + cn == n;
+        // (the pageable host vectors are staged by the driver before cudaMemcpyAsync returns)
+        forward_rows(m, kv, cn, start + off + cn, last ? cn - 1 : 0, last ? 1 : 0, 1);
+    }
+    kv->lengths[seq] = start + n;
+}
+
+
+__global__ void k_step_begin(const soc_model::LoopState* st, int* tokens, int* seq, int* pos) {
+    const int i = st->step;
+    tokens[0] = st->out[i];
+    seq[0] = st->seq;
+    pos[0] = st->start + i;
+}
+
+__global__ void k_step_end(soc_model::LoopState* st, const int* next) {
+    st->out[st->step + 1] = next[0];
+    st->step += 1;
+}
+
+// `steps` decode steps of sequence `seq`, whose cache holds `start` tokens and whose
+// next input id is d_out[0]; writes ids 1..steps of d_out.  One step is captured as a
+// CUDA graph (bound to this cache and split count) and replayed per token.
+void decode_loop(soc_model* m, soc_kv* kv, int seq, int start, int steps, int32_t* d_out) {
+    cudaStream_t st = m->ctx->stream;
+    const int splits = attention_splits(1, static_cast<int>(m->cfg.hkv), start + steps);
+    ensure_workspace(m, 1);
+    ensure_logits(m, 1);
+    if (splits > 1) ensure_attn_scratch(m, static_cast<size_t>(m->cfg.hq) * splits * (m->cfg.hd + 2));
+    if (!m->d_loop) m->d_loop = static_cast<soc_model::LoopState*>(m->dmalloc(sizeof(soc_model::LoopState)));
+    if (!m->step_graph || m->graph_kv != kv || m->graph_splits != splits) {
+        if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
+        m->step_graph = nullptr;
+        cudaGraph_t g = nullptr;
+        const long long before = launches_so_far();
+        SOCB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        try {
+            k_step_begin<<<1, 1, 0, st>>>(m->d_loop, m->d_tokens, m->d_seq, m->d_pos);
+            forward_rows(m, kv, 1, start + steps, 0, 1, splits);
+            k_step_end<<<1, 1, 0, st>>>(m->d_loop, m->d_next);
+            // captured launches did not run: move them from the counter to the graph's size
+            m->graph_kernels = launches_so_far() - before + 2;
+            count_launches(-(launches_so_far() - before));
+        } catch (...) {
+            cudaStreamEndCapture(st, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        SOCB_CUDA(cudaStreamEndCapture(st, &g));
+        const cudaError_t e = cudaGraphInstantiate(&m->step_graph, g, 0);
+        cudaGraphDestroy(g);
+        SOCB_CUDA(e);
+        m->graph_kv = kv;
+        m->graph_splits = splits;
+    }
+    const soc_model::LoopState init{d_out, seq, start, 0};
+    SOCB_CUDA(cudaMemcpyAsync(m->d_loop, &init, sizeof(init), cudaMemcpyHostToDevice, st));
+    for (int i = 0; i < steps; ++i) SOCB_CUDA(cudaGraphLaunch(m->step_graph, st));
+    count_launches(m->graph_kernels * steps);
+}
+
+}  // namespace
+
+// ============================================================== C ABI
+extern "C" {
+
+const char* soc_b200_last_error(void) { return g_last_error.c_str(); }
+
+long long soc_b200_kernel_launches(void) { return launches_so_far(); }
+
+int soc_b200_open(int device, soc_ctx** out) {
+    if (!out) return fail(SOC_B200_ERR_INVALID, "soc_b200_open: null output");
+    return guarded([&] {
+        int n = 0;
+        SOCB_CUDA(cudaGetDeviceCount(&n));
+        if (device < 0 || device >= n) throw Error(SOC_B200_ERR_INVALID, "soc_b200_open: device index out of range");
+        SOCB_CUDA(cudaSetDevice(device));
+        auto c = std::make_unique<soc_ctx>();
+        c->device = device;
+        SOCB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+        SOCB_CUDA(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device));
+        SOCB_CUDA(cudaMalloc(&c->d_err, sizeof(int)));
+        SOCB_CUDA(cudaMemset(c->d_err, 0, sizeof(int)));
+        *out = c.release();
+    });
+}
+
+void soc_b200_close(soc_ctx* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->d_err);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+int soc_b200_synchronize(soc_ctx* ctx) {
+    if (!ctx) return fail(SOC_B200_ERR_INVALID, "null context");
+    return guarded([&] { SOCB_CUDA(cudaStreamSynchronize(ctx->stream)); });
+}
+
+void* soc_b200_stream(soc_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_format, int tp_rank, int tp_size,
+                         void* nccl_comm, soc_model** out) {
+    if (!ctx || !manifest_path || !out) return fail(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: null argument");
+    if (tp_size != 1 || tp_rank != 0 || nccl_comm != nullptr)
+        return fail(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: tensor parallelism is not enabled in this build");
+    auto m = std::make_unique<soc_model>();
+    const int rc = guarded([&] {
+        SOCB_CUDA(cudaSetDevice(ctx->device));
+        m->ctx = ctx;
+        const Manifest man = load_manifest(manifest_path);
+        m->cfg = read_config(man.config);
+        const Config& c = m->cfg;
+        const size_t H = c.hidden, I = c.inter, D = c.hd, QW = c.hq * D, KW = c.hkv * D;
+
+        // Linear weight format: every block linear must share one float type.
+        const std::string lin_dtype = man.find("model.layers.0.self_attn.q_proj.weight").dtype;
+        int fmt = lin_dtype == "bfloat16" ? WF_BF16 : WF_F16;
+        if (lin_dtype != "float16" && lin_dtype != "bfloat16" && lin_dtype != "float32")
+            throw_fmt("model loader requires floating-point weights for: model.layers.0.self_attn.q_proj.weight");
+        if (weight_format == SOC_B200_WEIGHTS_F16) fmt = WF_F16;
+        else if (weight_format == SOC_B200_WEIGHTS_BF16) fmt = WF_BF16;
+        else if (weight_format != SOC_B200_WEIGHTS_NATIVE)
+            throw Error(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: weight_format not supported by this build");
+        m->wfmt = fmt;
+
+        // Converts a float tensor to the device element type `f` (bit copy when it already matches).
+        auto upload_matrix = [&](const TensorRecord& r, const std::vector<char>& b, void* dst, int f) {
+            const size_t n = b.size() / dtype_width(r.dtype);
+            const bool same = (f == WF_F16 && r.dtype == "float16") || (f == WF_BF16 && r.dtype == "bfloat16");
+            if (same) {
+                SOCB_CUDA(cudaMemcpy(dst, b.data(), b.size(), cudaMemcpyHostToDevice));
+                return;
+            }
+            const std::vector<float> fv = to_f32(r, b);
+            std::vector<uint16_t> conv(n);
+            for (size_t i = 0; i < n; ++i) {
+                if (f == WF_F16) {
+                    conv[i] = float_to_half_bits(fv[i]);
+                } else {
+                    const __nv_bfloat16 bb = __float2bfloat16_rn(fv[i]);
+                    std::memcpy(&conv[i], &bb, 2);
+                }
+            }
+            SOCB_CUDA(cudaMemcpy(dst, conv.data(), n * 2, cudaMemcpyHostToDevice));
+        };
+        auto upload_norm = [&](const std::string& name, size_t n) -> float* {
+            const TensorRecord& r = man.find(name);
+            const std::vector<float> f = to_f32(r, load_record(r, {n}));
+            float* d = static_cast<float*>(m->dmalloc(n * sizeof(float)));
+            SOCB_CUDA(cudaMemcpy(d, f.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+            return d;
+        };
+
+        // Embedding (and tied lm_head).
+        {
+            const TensorRecord& r = man.find("model.embed_tokens.weight");
+            const auto b = load_record(r, {c.vocab, H});
+            m->efmt = r.dtype == "bfloat16" ? WF_BF16 : WF_F16;
+            if (weight_format == SOC_B200_WEIGHTS_BF16) m->efmt = WF_BF16;
+            if (weight_format == SOC_B200_WEIGHTS_F16) m->efmt = WF_F16;
+            m->embed = m->dmalloc(c.vocab * H * 2);
+            upload_matrix(r, b, m->embed, m->efmt);
+        }
+        m->layers.resize(c.layers);
+        for (size_t l = 0; l < c.layers; ++l) {
+            const std::string p = "model.layers." + std::to_string(l) + ".";
+            LayerW& w = m->layers[l];
+            w.in_norm = upload_norm(p + "input_layernorm.weight", H);
+            w.post_norm = upload_norm(p + "post_attention_layernorm.weight", H);
+            w.q_norm = upload_norm(p + "self_attn.q_norm.weight", D);
+            w.k_norm = upload_norm(p + "self_attn.k_norm.weight", D);
+            char* qkv = static_cast<char*>(m->dmalloc((QW + 2 * KW) * H * 2));
+            w.wqkv = qkv;
+            const TensorRecord& rq = man.find(p + "self_attn.q_proj.weight");
+            upload_matrix(rq, load_record(rq, {QW, H}), qkv, fmt);
+            const TensorRecord& rk = man.find(p + "self_attn.k_proj.weight");
+            upload_matrix(rk, load_record(rk, {KW, H}), qkv + QW * H * 2, fmt);
+            const TensorRecord& rv = man.find(p + "self_attn.v_proj.weight");
+            upload_matrix(rv, load_record(rv, {KW, H}), qkv + (QW + KW) * H * 2, fmt);
+            const TensorRecord& ro = man.find(p + "self_attn.o_proj.weight");
+            w.wo = m->dmalloc(H * QW * 2);
+            upload_matrix(ro, load_record(ro, {H, QW}), w.wo, fmt);
+            // gate / up interleaved by row: staged as two dense blocks, then shuffled on the host.
+            const TensorRecord& rg = man.find(p + "mlp.gate_proj.weight");
+            const TensorRecord& ru = man.find(p + "mlp.up_proj.weight");
+            void* tmp_g = m->dmalloc(I * H * 2);
+            void* tmp_u = m->dmalloc(I * H * 2);
+            upload_matrix(rg, load_record(rg, {I, H}), tmp_g, fmt);
+            upload_matrix(ru, load_record(ru, {I, H}), tmp_u, fmt);
+            w.wgu = m->dmalloc(2 * I * H * 2);
+            SOCB_CUDA(cudaMemcpy2D(w.wgu, 2 * H * 2, tmp_g, H * 2, H * 2, I, cudaMemcpyDeviceToDevice));
+            SOCB_CUDA(cudaMemcpy2D(static_cast<char*>(w.wgu) + H * 2, 2 * H * 2, tmp_u, H * 2, H * 2, I,
+                                   cudaMemcpyDeviceToDevice));
+            m->dfree(tmp_g);
+            m->dfree(tmp_u);
+            const TensorRecord& rd = man.find(p + "mlp.down_proj.weight");
+            w.wd = m->dmalloc(H * I * 2);
+            upload_matrix(rd, load_record(rd, {H, I}), w.wd, fmt);
+        }
+        m->final_norm = upload_norm("model.norm.weight", H);
+        if (c.tied) {
+            m->lm_head = m->embed;
+        } else {
+            const TensorRecord& r = man.find("lm_head.weight");
+            m->lm_head = m->dmalloc(c.vocab * H * 2);
+            upload_matrix(r, load_record(r, {c.vocab, H}), m->lm_head, m->efmt);
+        }
+        // RoPE table (cos, sin) [max_pos][D/2], computed as RoPE::ApplyInPlace does (rope.cpp:74-79).
+        m->rope_len = static_cast<int>(c.max_pos);
+        std::vector<float2> cs(static_cast<size_t>(m->rope_len) * (D / 2));
+        for (int pos = 0; pos < m->rope_len; ++pos) {
+            const double ap = static_cast<double>(pos);
+            for (size_t i = 0; i < D / 2; ++i) {
+                const double ex = static_cast<double>(i * 2) / static_cast<double>(D);
+                const double ang = ap / std::pow(c.theta, ex);
+                cs[static_cast<size_t>(pos) * (D / 2) + i] =
+                    make_float2(static_cast<float>(std::cos(ang)), static_cast<float>(std::sin(ang)));
+            }
+        }
+        m->rope_cs = static_cast<float2*>(m->dmalloc(cs.size() * sizeof(float2)));
+        SOCB_CUDA(cudaMemcpy(m->rope_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        ensure_workspace(m.get(), 16);
+        SOCB_CUDA(cudaDeviceSynchronize());
+    });
+    if (rc != SOC_B200_OK) {
+        for (void* p : m->allocs)
+            if (p) cudaFree(p);
+        return rc;
+    }
+    *out = m.release();
+    return SOC_B200_OK;
+}
+
+int soc_b200_model_info(const soc_model* m, soc_model_info* out) {
+    if (!m || !out) return fail(SOC_B200_ERR_INVALID, "null argument");
+    const Config& c = m->cfg;
+    out->layers = static_cast<int>(c.layers);
+    out->hidden = static_cast<int>(c.hidden);
+    out->intermediate = static_cast<int>(c.inter);
+    out->q_heads = static_cast<int>(c.hq);
+    out->kv_heads = static_cast<int>(c.hkv);
+    out->head_dim = static_cast<int>(c.hd);
+    out->vocab = static_cast<int>(c.vocab);
+    out->tied_embeddings = c.tied ? 1 : 0;
+    out->weight_format = m->wfmt;
+    out->max_position = m->rope_len;
+    out->rms_norm_eps = static_cast<float>(c.eps);
+    out->rope_theta = c.theta;
+    return SOC_B200_OK;
+}
+
+void soc_b200_free_model(soc_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
+    for (void* p : m->allocs)
+        if (p) cudaFree(p);
+    delete m;
+}
+
+int soc_b200_kv_create(soc_model* m, int max_seqs, int max_tokens, int page_tokens, soc_kv** out) {
+    if (!m || !out) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (max_seqs <= 0 || max_tokens <= 0) return fail(SOC_B200_ERR_INVALID, "kv cache requires positive capacity");
+    if (page_tokens != 16) return fail(SOC_B200_ERR_INVALID, "kv cache page_tokens must be 16");
+    auto kv = std::make_unique<soc_kv>();
+    const int rc = guarded([&] {
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        kv->m = m;
+        kv->max_seqs = max_seqs;
+        kv->page_tokens = page_tokens;
+        kv->num_pages = (max_tokens + page_tokens - 1) / page_tokens;
+        kv->max_pages = std::min(kv->num_pages, (m->rope_len + page_tokens - 1) / page_tokens);
+        const size_t elems = static_cast<size_t>(m->cfg.layers) * kv->layer_stride();
+        SOCB_CUDA(cudaMalloc(&kv->k, elems * sizeof(__half)));
+        SOCB_CUDA(cudaMalloc(&kv->v, elems * sizeof(__half)));
+        SOCB_CUDA(cudaMalloc(&kv->d_page_table, sizeof(int) * static_cast<size_t>(max_seqs) * kv->max_pages));
+        SOCB_CUDA(cudaMemset(kv->d_page_table, 0, sizeof(int) * static_cast<size_t>(max_seqs) * kv->max_pages));
+        kv->lengths.assign(max_seqs, 0);
+        kv->pages.assign(max_seqs, {});
+        kv->free_pages.resize(kv->num_pages);
+        for (int i = 0; i < kv->num_pages; ++i) kv->free_pages[i] = kv->num_pages - 1 - i;
+    });
+    if (rc != SOC_B200_OK) {
+        cudaFree(kv->k);
+        cudaFree(kv->v);
+        cudaFree(kv->d_page_table);
+        return rc;
+    }
+    *out = kv.release();
+    return SOC_B200_OK;
+}
+
+void soc_b200_free_kv(soc_kv* kv) {
+    if (!kv) return;
+    cudaSetDevice(kv->m->ctx->device);
+    cudaStreamSynchronize(kv->m->ctx->stream);
+    if (kv->m->graph_kv == kv) {
+        cudaGraphExecDestroy(kv->m->step_graph);
+        kv->m->step_graph = nullptr;
+        kv->m->graph_kv = nullptr;
+    }
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    cudaFree(kv->d_page_table);
+    delete kv;
+}
+
+int soc_b200_kv_reset(soc_kv* kv, int seq) {
+    if (!kv) return fail(SOC_B200_ERR_INVALID, "null argument");
+    return guarded([&] {
+        kv->check_seq(seq);
+        kv->reset(seq);
+    });
+}
+
+int soc_b200_kv_length(const soc_kv* kv, int seq) {
+    if (!kv) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (seq < 0 || seq >= kv->max_seqs) return fail(SOC_B200_ERR_INVALID, "kv cache length batch_index out of range");
+    return kv->lengths[seq];
+}
+
+int soc_b200_kv_read(soc_kv* kv, int seq, int layer, int start, int end, float* k, float* v) {
+    if (!kv || !k || !v) return fail(SOC_B200_ERR_INVALID, "null argument");
+    return guarded([&] {
+        soc_model* m = kv->m;
+        kv->check_seq(seq);
+        if (layer < 0 || static_cast<size_t>(layer) >= m->cfg.layers)
+            throw Error(SOC_B200_ERR_INVALID, "kv cache read layer_index out of range");
+        if (start < 0 || start > end) throw Error(SOC_B200_ERR_INVALID, "kv cache read range must be ordered");
+        if (end > kv->lengths[seq]) throw Error(SOC_B200_ERR_INVALID, "kv cache read range exceeds cached sequence length");
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        const size_t hkv = m->cfg.hkv, D = m->cfg.hd, pt = kv->page_tokens;
+        std::vector<uint16_t> hk(pt * hkv * D), hv(pt * hkv * D);
+        const KVLayerView lv = kv->view(layer);
+        for (int p = start; p < end;) {
+            const int pi = p / static_cast<int>(pt);
+            const int page = kv->pages[seq][pi];
+            const size_t base = static_cast<size_t>(page) * hkv * pt * D;
+            SOCB_CUDA(cudaMemcpy(hk.data(), lv.k + base, hk.size() * 2, cudaMemcpyDeviceToHost));
+            SOCB_CUDA(cudaMemcpy(hv.data(), lv.v + base, hv.size() * 2, cudaMemcpyDeviceToHost));
+            const int pend = std::min(end, (pi + 1) * static_cast<int>(pt));
+            for (; p < pend; ++p) {
+                const size_t slot = static_cast<size_t>(p) % pt;
+                for (size_t h = 0; h < hkv; ++h)
+                    for (size_t d = 0; d < D; ++d) {
+                        const size_t src = (h * pt + slot) * D + d;
+                        const size_t dst = (static_cast<size_t>(p - start) * hkv + h) * D + d;
+                        k[dst] = half_bits_to_float(hk[src]);
+                        v[dst] = half_bits_to_float(hv[src]);
+                    }
+            }
+        }
+    });
+}
+
+int soc_b200_kv_write(soc_kv* kv, int seq, int layer, int start, int end, const float* k, const float* v) {
+    if (!kv || !k || !v) return fail(SOC_B200_ERR_INVALID, "null argument");
+    return guarded([&] {
+        soc_model* m = kv->m;
+        kv->check_seq(seq);
+        if (layer < 0 || static_cast<size_t>(layer) >= m->cfg.layers)
+            throw Error(SOC_B200_ERR_INVALID, "kv cache write layer_index out of range");
+        if (start < 0 || start > end) throw Error(SOC_B200_ERR_INVALID, "kv cache write range must be ordered");
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        cudaStream_t st = m->ctx->stream;
+        kv->reserve(seq, end, st);
+        SOCB_CUDA(cudaStreamSynchronize(st));
+        const size_t hkv = m->cfg.hkv, D = m->cfg.hd, pt = kv->page_tokens;
+        const KVLayerView lv = kv->view(layer);
+        std::vector<uint16_t> hk(hkv * D), hv(hkv * D);
+        for (int p = start; p < end; ++p) {
+            const int page = kv->pages[seq][p / static_cast<int>(pt)];
+            const size_t slot = static_cast<size_t>(p) % pt;
+            for (size_t h = 0; h < hkv; ++h) {
+                for (size_t d = 0; d < D; ++d) {
+                    const size_t src = (static_cast<size_t>(p - start) * hkv + h) * D + d;
+                    hk[h * D + d] = float_to_half_bits(k[src]);
+                    hv[h * D + d] = float_to_half_bits(v[src]);
+                }
+                const size_t dst = ((static_cast<size_t>(page) * hkv + h) * pt + slot) * D;
+                SOCB_CUDA(cudaMemcpy(lv.k + dst, hk.data() + h * D, D * 2, cudaMemcpyHostToDevice));
+                SOCB_CUDA(cudaMemcpy(lv.v + dst, hv.data() + h * D, D * 2, cudaMemcpyHostToDevice));
+            }
+        }
+        if (end > kv->lengths[seq]) kv->lengths[seq] = end;
+    });
+}
+
+int soc_b200_prefill(soc_model* m, soc_kv* kv, int seq, const int32_t* ids, int n, float* logits_last,
+                     int32_t* next_id) {
+    if (!m || !kv || !ids) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (kv->m != m) return fail(SOC_B200_ERR_INVALID, "kv cache belongs to another model");
+    return guarded([&] {
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        prefill_impl(m, kv, seq, ids, n, false);
+        cudaStream_t st = m->ctx->stream;
+        if (logits_last)
+            SOCB_CUDA(cudaMemcpyAsync(logits_last, m->logits, sizeof(float) * m->cfg.vocab, cudaMemcpyDeviceToHost, st));
+        int nid = 0;
+        SOCB_CUDA(cudaMemcpyAsync(&nid, m->d_next, sizeof(int), cudaMemcpyDeviceToHost, st));
+        check_device_error(m);
+        if (next_id) *next_id = nid;
+    });
+}
+
+int soc_b200_decode(soc_model* m, soc_kv* kv, int n_seqs, const int* seq_ids, const int32_t* last_ids,
+                    float* logits, int32_t* next_ids) {
+    if (!m || !kv || !seq_ids || !last_ids) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (kv->m != m) return fail(SOC_B200_ERR_INVALID, "kv cache belongs to another model");
+    return guarded([&] {
+        if (n_seqs <= 0) throw Error(SOC_B200_ERR_INVALID, "decode requires at least one sequence");
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        check_ids(m, last_ids, n_seqs);
+        std::vector<char> seen(kv->max_seqs, 0);
+        std::vector<int> pos(n_seqs);
+        int max_vis = 0;
+        for (int i = 0; i < n_seqs; ++i) {
+            kv->check_seq(seq_ids[i]);
+            if (seen[seq_ids[i]]) throw Error(SOC_B200_ERR_INVALID, "decode sequence ids must be distinct");
+            seen[seq_ids[i]] = 1;
+            if (kv->lengths[seq_ids[i]] == 0)
+                throw Error(SOC_B200_ERR_INVALID, "GenerationContext decode requires a prefilled KV cache");
+            pos[i] = kv->lengths[seq_ids[i]];
+            max_vis = std::max(max_vis, pos[i] + 1);
+        }
+        cudaStream_t st = m->ctx->stream;
+        for (int i = 0; i < n_seqs; ++i) kv->reserve(seq_ids[i], pos[i] + 1, st);
+        ensure_workspace(m, n_seqs);
+        SOCB_CUDA(cudaMemcpyAsync(m->d_tokens, last_ids, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, st));
+        SOCB_CUDA(cudaMemcpyAsync(m->d_seq, seq_ids, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, st));
+        SOCB_CUDA(cudaMemcpyAsync(m->d_pos, pos.data(), sizeof(int) * n_seqs, cudaMemcpyHostToDevice, st));
+        forward_rows(m, kv, n_seqs, max_vis, 0, n_seqs, 0);
+        if (logits)
+            SOCB_CUDA(cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->cfg.vocab * n_seqs, cudaMemcpyDeviceToHost,
+                                      st));
+        if (next_ids) SOCB_CUDA(cudaMemcpyAsync(next_ids, m->d_next, sizeof(int) * n_seqs, cudaMemcpyDeviceToHost, st));
+        check_device_error(m);
+        for (int i = 0; i < n_seqs; ++i) kv->lengths[seq_ids[i]] = pos[i] + 1;
+    });
+}
+
+// Device-side generation: prefill, then max_new - 1 decode steps that feed each greedy id
+// back on the device (no host round trip per token).
+static void generate_dev(soc_model* m, soc_kv* kv, int seq, const int32_t* prompt, int n_prompt, int max_new,
+                         int32_t* d_out, bool prompt_on_device) {
+    kv->check_seq(seq);
+    if (max_new <= 0) throw Error(SOC_B200_ERR_INVALID, "generate requires max_new >= 1");
+    kv->reset(seq);
+    cudaStream_t st = m->ctx->stream;
+    kv->reserve(seq, n_prompt + max_new - 1, st);
+    prefill_impl(m, kv, seq, prompt, n_prompt, prompt_on_device);
+    SOCB_CUDA(cudaMemcpyAsync(d_out, m->d_next, sizeof(int), cudaMemcpyDeviceToDevice, st));
+    if (max_new > 1) decode_loop(m, kv, seq, n_prompt, max_new - 1, d_out);
+    kv->lengths[seq] = n_prompt + max_new - 1;
+}
+
+int soc_b200_generate(soc_model* m, soc_kv* kv, int seq, const int32_t* prompt, int n_prompt, int max_new,
+                      int eos_token_id, int32_t* out_ids, int* n_out) {
+    if (!m || !kv || !prompt || !out_ids) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (kv->m != m) return fail(SOC_B200_ERR_INVALID, "kv cache belongs to another model");
+    return guarded([&] {
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        if (n_out) *n_out = 0;
+        if (max_new == 0) {
+            kv->check_seq(seq);
+            kv->reset(seq);
+            prefill_impl(m, kv, seq, prompt, n_prompt, false);
+            check_device_error(m);
+            return;
+        }
+        int32_t* d_out = static_cast<int32_t*>(m->dmalloc(sizeof(int32_t) * max_new));
+        try {
+            generate_dev(m, kv, seq, prompt, n_prompt, max_new, d_out, false);
+            SOCB_CUDA(cudaMemcpyAsync(out_ids, d_out, sizeof(int32_t) * max_new, cudaMemcpyDeviceToHost,
+                                      m->ctx->stream));
+            check_device_error(m);
+        } catch (...) {
+            m->dfree(d_out);
+            throw;
+        }
+        m->dfree(d_out);
+        int n = max_new;
+        if (eos_token_id >= 0)
+            for (int i = 0; i < max_new; ++i)
+                if (out_ids[i] == eos_token_id) {
+                    n = i + 1;
+                    break;
+                }
+        // Tokens generated after an EOS were computed on the device; drop them from the cache.
+        kv->lengths[seq] = n_prompt + n - 1;
+        if (n_out) *n_out = n;
+    });
+}
+
+int soc_b200_generate_device(soc_model* m, soc_kv* kv, int seq, const int32_t* d_prompt, int n_prompt, int max_new,
+                             int32_t* d_out) {
+    if (!m || !kv || !d_prompt || !d_out) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (kv->m != m) return fail(SOC_B200_ERR_INVALID, "kv cache belongs to another model");
+    return guarded([&] {
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        generate_dev(m, kv, seq, d_prompt, n_prompt, max_new, d_out, true);
+    });
+}
+
+int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* scales, int out_features,
+                    int in_features, const float* x, int rows, float* y, void* stream) {
+    if (!ctx || !w || !x || !y) return fail(SOC_B200_ERR_INVALID, "null argument");
+    return guarded([&] {
+        if (out_features <= 0 || in_features <= 0 || rows <= 0)
+            throw Error(SOC_B200_ERR_INVALID, "linear: dimensions must be positive");
+        int f = weight_format == SOC_B200_WEIGHTS_BF16 ? WF_BF16
+                : weight_format == SOC_B200_WEIGHTS_F16 ? WF_F16
+                                                        : -1;
+        if (f < 0) throw Error(SOC_B200_ERR_INVALID, "linear: weight format not supported by this build");
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+        launch_linear(f, w, scales, out_features, in_features, x, in_features, rows, nullptr, 0.0f, y, out_features,
+                      LIN_STORE, st);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,289 @@
+"""Parity of the B200 path (through the C ABI) with the CPU oracle / reference goldens.
+
+Tolerances: logits within 2e-2 max-abs (fp32 accumulation, fp16 KV cache);
+greedy ids identical; KV-cache indexing bit-exact (kv_write -> kv_read).
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from soc_b200 import runtime as R
+from soc_b200.bundle import QWEN3_0_6B, tiny_config
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 2e-2
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+CASES = {
+    "tied_f16_gqa2_d64": (tiny_config(), "float16"),
+    "untied_f16": (tiny_config(tie_word_embeddings=False), "float16"),
+    "bf16_gqa4_d128": (tiny_config(num_attention_heads=8, num_key_value_heads=2, head_dim=128), "bfloat16"),
+    "mha_d128": (tiny_config(num_attention_heads=2, num_key_value_heads=2, head_dim=128), "float16"),
+    "qwen06_shape_2layer": (dict(QWEN3_0_6B, num_hidden_layers=2), "float16"),
+}
+
+
+@pytest.fixture(scope="module")
+def models(gpu_ctx, make_bundle):
+    cache = {}
+
+    def get(case):
+        if case not in cache:
+            cfg, dt = CASES[case]
+            p = make_bundle(case, cfg, seed=7, dtype=dt)
+            cache[case] = (p, R.Model(gpu_ctx, p))
+        return cache[case]
+
+    yield get
+    for _, m in cache.values():
+        m.free()
+
+
+def _prompt(cfg, n, seed):
+    return np.random.default_rng(seed).integers(0, cfg["vocab_size"], n).astype(np.int32)
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_prefill_and_decode_logits_match_oracle(models, case):
+    p, m = models(case)
+    cfg = CASES[case][0]
+    kv = R.KVCache(m, 1, 256)
+    om = O.OracleModel(p, 256)
+    prompt = _prompt(cfg, 13, 1)
+    lg, nid = m.forward_logits_cached(kv, 0, prompt)
+    ref = om.forward(prompt, 0, last_only=True)[0]
+    assert np.abs(lg - ref).max() <= LOGIT_TOL
+    assert nid == O.argmax(ref)
+    tok, pos = nid, len(prompt)
+    for _ in range(6):
+        lg, nxt = m.decode(kv, [0], [tok])
+        ref = om.forward([tok], pos, last_only=True)[0]
+        assert np.abs(lg[0] - ref).max() <= LOGIT_TOL
+        assert int(nxt[0]) == O.argmax(ref)
+        tok, pos = int(nxt[0]), pos + 1
+    assert kv.length(0) == pos
+    kv.free()
+
+
+@pytest.mark.parametrize("case", ["tied_f16_gqa2_d64", "bf16_gqa4_d128", "qwen06_shape_2layer"])
+def test_generate_matches_oracle_greedy(models, case):
+    p, m = models(case)
+    cfg = CASES[case][0]
+    kv = R.KVCache(m, 2, 512)
+    prompt = _prompt(cfg, 9, 2)
+    toks, _ = O.OracleModel(p, 256).generate(prompt, 12)
+    assert m.generate(kv, 1, prompt, 12) == toks
+    assert kv.length(1) == len(prompt) + 11
+    # a second run on the same cache re-uses the captured decode graph
+    assert m.generate(kv, 1, prompt, 12) == toks
+    kv.free()
+
+
+def test_generate_eos_stops_and_truncates_cache(models):
+    p, m = models("tied_f16_gqa2_d64")
+    prompt = _prompt(CASES["tied_f16_gqa2_d64"][0], 5, 3)
+    toks, _ = O.OracleModel(p, 64).generate(prompt, 8)
+    kv = R.KVCache(m, 1, 64)
+    eos = toks[3]
+    out = m.generate(kv, 0, prompt, 8, eos=eos)
+    first = toks.index(eos)
+    assert out == toks[: first + 1]
+    assert kv.length(0) == len(prompt) + first
+    kv.free()
+
+
+def test_batched_ragged_decode(models):
+    p, m = models("bf16_gqa4_d128")
+    cfg = CASES["bf16_gqa4_d128"][0]
+    kv = R.KVCache(m, 4, 1024)
+    lens = [3, 17, 40]
+    oms, toks, pos = [], [], []
+    for s, n in enumerate(lens):
+        pr = _prompt(cfg, n, 10 + s)
+        om = O.OracleModel(p, 128)
+        ref = om.forward(pr, 0, last_only=True)[0]
+        _, nid = m.forward_logits_cached(kv, s, pr)
+        assert nid == O.argmax(ref)
+        oms.append(om)
+        toks.append(nid)
+        pos.append(n)
+    for _ in range(4):
+        lg, nxt = m.decode(kv, [0, 1, 2], toks)
+        for s in range(3):
+            ref = oms[s].forward([toks[s]], pos[s], last_only=True)[0]
+            assert np.abs(lg[s] - ref).max() <= LOGIT_TOL
+            assert int(nxt[s]) == O.argmax(ref)
+        toks = [int(t) for t in nxt]
+        pos = [q + 1 for q in pos]
+    kv.free()
+
+
+def test_long_prompt_and_chunk_consistency(models):
+    """600-token prompt: one prefill == two half prefills == prefill(599) + decode(1) == oracle."""
+    p, m = models("tied_f16_gqa2_d64")
+    cfg = CASES["tied_f16_gqa2_d64"][0]
+    pr = _prompt(cfg, 600, 4)
+    kv = R.KVCache(m, 3, 4096)
+    a, _ = m.forward_logits_cached(kv, 0, pr)
+    m.forward_logits_cached(kv, 1, pr[:300])
+    b, _ = m.forward_logits_cached(kv, 1, pr[300:])
+    m.forward_logits_cached(kv, 2, pr[:599])
+    c, _ = m.decode(kv, [2], [pr[599]])
+    ref = O.OracleModel(p, 700).forward(pr, 0, last_only=True)[0]
+    for x in (a, b, c[0]):
+        assert np.abs(x - ref).max() <= LOGIT_TOL
+    kv.free()
+
+
+def test_kv_cache_matches_oracle(models):
+    p, m = models("tied_f16_gqa2_d64")
+    cfg = CASES["tied_f16_gqa2_d64"][0]
+    pr = _prompt(cfg, 21, 5)
+    kv = R.KVCache(m, 1, 64)
+    m.forward_logits_cached(kv, 0, pr)
+    om = O.OracleModel(p, 64)
+    om.forward(pr, 0, last_only=True)
+    for layer in range(cfg["num_hidden_layers"]):
+        k, v = kv.read(0, layer, 0, 21)
+        ko, vo = om.kv_read(layer, 0, 21)
+        # fp16 storage: within half an fp16 ulp of the fp32 value, plus kernel rounding
+        assert np.all(np.abs(k - ko) <= np.abs(ko) * 2.0 ** -10 + 2e-4)
+        assert np.all(np.abs(v - vo) <= np.abs(vo) * 2.0 ** -10 + 2e-4)
+    kv.free()
+
+
+def test_kv_write_read_bit_exact_across_pages(models):
+    _, m = models("bf16_gqa4_d128")
+    hkv, hd = m.info.kv_heads, m.info.head_dim
+    kv = R.KVCache(m, 3, 512)
+    rng = np.random.default_rng(0)
+    for seq, n in [(0, 5), (2, 37), (1, 16)]:
+        k = rng.standard_normal((n, hkv, hd)).astype(np.float16).astype(np.float32)
+        v = rng.standard_normal((n, hkv, hd)).astype(np.float16).astype(np.float32)
+        kv.write(seq, 1, 0, k, v)
+        k2, v2 = kv.read(seq, 1, 0, n)
+        assert np.array_equal(k, k2) and np.array_equal(v, v2)
+        assert kv.length(seq) == n
+        # a window that straddles a 16-token page boundary
+        if n > 20:
+            k3, _ = kv.read(seq, 1, 14, 19)
+            assert np.array_equal(k3, k[14:19])
+    kv.free()
+
+
+def test_error_paths(models, gpu_ctx, tmp_path):
+    p, m = models("tied_f16_gqa2_d64")
+    kv = R.KVCache(m, 1, 32)
+    with pytest.raises(R.SocError, match="token id out of range") as e:
+        m.forward_logits_cached(kv, 0, [1, 1000])
+    assert e.value.code == R.ERR_RANGE
+    with pytest.raises(R.SocError, match="prefilled KV cache"):
+        m.decode(kv, [0], [1])
+    with pytest.raises(R.SocError) as e:
+        m.forward_logits_cached(kv, 0, list(range(40)))
+    assert e.value.code == R.ERR_CAPACITY
+    with pytest.raises(R.SocError, match="read range exceeds"):
+        kv.read(0, 0, 0, 5)
+    kv.free()
+    # manifest validation text follows the reference loader
+    import json
+    import shutil
+    bad = tmp_path / "bad"
+    shutil.copytree(Path(p).parent, bad)
+    man = json.loads((bad / "manifest.json").read_text())
+    man["format"] = "other"
+    (bad / "manifest.json").write_text(json.dumps(man))
+    with pytest.raises(R.SocError, match="manifest format must be soc.cpp.llm_export") as e:
+        R.Model(gpu_ctx, bad / "manifest.json")
+    assert e.value.code == R.ERR_FORMAT
+    man["format"] = "soc.cpp.llm_export"
+    man["tensors"] = [t for t in man["tensors"] if "k_norm" not in t["name"]]
+    (bad / "manifest.json").write_text(json.dumps(man))
+    with pytest.raises(R.SocError, match="missing tensor in manifest: model.layers.0.self_attn.k_norm.weight"):
+        R.Model(gpu_ctx, bad / "manifest.json")
+    man = json.loads((Path(p).parent / "manifest.json").read_text())
+    rec = next(t for t in man["tensors"] if t["name"].endswith("layers.1.mlp.up_proj.weight"))
+    with open(bad / rec["file"], "r+b") as f:
+        f.truncate(10)
+    (bad / "manifest.json").write_text(json.dumps(man))
+    with pytest.raises(R.SocError, match="smaller than expected byte_size") as e:
+        R.Model(gpu_ctx, bad / "manifest.json")
+    assert e.value.code == R.ERR_IO
+
+
+def test_generation_context_api(models):
+    p, m = models("tied_f16_gqa2_d64")
+    gc = R.GenerationContext(m, max_sequence_length=24)
+    prompt = _prompt(CASES["tied_f16_gqa2_d64"][0], 6, 8)
+    gc.prefill(prompt)
+    first = O.argmax(gc._last_logits)
+    gc.running_token_ids.append(first)
+    with pytest.raises(R.SocError, match="match the current sequence tail"):
+        gc.decode_next_token(first + 1)
+    r = gc.decode_next_token(first)
+    toks, _ = O.OracleModel(p, 64).generate(prompt, 2)
+    assert [first, r.token_id] == toks
+    assert gc.generate(prompt, 4) == O.OracleModel(p, 64).generate(prompt, 4)[0]
+
+
+@pytest.mark.parametrize("fixture", sorted(GOLDEN.glob("tiny_*.npz")), ids=lambda q: q.stem)
+def test_reference_golden_vectors_on_gpu(gpu_ctx, fixture, tmp_path):
+    from tests.golden.make_golden import bundle_for, load_fixture
+    fx = load_fixture(fixture)
+    p = bundle_for(fx, tmp_path)
+    m = R.Model(gpu_ctx, p)
+    kv = R.KVCache(m, 1, 64)
+    lg, nid = m.forward_logits_cached(kv, 0, fx["prompt"])
+    assert np.abs(lg - fx["prefill_logits"][-1]).max() <= LOGIT_TOL
+    assert nid == int(fx["greedy"][0])
+    for i, tok in enumerate(fx["decode_inputs"]):
+        lg, nxt = m.decode(kv, [0], [int(tok)])
+        assert np.abs(lg[0] - fx["decode_logits"][i]).max() <= LOGIT_TOL
+        assert int(nxt[0]) == int(fx["greedy"][i + 1])
+    kv.free()
+    m.free()
+
+
+def test_config0_greedy_matches_reference(gpu_ctx):
+    """Benchmark config 0 at full Qwen3-0.6B shape: 16-token prompt + 32 greedy tokens,
+    token-for-token equal to the reference CPU runtime's run (tests/golden/config0_greedy.npz)."""
+    path = GOLDEN / "config0_greedy.npz"
+    if not path.exists():
+        pytest.skip("config-0 golden not generated")
+    from soc_b200.bundle import cached_bundle
+    from tests.golden.make_golden import load_fixture, weights_digest
+    fx = load_fixture(path)
+    meta = fx["meta"]
+    p = cached_bundle("config0", meta["cfg"], seed=meta["seed"], dtype=meta["dtype"])
+    assert weights_digest(p) == meta["weights_sha256"]
+    m = R.Model(gpu_ctx, p)
+    kv = R.KVCache(m, 1, 256)
+    out = m.generate(kv, 0, fx["prompt"], len(fx["greedy"]))
+    assert out == fx["greedy"].tolist()
+    # logits of the first step agree with the reference's top-16
+    kv.reset(0)
+    lg, _ = m.forward_logits_cached(kv, 0, fx["prompt"])
+    assert np.abs(lg[fx["top_ids"][0]] - fx["top_logits"][0]).max() <= LOGIT_TOL
+    kv.free()
+    m.free()
+
+
+@pytest.mark.parametrize("rows", [1, 4, 16, 64])
+@pytest.mark.parametrize("shape", [(2048, 1024), (1024, 2048), (6144, 1024), (1024, 3072), (151936, 1024)],
+                         ids=["q", "o", "gate_up", "down", "lm_head"])
+def test_linear_kernel_against_fp64(gpu_ctx, rows, shape):
+    import torch
+    out_f, in_f = shape
+    g = torch.Generator().manual_seed(out_f + rows)
+    w = (torch.randn(out_f, in_f, generator=g) * 0.02).half()
+    x = torch.randn(rows, in_f, generator=g)
+    ref = x.double() @ w.double().T
+    wd, xd = w.cuda(), x.cuda()
+    y = torch.empty(rows, out_f, device="cuda")
+    gpu_ctx.linear(R.WEIGHTS_F16, wd.data_ptr(), None, out_f, in_f, xd.data_ptr(), rows, y.data_ptr(),
+                   torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    err = (y.double().cpu() - ref).abs().max().item()
+    assert err <= 1e-4 * (in_f ** 0.5), err

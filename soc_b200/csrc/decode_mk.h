@@ -1,0 +1,57 @@
+// Persistent batch-1 decode kernel (decode_mk.cu): one cooperative launch runs
+// `steps` greedy decode steps of one sequence through every layer and the lm_head.
+#pragma once
+
+#include "common.cuh"
+
+namespace socb {
+
+struct MKLayer {
+    const void* wqkv;  // [(hq + 2 hkv) * D, H]
+    const void* wo;    // [H, hq * D]
+    const void* wgu;   // [2 I, H], rows (2j, 2j+1) = (gate_j, up_j)
+    const void* wd;    // [H, I]
+    const float *in_norm, *post_norm, *q_norm, *k_norm;
+};
+
+struct MKParams {
+    int L, H, I, hq, hkv, D, V;
+    float eps;
+    int wfmt;  // WF_F16 / WF_BF16 for the block linears and the embedding/lm_head
+    const MKLayer* layers;  // device array [L]
+    const void* embed;
+    const void* lm_head;
+    const float* final_norm;
+    const float2* rope_cs;
+    int rope_len;
+    // paged KV cache
+    __half* kpool;
+    __half* vpool;
+    size_t kv_layer_stride;  // elements per layer
+    const int* page_table;   // row of this sequence: [max_pages]
+    int page_tokens;
+    int max_pages;
+    // the steps: step t consumes ids[t] at position start + t and writes ids[t + 1]
+    int* ids;
+    int start;
+    int steps;
+    float* logits;  // nullable: [steps, V]
+    // scratch (device)
+    float* h;         // [H] residual stream
+    float* qkv;       // [(hq + 2 hkv) D]
+    float* attn;      // [hq D]
+    float* act;       // [I]
+    float* att_part;  // [hkv][splits][G][D + 2]
+    unsigned int* bars;             // [mk_bar_count(L, hkv)], zeroed before launch
+    unsigned long long* best;       // [steps], zeroed before launch
+    int* err;
+    int att_splits;
+};
+
+int mk_bar_count(int L, int hkv);
+// Whether the persistent kernel supports this shape (else the graph path is used).
+bool mk_supported(int H, int I, int hq, int hkv, int D, int wfmt);
+int mk_grid(int device);
+void mk_launch(const MKParams& p, int grid, cudaStream_t st);
+
+}  // namespace socb

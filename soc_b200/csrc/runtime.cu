@@ -8,6 +8,7 @@
 #include <sys/stat.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -19,6 +20,7 @@
 
 #include "../../include/soc_b200.h"
 #include "common.cuh"
+#include "decode_mk.h"
 #include "json.hpp"
 #include "kernels.h"
 
@@ -288,6 +290,17 @@ struct soc_model {
     const soc_kv* graph_kv = nullptr;
     int graph_splits = 0;
     long long graph_kernels = 0;
+    // persistent batch-1 decode kernel (decode_mk.cu)
+    bool mk_ok = false;
+    int mk_grid = 0;
+    MKLayer* d_mk_layers = nullptr;
+    unsigned* mk_bars = nullptr;
+    int mk_bar_n = 0;
+    unsigned long long* mk_best = nullptr;
+    int mk_best_n = 0;
+    float* mk_att_part = nullptr;
+    size_t mk_att_part_floats = 0;
+    int* mk_ids = nullptr;
 
     void* dmalloc(size_t bytes) {
         void* p = nullptr;
@@ -472,10 +485,84 @@ __global__ void k_step_end(soc_model::LoopState* st, const int* next) {
     st->step += 1;
 }
 
+// Persistent-kernel decode of `steps` tokens of one sequence (see decode_mk.cu).
+void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids, float* logits) {
+    const Config& c = m->cfg;
+    cudaStream_t st = m->ctx->stream;
+    if (start + steps > m->rope_len) throw Error(SOC_B200_ERR_CAPACITY, "decode position beyond the RoPE table");
+    ensure_workspace(m, 16);
+    const int G = static_cast<int>(c.hq / c.hkv);
+    const int hkv = static_cast<int>(c.hkv);
+    const int nb = mk_bar_count(static_cast<int>(c.layers), hkv);
+    if (nb > m->mk_bar_n) {
+        m->dfree(m->mk_bars);
+        m->mk_bars = static_cast<unsigned*>(m->dmalloc(sizeof(unsigned) * nb));
+        m->mk_bar_n = nb;
+    }
+    if (steps > m->mk_best_n) {
+        m->dfree(m->mk_best);
+        m->mk_best_n = std::max(steps, 64);
+        m->mk_best = static_cast<unsigned long long*>(m->dmalloc(sizeof(unsigned long long) * m->mk_best_n));
+    }
+    // split-K over the key range: about 128 keys per CTA, at most one CTA per (kv head, split)
+    const int max_ctx = start + steps;
+    int S = (max_ctx + 127) / 128;
+    S = std::max(1, std::min(S, m->mk_grid / hkv));
+    const size_t part = static_cast<size_t>(hkv) * S * G * (c.hd + 2);
+    if (part > m->mk_att_part_floats) {
+        m->dfree(m->mk_att_part);
+        m->mk_att_part = static_cast<float*>(m->dmalloc(sizeof(float) * part));
+        m->mk_att_part_floats = part;
+    }
+    SOCB_CUDA(cudaMemsetAsync(m->mk_bars, 0, sizeof(unsigned) * nb, st));
+    SOCB_CUDA(cudaMemsetAsync(m->mk_best, 0, sizeof(unsigned long long) * steps, st));
+    MKParams p{};
+    p.L = static_cast<int>(c.layers);
+    p.H = static_cast<int>(c.hidden);
+    p.I = static_cast<int>(c.inter);
+    p.hq = static_cast<int>(c.hq);
+    p.hkv = hkv;
+    p.D = static_cast<int>(c.hd);
+    p.V = static_cast<int>(c.vocab);
+    p.eps = static_cast<float>(c.eps);
+    p.wfmt = m->wfmt;
+    p.layers = m->d_mk_layers;
+    p.embed = m->embed;
+    p.lm_head = m->lm_head;
+    p.final_norm = m->final_norm;
+    p.rope_cs = m->rope_cs;
+    p.rope_len = m->rope_len;
+    p.kpool = kv->k;
+    p.vpool = kv->v;
+    p.kv_layer_stride = kv->layer_stride();
+    p.page_table = kv->d_page_table + static_cast<size_t>(seq) * kv->max_pages;
+    p.page_tokens = kv->page_tokens;
+    p.max_pages = kv->max_pages;
+    p.ids = d_ids;
+    p.start = start;
+    p.steps = steps;
+    p.logits = logits;
+    p.h = m->h;
+    p.qkv = m->qkv;
+    p.attn = m->att;
+    p.act = m->act;
+    p.att_part = m->mk_att_part;
+    p.bars = m->mk_bars;
+    p.best = m->mk_best;
+    p.err = m->ctx->d_err;
+    p.att_splits = S;
+    mk_launch(p, m->mk_grid, st);
+    count_launches(1);
+}
+
 // `steps` decode steps of sequence `seq`, whose cache holds `start` tokens and whose
 // next input id is d_out[0]; writes ids 1..steps of d_out.  One step is captured as a
 // CUDA graph (bound to this cache and split count) and replayed per token.
 void decode_loop(soc_model* m, soc_kv* kv, int seq, int start, int steps, int32_t* d_out) {
+    if (m->mk_ok) {
+        run_mk(m, kv, seq, start, steps, d_out, nullptr);
+        return;
+    }
     cudaStream_t st = m->ctx->stream;
     const int splits = attention_splits(1, static_cast<int>(m->cfg.hkv), start + steps);
     ensure_workspace(m, 1);
@@ -677,6 +764,24 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
         m->rope_cs = static_cast<float2*>(m->dmalloc(cs.size() * sizeof(float2)));
         SOCB_CUDA(cudaMemcpy(m->rope_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice));
         ensure_workspace(m.get(), 16);
+        // Persistent decode kernel, unless the shape is outside its limits or the
+        // caller asks for the graph path (SOC_B200_DECODE_PATH=graph).
+        const char* path = std::getenv("SOC_B200_DECODE_PATH");
+        const bool want_mk = !(path && std::string(path) == "graph");
+        if (want_mk && mk_supported(static_cast<int>(H), static_cast<int>(I), static_cast<int>(c.hq),
+                                    static_cast<int>(c.hkv), static_cast<int>(D), fmt) &&
+            m->efmt == fmt) {
+            std::vector<MKLayer> ml(c.layers);
+            for (size_t l = 0; l < c.layers; ++l) {
+                const LayerW& w = m->layers[l];
+                ml[l] = MKLayer{w.wqkv, w.wo, w.wgu, w.wd, w.in_norm, w.post_norm, w.q_norm, w.k_norm};
+            }
+            m->d_mk_layers = static_cast<MKLayer*>(m->dmalloc(sizeof(MKLayer) * c.layers));
+            SOCB_CUDA(cudaMemcpy(m->d_mk_layers, ml.data(), sizeof(MKLayer) * c.layers, cudaMemcpyHostToDevice));
+            m->mk_ids = static_cast<int*>(m->dmalloc(sizeof(int) * 2));
+            m->mk_grid = mk_grid(ctx->device);
+            m->mk_ok = true;
+        }
         SOCB_CUDA(cudaDeviceSynchronize());
     });
     if (rc != SOC_B200_OK) {
@@ -883,6 +988,17 @@ int soc_b200_decode(soc_model* m, soc_kv* kv, int n_seqs, const int* seq_ids, co
         }
         cudaStream_t st = m->ctx->stream;
         for (int i = 0; i < n_seqs; ++i) kv->reserve(seq_ids[i], pos[i] + 1, st);
+        if (n_seqs == 1 && m->mk_ok) {
+            ensure_logits(m, 1);
+            SOCB_CUDA(cudaMemcpyAsync(m->mk_ids, last_ids, sizeof(int), cudaMemcpyHostToDevice, st));
+            run_mk(m, kv, seq_ids[0], pos[0], 1, m->mk_ids, m->logits);
+            if (logits)
+                SOCB_CUDA(cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->cfg.vocab, cudaMemcpyDeviceToHost, st));
+            if (next_ids) SOCB_CUDA(cudaMemcpyAsync(next_ids, m->mk_ids + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
+            check_device_error(m);
+            kv->lengths[seq_ids[0]] = pos[0] + 1;
+            return;
+        }
         ensure_workspace(m, n_seqs);
         SOCB_CUDA(cudaMemcpyAsync(m->d_tokens, last_ids, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, st));
         SOCB_CUDA(cudaMemcpyAsync(m->d_seq, seq_ids, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, st));

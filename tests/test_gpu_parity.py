@@ -27,14 +27,25 @@ CASES = {
 
 @pytest.fixture(scope="module")
 def models(gpu_ctx, make_bundle):
+    """(case, decode path) -> (manifest, Model).  Path "mk" is the persistent batch-1 decode
+    kernel (the default where the shape allows it), "graph" the CUDA-graph of modular kernels."""
+    import os
     cache = {}
 
-    def get(case):
-        if case not in cache:
+    def get(case, path="mk"):
+        if (case, path) not in cache:
             cfg, dt = CASES[case]
             p = make_bundle(case, cfg, seed=7, dtype=dt)
-            cache[case] = (p, R.Model(gpu_ctx, p))
-        return cache[case]
+            old = os.environ.get("SOC_B200_DECODE_PATH")
+            os.environ["SOC_B200_DECODE_PATH"] = path
+            try:
+                cache[(case, path)] = (p, R.Model(gpu_ctx, p))
+            finally:
+                if old is None:
+                    os.environ.pop("SOC_B200_DECODE_PATH")
+                else:
+                    os.environ["SOC_B200_DECODE_PATH"] = old
+        return cache[(case, path)]
 
     yield get
     for _, m in cache.values():
@@ -45,9 +56,10 @@ def _prompt(cfg, n, seed):
     return np.random.default_rng(seed).integers(0, cfg["vocab_size"], n).astype(np.int32)
 
 
+@pytest.mark.parametrize("path", ["mk", "graph"])
 @pytest.mark.parametrize("case", sorted(CASES))
-def test_prefill_and_decode_logits_match_oracle(models, case):
-    p, m = models(case)
+def test_prefill_and_decode_logits_match_oracle(models, case, path):
+    p, m = models(case, path)
     cfg = CASES[case][0]
     kv = R.KVCache(m, 1, 256)
     om = O.OracleModel(p, 256)
@@ -67,9 +79,10 @@ def test_prefill_and_decode_logits_match_oracle(models, case):
     kv.free()
 
 
-@pytest.mark.parametrize("case", ["tied_f16_gqa2_d64", "bf16_gqa4_d128", "qwen06_shape_2layer"])
-def test_generate_matches_oracle_greedy(models, case):
-    p, m = models(case)
+@pytest.mark.parametrize("path", ["mk", "graph"])
+@pytest.mark.parametrize("case", ["tied_f16_gqa2_d64", "bf16_gqa4_d128", "qwen06_shape_2layer", "mha_d128"])
+def test_generate_matches_oracle_greedy(models, case, path):
+    p, m = models(case, path)
     cfg = CASES[case][0]
     kv = R.KVCache(m, 2, 512)
     prompt = _prompt(cfg, 9, 2)
@@ -78,6 +91,17 @@ def test_generate_matches_oracle_greedy(models, case):
     assert kv.length(1) == len(prompt) + 11
     # a second run on the same cache re-uses the captured decode graph
     assert m.generate(kv, 1, prompt, 12) == toks
+    kv.free()
+
+
+@pytest.mark.parametrize("path", ["mk", "graph"])
+def test_generate_long_context_split_k(models, path):
+    """Decode at contexts 300..340 (several attention splits per kv head)."""
+    p, m = models("tied_f16_gqa2_d64", path)
+    prompt = _prompt(CASES["tied_f16_gqa2_d64"][0], 300, 6)
+    toks, _ = O.OracleModel(p, 400).generate(prompt, 40)
+    kv = R.KVCache(m, 1, 512)
+    assert m.generate(kv, 0, prompt, 40) == toks
     kv.free()
 
 
@@ -148,9 +172,11 @@ def test_kv_cache_matches_oracle(models):
     for layer in range(cfg["num_hidden_layers"]):
         k, v = kv.read(0, layer, 0, 21)
         ko, vo = om.kv_read(layer, 0, 21)
-        # fp16 storage: within half an fp16 ulp of the fp32 value, plus kernel rounding
-        assert np.all(np.abs(k - ko) <= np.abs(ko) * 2.0 ** -10 + 2e-4)
-        assert np.all(np.abs(v - vo) <= np.abs(vo) * 2.0 ** -10 + 2e-4)
+        # fp16 storage (half an fp16 ulp of the fp32 value) plus the fp32 rounding the
+        # earlier layers carry in (amplified by the k RMSNorm); indexing itself is pinned
+        # bit-exactly by test_kv_write_read_bit_exact_across_pages.
+        assert np.all(np.abs(k - ko) <= np.abs(ko) * 2.0 ** -10 + 5e-3), np.abs(k - ko).max()
+        assert np.all(np.abs(v - vo) <= np.abs(vo) * 2.0 ** -10 + 5e-3), np.abs(v - vo).max()
     kv.free()
 
 

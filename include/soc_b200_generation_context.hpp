@@ -1,0 +1,135 @@
+// C++ host-side mirror of the reference runtime's GenerationContext over the
+// soc_b200 C ABI (header-only).
+//
+// Same call shape as soc::gpu::GenerationContext (Mac/gpu/include/runtime/
+// generation_context.h:23-74): bool-returning Prefill / DecodeNextToken /
+// Generate with a nullable std::string* error_message, Reset(), and the prompt
+// / running token id accessors.  The Metal-specific arguments (MetalContext,
+// PipelineCache*, BufferArena*) have no B200 counterpart: device, stream and
+// buffers live in the soc_ctx / soc_model / soc_kv handles.  Sampling is greedy
+// on the device (top_k 1, the reference's default SamplerConfig), so only the
+// token id -- and the logits row when asked for -- crosses PCIe.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "soc_b200.h"
+
+namespace soc::b200 {
+
+struct GenerationStepResult {
+    int token_id = -1;
+    std::vector<float> logits;  // filled when requested
+};
+
+class GenerationContext {
+public:
+    // `model` and `kv` stay owned by the caller; `seq` is this context's slot in `kv`.
+    GenerationContext(soc_model* model, soc_kv* kv, int seq, std::size_t max_sequence_length)
+        : model_(model), kv_(kv), seq_(seq), max_sequence_length_(max_sequence_length) {
+        soc_b200_model_info(model_, &info_);
+    }
+
+    // generation_context.cpp:17-59: reset, then run the prompt; logits of the last row
+    // go to *last_logits when it is non-null.
+    bool Prefill(const std::vector<int>& token_ids, std::vector<float>* last_logits, std::string* error_message) {
+        if (token_ids.empty()) return Fail("GenerationContext prefill requires at least one token", error_message);
+        if (token_ids.size() > max_sequence_length_)
+            return Fail("GenerationContext sequence length would exceed max_sequence_length", error_message);
+        Reset();
+        std::vector<int32_t> ids(token_ids.begin(), token_ids.end());
+        std::vector<float> row;
+        if (last_logits) row.resize(static_cast<std::size_t>(info_.vocab));
+        int32_t next = -1;
+        if (soc_b200_prefill(model_, kv_, seq_, ids.data(), static_cast<int>(ids.size()),
+                             last_logits ? row.data() : nullptr, &next) != SOC_B200_OK)
+            return Fail(soc_b200_last_error(), error_message);
+        if (last_logits) *last_logits = std::move(row);
+        prompt_token_ids_ = token_ids;
+        running_token_ids_ = token_ids;
+        prefill_next_ = next;
+        return true;
+    }
+
+    // generation_context.cpp:61-116: the tail and length checks, one step, greedy pick.
+    bool DecodeNextToken(int last_token_id, GenerationStepResult* result, std::string* error_message,
+                         bool want_logits = false) {
+        if (result == nullptr) return Fail("GenerationContext decode requires a non-null result", error_message);
+        if (running_token_ids_.empty())
+            return Fail("GenerationContext decode requires a prefilled KV cache", error_message);
+        if (running_token_ids_.back() != last_token_id)
+            return Fail("GenerationContext decode requires last_token_id to match the current sequence tail",
+                        error_message);
+        if (running_token_ids_.size() >= max_sequence_length_)
+            return Fail("GenerationContext sequence length would exceed max_sequence_length", error_message);
+        const int seq = seq_;
+        const int32_t last = last_token_id;
+        int32_t next = -1;
+        if (want_logits) result->logits.resize(static_cast<std::size_t>(info_.vocab));
+        if (soc_b200_decode(model_, kv_, 1, &seq, &last, want_logits ? result->logits.data() : nullptr, &next) !=
+            SOC_B200_OK)
+            return Fail(soc_b200_last_error(), error_message);
+        result->token_id = next;
+        running_token_ids_.push_back(next);
+        return true;
+    }
+
+    // generation_context.cpp:118-172, with the decode loop resident on the device.
+    bool Generate(const std::vector<int>& prompt_token_ids, std::size_t max_new_tokens, int eos_token_id,
+                  std::vector<int>* generated_token_ids, std::string* error_message) {
+        if (generated_token_ids == nullptr)
+            return Fail("GenerationContext generate requires a non-null generated_token_ids output", error_message);
+        generated_token_ids->clear();
+        if (prompt_token_ids.empty()) return Fail("GenerationContext prefill requires at least one token", error_message);
+        if (prompt_token_ids.size() + (max_new_tokens ? max_new_tokens - 1 : 0) > max_sequence_length_)
+            return Fail("GenerationContext sequence length would exceed max_sequence_length", error_message);
+        Reset();
+        std::vector<int32_t> ids(prompt_token_ids.begin(), prompt_token_ids.end());
+        std::vector<int32_t> out(max_new_tokens ? max_new_tokens : 1);
+        int n = 0;
+        if (soc_b200_generate(model_, kv_, seq_, ids.data(), static_cast<int>(ids.size()),
+                              static_cast<int>(max_new_tokens), eos_token_id, out.data(), &n) != SOC_B200_OK)
+            return Fail(soc_b200_last_error(), error_message);
+        generated_token_ids->assign(out.begin(), out.begin() + n);
+        prompt_token_ids_ = prompt_token_ids;
+        running_token_ids_ = prompt_token_ids;
+        running_token_ids_.insert(running_token_ids_.end(), generated_token_ids->begin(), generated_token_ids->end());
+        return true;
+    }
+
+    // generation_context.cpp:174-179
+    void Reset() {
+        soc_b200_kv_reset(kv_, seq_);
+        prompt_token_ids_.clear();
+        running_token_ids_.clear();
+        prefill_next_ = -1;
+    }
+
+    // Greedy id of the prompt's last row after Prefill (the first generated token).
+    int prefill_next_token() const { return prefill_next_; }
+    // Appends the id picked after Prefill to the running sequence (what Generate does).
+    void AcceptPrefillToken() { running_token_ids_.push_back(prefill_next_); }
+
+    const std::vector<int>& prompt_token_ids() const { return prompt_token_ids_; }
+    const std::vector<int>& running_token_ids() const { return running_token_ids_; }
+
+private:
+    static bool Fail(const char* msg, std::string* error_message) {
+        if (error_message != nullptr) *error_message = msg;
+        return false;
+    }
+
+    soc_model* model_;
+    soc_kv* kv_;
+    int seq_;
+    std::size_t max_sequence_length_;
+    soc_model_info info_{};
+    std::vector<int> prompt_token_ids_;
+    std::vector<int> running_token_ids_;
+    int prefill_next_ = -1;
+};
+
+}  // namespace soc::b200

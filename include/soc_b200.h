@@ -139,6 +139,22 @@ SOC_B200_API int soc_b200_generate_device(soc_model* model, soc_kv* kv, int seq,
 SOC_B200_API int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* scales, int out_features,
                     int in_features, const float* x, int rows, float* y, void* stream);
 
+/* One batch-1 decode step of sequence `seq` that allocates no device memory.
+ * No counterpart in the reference.  For callers that cannot call cudaMalloc
+ * while serving (an engine that gives the whole GPU to its own pool at
+ * start-up, or a latency path that must not take cudaMalloc's implicit device
+ * synchronisation).  Same inputs and outputs as soc_b200_decode with one
+ * sequence: last_id is appended at the cached length, logits (nullable, host)
+ * receives the vocab row, next_id the greedy id.  All scratch of the step lives
+ * in one static device array of 4 MiB that every GPU loading this library keeps
+ * until exit; a model whose step needs more is rejected with
+ * SOC_B200_ERR_CAPACITY, and shapes outside the persistent decode kernel's
+ * limits with SOC_B200_ERR_INVALID.  The first call on a device looks up the
+ * array's device address, so make it before any stream capture.  Calls share
+ * the array: calls whose GPU work overlaps race. */
+SOC_B200_API int soc_b200_decode_noalloc(soc_model* model, soc_kv* kv, int seq, int32_t last_id, float* logits,
+                                         int32_t* next_id);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,7 @@
 #include <cstring>
 #include <fstream>
 #include <memory>
+#include <mutex>
 #include <sstream>
 #include <string>
 #include <unordered_map>
@@ -1093,3 +1094,140 @@ int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode step that allocates nothing (soc_b200_decode_noalloc).
+//
+// Some hosts cannot allocate device memory while serving: for example an
+// engine that hands every byte of the GPU to its own pool at start-up, or a
+// caller that must not make cudaMalloc's implicit device synchronisation on its
+// latency path.  This entry point runs one batch-1 decode step through the
+// persistent decode kernel with all of that kernel's scratch -- residual and
+// activation vectors, split-K attention partials, dependency counters, the
+// argmax slot and the logits row -- in one file-scope device array of fixed size.
+// Every GPU that loads this library keeps that array (kNoAllocScratchBytes)
+// until the process exits.  All calls share the array and it keeps the last
+// call's contents: the counters and the argmax slot are cleared at the start of
+// each call; calls whose GPU work overlaps (other streams, other threads) race.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 128;
+void* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on `device` (which must be current).  The host-side
+// symbol is only a stand-in, so the address comes from cudaGetSymbolAddress, once per device.
+void* noalloc_scratch(int device) {
+    if (device < 0 || device >= kMaxDevices) throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: device index out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[device] == nullptr) {
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || ptr == nullptr)
+            throw Error(SOC_B200_ERR_CUDA, std::string("decode_noalloc: cudaGetSymbolAddress failed: ") +
+                                               cudaGetErrorString(e));
+        g_noalloc_addr[device] = ptr;
+    }
+    return g_noalloc_addr[device];
+}
+}  // namespace
+
+extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_t last_id, float* logits,
+                                       int32_t* next_id) {
+    if (!m || !kv) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (kv->m != m) return fail(SOC_B200_ERR_INVALID, "kv cache belongs to another model");
+    return guarded([&] {
+        const Config& c = m->cfg;
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        cudaStream_t st = m->ctx->stream;
+        const int H = static_cast<int>(c.hidden), I = static_cast<int>(c.inter), hq = static_cast<int>(c.hq);
+        const int hkv = static_cast<int>(c.hkv), D = static_cast<int>(c.hd), V = static_cast<int>(c.vocab);
+        if (!mk_supported(H, I, hq, hkv, D, m->wfmt) || m->efmt != m->wfmt)
+            throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: model shape not supported by the persistent decode kernel");
+        kv->check_seq(seq);
+        check_ids(m, &last_id, 1);
+        const int pos = kv->lengths[seq];
+        if (pos == 0) throw Error(SOC_B200_ERR_INVALID, "GenerationContext decode requires a prefilled KV cache");
+        if (pos + 1 > m->rope_len) throw Error(SOC_B200_ERR_CAPACITY, "decode position beyond the RoPE table");
+        kv->reserve(seq, pos + 1, st);
+
+        const int grid = mk_grid(m->ctx->device);
+        const int G = hq / hkv;
+        int S = (pos + 1 + 127) / 128;
+        S = std::max(1, std::min(S, grid / hkv));
+        const int nb = mk_bar_count(static_cast<int>(c.layers), hkv);
+        // carve the array (256-byte aligned pieces)
+        char* base = static_cast<char*>(noalloc_scratch(m->ctx->device));
+        size_t off = 0;
+        auto carve = [&](size_t bytes) {
+            char* q = base + off;
+            off += (bytes + 255) / 256 * 256;
+            return static_cast<void*>(q);
+        };
+        auto* bars = static_cast<unsigned*>(carve(sizeof(unsigned) * nb));
+        auto* best = static_cast<unsigned long long*>(carve(sizeof(unsigned long long)));
+        auto* ids = static_cast<int*>(carve(sizeof(int) * 2));
+        auto* h = static_cast<float*>(carve(sizeof(float) * H));
+        auto* qkv = static_cast<float*>(carve(sizeof(float) * (hq + 2 * hkv) * D));
+        auto* attn = static_cast<float*>(carve(sizeof(float) * hq * D));
+        auto* act = static_cast<float*>(carve(sizeof(float) * I));
+        auto* part = static_cast<float*>(carve(sizeof(float) * static_cast<size_t>(hkv) * S * G * (D + 2)));
+        auto* lg = static_cast<float*>(carve(sizeof(float) * V));
+        if (off > kNoAllocScratchBytes)
+            throw Error(SOC_B200_ERR_CAPACITY, "decode_noalloc: this model needs " + std::to_string(off) +
+                                                   " bytes of scratch, above the static maximum of " +
+                                                   std::to_string(kNoAllocScratchBytes));
+        SOCB_CUDA(cudaMemsetAsync(bars, 0, sizeof(unsigned) * nb, st));
+        SOCB_CUDA(cudaMemsetAsync(best, 0, sizeof(unsigned long long), st));
+        SOCB_CUDA(cudaMemcpyAsync(ids, &last_id, sizeof(int), cudaMemcpyHostToDevice, st));
+
+        MKParams p{};
+        p.L = static_cast<int>(c.layers);
+        p.H = H;
+        p.I = I;
+        p.hq = hq;
+        p.hkv = hkv;
+        p.D = D;
+        p.V = V;
+        p.eps = static_cast<float>(c.eps);
+        p.wfmt = m->wfmt;
+        p.layers = m->d_mk_layers;
+        p.embed = m->embed;
+        p.lm_head = m->lm_head;
+        p.final_norm = m->final_norm;
+        p.rope_cs = m->rope_cs;
+        p.rope_len = m->rope_len;
+        p.kpool = kv->k;
+        p.vpool = kv->v;
+        p.kv_layer_stride = kv->layer_stride();
+        p.page_table = kv->d_page_table + static_cast<size_t>(seq) * kv->max_pages;
+        p.page_tokens = kv->page_tokens;
+        p.max_pages = kv->max_pages;
+        p.ids = ids;
+        p.start = pos;
+        p.steps = 1;
+        p.logits = lg;
+        p.h = h;
+        p.qkv = qkv;
+        p.attn = attn;
+        p.act = act;
+        p.att_part = part;
+        p.bars = bars;
+        p.best = best;
+        p.err = m->ctx->d_err;
+        p.att_splits = S;
+        if (p.layers == nullptr)
+            throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: the model was loaded without the persistent decode kernel");
+        mk_launch(p, grid, st);
+        count_launches(1);
+        if (logits) SOCB_CUDA(cudaMemcpyAsync(logits, lg, sizeof(float) * V, cudaMemcpyDeviceToHost, st));
+        int nid = 0;
+        SOCB_CUDA(cudaMemcpyAsync(&nid, ids + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
+        check_device_error(m);
+        kv->lengths[seq] = pos + 1;
+        if (next_id) *next_id = nid;
+    });
+}

@@ -73,6 +73,7 @@ _SIGNATURES = {
                                     C.POINTER(C.c_int)]),
     "soc_b200_generate_device": (C.c_int, [_VP, _VP, C.c_int, _VP, C.c_int, C.c_int, _VP]),
     "soc_b200_linear": (C.c_int, [_VP, C.c_int, _VP, _VP, C.c_int, C.c_int, _VP, C.c_int, _VP, _VP]),
+    "soc_b200_decode_noalloc": (C.c_int, [_VP, _VP, C.c_int, C.c_int32, _FP, _I32P]),
 }
 
 
@@ -170,6 +171,15 @@ class Model:
         _check(lib().soc_b200_decode(self.h, kv.h, n, _ip(seq_ids), _ip(last_ids),
                                      _fp(logits) if logits is not None else None, _ip(nxt)))
         return logits, nxt
+
+    def decode_noalloc(self, kv: "KVCache", seq: int, last_id: int, want_logits=True):
+        """One decode step that allocates no device memory (``soc_b200_decode_noalloc``):
+        for hosts that cannot call cudaMalloc while serving."""
+        logits = np.empty(self.vocab, dtype=np.float32) if want_logits else None
+        nid = np.zeros(1, dtype=np.int32)
+        _check(lib().soc_b200_decode_noalloc(self.h, kv.h, seq, int(last_id),
+                                             _fp(logits) if logits is not None else None, _ip(nid)))
+        return logits, int(nid[0])
 
     def generate(self, kv: "KVCache", seq: int, prompt, max_new: int, eos: int = -1) -> list[int]:
         prompt = _i32(prompt)

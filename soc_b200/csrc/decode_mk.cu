@@ -6,44 +6,59 @@
 // residual] -> final RMSNorm -> tied lm_head -> argmax, feeding each id to the
 // next step on the device.  Same arithmetic as the modular kernels (and the
 // reference: Mac/cpu/src/qwen_block.cpp:63-72, qwen_attention.cpp:142-205,
-// qwen_mlp.cpp:65-74, qwen_causal_lm.cpp:82-116, sampler.cpp:26-62).
+// qwen_mlp.cpp:65-74, qwen_causal_lm.cpp:82-116, sampler.cpp:26-62), except
+// that the RMSNorm scale is applied after the dot product:
+// sum_i W[r,i] (x_i s w_i) = s * sum_i W[r,i] (x_i w_i).
 //
 // Batch-1 decode streams every weight byte once per token (1.19 GB for
-// Qwen3-0.6B), so the kernel is HBM-bound.  Layout of the work:
+// Qwen3-0.6B) and is a chain of ~140 dependent matrix-vector phases, so the
+// design works on two things: keeping HBM busy across the dependencies, and
+// making each dependency hand-off short.
 //   * warp 0, lane 0 is a producer: it walks this CTA's share of every weight
 //     matrix in execution order and streams it into a 5 x 32 KB shared-memory
 //     ring with cp.async.bulk (TMA bulk copies, mbarrier completion, L2
-//     evict-first).  It never waits on activations, so HBM keeps streaming the
-//     next matrices while the consumers wait at a dependency.
-//   * warps 1..8 are consumers: per matrix they stage the input vector once per
-//     CTA (with the RMSNorm fused), hold their slice of it in registers, and
-//     reduce 16-byte weight vectors from the ring with fp32 FMAs and warp
-//     shuffles.  Each matrix's rows are split into contiguous per-CTA ranges.
-//   * dependencies between matrices are monotonic global counters: a CTA
-//     releases (fence + atomic add) after its rows are written; consumers of
-//     the next phase acquire (ld.acquire.gpu spin, bounded).  Attention runs on
-//     kv_heads x splits CTAs with a split-K combine by the last arriving CTA.
+//     evict-first).  It never waits on activations.
+//   * warps 1..7 are consumers: per matrix they stage the input vector once per
+//     CTA (double-buffered, one CTA barrier per phase), hold their slice of it in
+//     registers and reduce 16-byte weight vectors from the ring with fp32 FMAs
+//     and warp shuffles.  Each matrix's rows are split into contiguous per-CTA
+//     ranges.
+//   * hand-offs between matrices are monotonic counters, one per layer and
+//     phase: a CTA adds 1 with release semantics after its rows are stored, and
+//     a CTA that needs the vector waits (one thread, acquire) for the count.
+//   * attention runs on kv_heads x splits CTAs; the cached keys, the RoPE row
+//     and the norm weights are loaded before the q/k/v rows arrive.  With more
+//     than one split the last CTA of a kv head combines the partials.
 // Every wait is bounded: on expiry the kernel sets DERR_WAIT_TIMEOUT in *err,
-// which makes every other wait return at once, and the kernel winds down.
+// which makes every other wait return at once, and the kernel winds down
+// (the producer first waits, bounded, for its copies in flight).
 #include "decode_mk.h"
 
 namespace socb {
 namespace {
 
-constexpr int NC = 8;                   // consumer warps
-constexpr int THREADS = (NC + 1) * 32;  // + producer warp
-constexpr int SLOTS = 5;
+constexpr int NC = 7;                   // consumer warps (256 threads per CTA: up to 255 registers)
+constexpr int CT = NC * 32;             // consumer threads
+constexpr int THREADS = CT + 32;        // + producer warp
+constexpr int SLOTS = 6;
 constexpr int SLOT_BYTES = 32 * 1024;
-constexpr int XBUF = 4352;              // floats: max K (4096) and the attention merge area
-constexpr int MAXG = 4;                 // query heads per kv head
+constexpr int INFLIGHT = SLOTS;         // TMA loads into shared memory in flight per CTA
+constexpr int PF_CHUNKS = 0;            // chunks prefetched into L2 ahead of the load cursor
+constexpr int XMAX = 3072;              // widest staged input (floats)
+constexpr int HMAX = 1024;              // widest hidden size
+constexpr int MAXG = 2;                 // query heads per kv head
+constexpr int KPF = 8;                  // keys per warp per attention batch
+constexpr int MAXFL = 5;                // phase flags polled per lane (grid <= 160)
 constexpr unsigned SPIN_LIMIT = 1u << 21;
 
 enum Kind { K_QKV = 0, K_O = 1, K_GU = 2, K_D = 3, K_LM = 4 };
+enum Ep { E_QKV = 0, E_ATT = 1, E_HO = 2, E_ACT = 3, E_HD = 4, E_LM = 5 };
 
 struct __align__(128) Smem {
     uint8_t ring[SLOTS][SLOT_BYTES];
-    float x[XBUF];
-    float red[NC];
+    float x[2][XMAX];
+    float hraw[2][HMAX];
+    float red[2][NC];
     unsigned long long best[NC];
     unsigned long long full[SLOTS];
     unsigned long long empty[SLOTS];
@@ -87,14 +102,33 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
         "l"(src), "r"(bytes), "r"(s32(bar)), "l"(pol)
         : "memory");
 }
-__device__ __forceinline__ void nbar() { asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory"); }
+// Fire-and-forget prefetch of a global range into L2 (no data returns to the SM).
+__device__ __forceinline__ void prefetch_l2(const void* src, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void nbar() { asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory"); }
+
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ bool aborted(const int* err) {
     return (*reinterpret_cast<const volatile int*>(err) & DERR_WAIT_TIMEOUT) != 0;
 }
 
+__device__ __forceinline__ unsigned ld_flag(const unsigned* f) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_flag_release(unsigned* f, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
 // Bounded wait on an mbarrier phase (non-blocking test + short sleep per try).
-__device__ bool mbar_wait(unsigned long long* b, unsigned parity, int* err) {
+__device__ __forceinline__ bool mbar_wait(unsigned long long* b, unsigned parity, int* err) {
     for (unsigned i = 0;; ++i) {
         if (mbar_test(b, parity)) return true;
         if ((i & 255u) == 255u && aborted(err)) return false;
@@ -106,8 +140,50 @@ __device__ bool mbar_wait(unsigned long long* b, unsigned parity, int* err) {
     }
 }
 
-// Bounded acquire-wait until *c >= target.
-__device__ bool wait_count(const unsigned* c, unsigned target, int* err) {
+// Hand-offs between phases are monotonic counters, one per (layer, phase): when a CTA's
+// part of a phase is stored it adds 1 with release semantics; a CTA that needs the phase's
+// output waits (one thread, acquire) until the counter reaches (step + 1) * contributors.
+// A device-wide hand-off of this kind measured about 1 us on B200 with 148 CTAs; polling
+// one flag per CTA instead was about 4 us (148 writers and pollers on the same lines).
+//   [l * 6 + e]        e in {E_QKV, E_ATT, E_HO, E_ACT, E_HD}; E_ATT counts kv heads
+//   [L * 6]            lm_head done (per CTA)
+//   [L * 6 + 1 + l * hkv + j]  split-K arrivals of kv head j
+__device__ __forceinline__ unsigned* ctr(const MKParams& p, int l, int e) { return p.flags + l * 6 + e; }
+__device__ __forceinline__ unsigned* ctr_lm(const MKParams& p) { return p.flags + p.L * 6; }
+__device__ __forceinline__ unsigned* split_ctr(const MKParams& p, int l, int j) {
+    return p.flags + p.L * 6 + 1 + l * p.hkv + j;
+}
+
+__device__ __forceinline__ void red_release_add(unsigned* c) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
+}
+
+// One consumer thread waits (bounded) until *c >= target with acquire semantics; then the CTA barrier.
+__device__ __forceinline__ void wait_ctr(const unsigned* c, unsigned target, int* err, int ctid) {
+    if (ctid == 0) {
+        for (unsigned i = 0;; ++i) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+            if (v >= target) break;
+            if (i > SPIN_LIMIT) {
+                atomicOr(err, DERR_WAIT_TIMEOUT);
+                break;
+            }
+            if ((i & 63u) == 63u && aborted(err)) break;
+            if (i > 4) __nanosleep(32);
+        }
+    }
+    nbar();
+}
+
+// After this CTA's part of a phase is stored: the CTA barrier, then one release add.
+__device__ __forceinline__ void signal(unsigned* c, int ctid) {
+    nbar();
+    if (ctid == 0) red_release_add(c);
+}
+
+// Bounded acquire-wait until *c >= target (split-K counters).
+__device__ __forceinline__ bool wait_count(const unsigned* c, unsigned target, int* err) {
     for (unsigned i = 0;; ++i) {
         unsigned v;
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
@@ -117,23 +193,21 @@ __device__ bool wait_count(const unsigned* c, unsigned target, int* err) {
             atomicOr(err, DERR_WAIT_TIMEOUT);
             return false;
         }
-        __nanosleep(64);
+        if (i > 8) __nanosleep(32);
     }
 }
 
-__device__ __forceinline__ void release_add(unsigned* c) {
-    __threadfence();
-    atomicAdd(c, 1u);
-}
-
-// Consumer-side dependency wait: one thread spins, the others meet it at the named barrier.
-__device__ __forceinline__ void cwait(const unsigned* c, unsigned target, int* err, int ctid) {
-    if (ctid == 0) {
-        wait_count(c, target, err);
-        __threadfence();
-    }
-    nbar();
-}
+// Trace slot `e` of layer `l` (first step only, consumer thread 0).  Slots per layer:
+// 0 start, 1 qkv input ready, 2 qkv staged, 3 qkv first chunk, 4 qkv done, 5 attention input
+// ready, 6 attention done, 7 o input ready, 8 o first chunk, 9 o done, 10 gu input ready,
+// 11 gu first chunk, 12 gu done, 13 down input ready, 14 down first chunk, 15 down done.
+// Layer L holds the lm_head: 1 input ready, 2 staged, 3 first chunk, 4 done.
+#define MK_TR(l, e)                                                                                                  \
+    do {                                                                                                             \
+        if (p.trace != nullptr && sc.t == 0 && ctid == 0)                                                            \
+            p.trace[static_cast<size_t>(blockIdx.x) * mk_trace_stride(p.L) + (l) * MK_TRACE_PER_LAYER + (e)] =      \
+                gtime();                                                                                             \
+    } while (0)
 
 // ------------------------------------------------------------------- schedule
 struct Phase {
@@ -141,41 +215,36 @@ struct Phase {
     int units, unit_bytes, K, rows;  // rows per unit: 1, or 2 for (gate, up)
 };
 
-__device__ __forceinline__ Phase phase_of(const MKParams& p, int l, int kind) {
+__device__ __forceinline__ Phase phase_of(const MKParams& p, const MKLayer& ly, int kind) {
     Phase ph;
-    if (kind == K_LM) {
-        ph.w = static_cast<const uint8_t*>(p.lm_head);
-        ph.units = p.V;
-        ph.K = p.H;
-        ph.rows = 1;
-    } else {
-        const MKLayer& ly = p.layers[l];
-        switch (kind) {
-            case K_QKV:
-                ph.w = static_cast<const uint8_t*>(ly.wqkv);
-                ph.units = (p.hq + 2 * p.hkv) * p.D;
-                ph.K = p.H;
-                ph.rows = 1;
-                break;
-            case K_O:
-                ph.w = static_cast<const uint8_t*>(ly.wo);
-                ph.units = p.H;
-                ph.K = p.hq * p.D;
-                ph.rows = 1;
-                break;
-            case K_GU:
-                ph.w = static_cast<const uint8_t*>(ly.wgu);
-                ph.units = p.I;
-                ph.K = p.H;
-                ph.rows = 2;
-                break;
-            default:
-                ph.w = static_cast<const uint8_t*>(ly.wd);
-                ph.units = p.H;
-                ph.K = p.I;
-                ph.rows = 1;
-                break;
-        }
+    ph.rows = 1;
+    switch (kind) {
+        case K_QKV:
+            ph.w = static_cast<const uint8_t*>(ly.wqkv);
+            ph.units = (p.hq + 2 * p.hkv) * p.D;
+            ph.K = p.H;
+            break;
+        case K_O:
+            ph.w = static_cast<const uint8_t*>(ly.wo);
+            ph.units = p.H;
+            ph.K = p.hq * p.D;
+            break;
+        case K_GU:
+            ph.w = static_cast<const uint8_t*>(ly.wgu);
+            ph.units = p.I;
+            ph.K = p.H;
+            ph.rows = 2;
+            break;
+        case K_D:
+            ph.w = static_cast<const uint8_t*>(ly.wd);
+            ph.units = p.H;
+            ph.K = p.I;
+            break;
+        default:
+            ph.w = static_cast<const uint8_t*>(p.lm_head);
+            ph.units = p.V;
+            ph.K = p.H;
+            break;
     }
     ph.unit_bytes = ph.rows * ph.K * 2;
     return ph;
@@ -189,39 +258,116 @@ __device__ __forceinline__ void cta_range(int units, int cta, int G, int l, int 
     b = static_cast<int>(static_cast<long long>(units) * (v + 1) / G);
 }
 
-// Barrier counter indices.
-__device__ __forceinline__ int bar_phase(int l, int k) { return l * 5 + k; }  // k: 0 qkv, 1 attn, 2 o, 3 gu, 4 d
-__device__ __forceinline__ int bar_lm(const MKParams& p) { return p.L * 5; }
-__device__ __forceinline__ int bar_split(const MKParams& p, int l, int j) { return p.L * 5 + 1 + l * p.hkv + j; }
-
 // ------------------------------------------------------------------- producer
-__device__ void produce_phase(const MKParams& p, Smem& sm, const Phase& ph, int l, int kind, long long& k, uint64_t pol,
-                              bool& ok) {
-    int a, b;
-    cta_range(ph.units, blockIdx.x, gridDim.x, l, kind, a, b);
-    const int cu = max(1, SLOT_BYTES / ph.unit_bytes);
-    for (int u = a; u < b && ok; u += cu, ++k) {
-        const int n = min(cu, b - u);
+// Walks this CTA's chunks in consumption order: per step, per layer the qkv, o, gate/up and
+// down matrices, then the lm_head.  A chunk is up to SLOT_BYTES of whole units.
+struct Cursor {
+    int t, l, kind, u;  // kind == K_LM means the lm_head of step t
+    int a, b, cu;       // unit range of this CTA in the current phase, units per chunk
+    const uint8_t* w;
+    int unit_bytes;
+    bool done;
+};
+
+__device__ __forceinline__ void cursor_phase(const MKParams& p, Cursor& c) {
+    const Phase ph = phase_of(p, p.layers[c.kind == K_LM ? 0 : c.l], c.kind);
+    cta_range(ph.units, blockIdx.x, gridDim.x, c.l, c.kind, c.a, c.b);
+    c.cu = max(1, SLOT_BYTES / ph.unit_bytes);
+    c.w = ph.w;
+    c.unit_bytes = ph.unit_bytes;
+    c.u = c.a;
+}
+
+__device__ __forceinline__ void cursor_init(const MKParams& p, Cursor& c) {
+    c.t = 0;
+    c.l = 0;
+    c.kind = K_QKV;
+    c.done = p.steps <= 0;
+    if (!c.done) cursor_phase(p, c);
+}
+
+// Move to the next phase that has units (every phase has some for this CTA, see mk_supported;
+// an empty one would be skipped here exactly as the consumers' loops skip it).
+__device__ __forceinline__ void cursor_next_phase(const MKParams& p, Cursor& c);
+__device__ __forceinline__ void cursor_next_phase1(const MKParams& p, Cursor& c) {
+    if (c.kind == K_LM) {
+        c.kind = K_QKV;
+        c.l = 0;
+        if (++c.t >= p.steps) {
+            c.done = true;
+            return;
+        }
+    } else if (c.kind == K_D) {
+        if (++c.l >= p.L) {
+            c.kind = K_LM;
+            c.l = 0;
+        } else {
+            c.kind = K_QKV;
+        }
+    } else {
+        ++c.kind;
+    }
+    cursor_phase(p, c);
+}
+
+__device__ __forceinline__ void cursor_next_phase(const MKParams& p, Cursor& c) {
+    do {
+        cursor_next_phase1(p, c);
+    } while (!c.done && c.a >= c.b);
+}
+
+// Current chunk of the cursor (pointer and bytes), then advance.
+__device__ __forceinline__ void cursor_take(const MKParams& p, Cursor& c, const uint8_t*& ptr, unsigned& bytes) {
+    const int n = min(c.cu, c.b - c.u);
+    ptr = c.w + static_cast<size_t>(c.u) * c.unit_bytes;
+    bytes = static_cast<unsigned>(n) * c.unit_bytes;
+    c.u += n;
+    if (c.u >= c.b) cursor_next_phase(p, c);
+}
+
+__device__ __forceinline__ void producer(const MKParams& p, Smem& sm) {
+    const uint64_t pol = evict_first_policy();
+    Cursor ld, pf;
+    cursor_init(p, ld);
+    cursor_init(p, pf);
+    // L2 prefetch runs PF_CHUNKS ahead of the loads into shared memory.
+    for (int i = 0; i < PF_CHUNKS && !pf.done; ++i) {
+        const uint8_t* ptr;
+        unsigned bytes;
+        cursor_take(p, pf, ptr, bytes);
+        prefetch_l2(ptr, bytes);
+    }
+    long long k = 0;
+    bool ok = true;
+    while (!ld.done && ok) {
         const int slot = static_cast<int>(k % SLOTS);
         const long long round = k / SLOTS;
         if (round > 0 && !mbar_wait(&sm.empty[slot], static_cast<unsigned>((round - 1) & 1), p.err)) {
             ok = false;
             break;
         }
-        const unsigned bytes = static_cast<unsigned>(n) * ph.unit_bytes;
+        // keep at most INFLIGHT loads into shared memory outstanding
+        if (INFLIGHT < SLOTS && k >= INFLIGHT) {
+            const long long q = k - INFLIGHT;
+            if (!mbar_wait(&sm.full[q % SLOTS], static_cast<unsigned>((q / SLOTS) & 1), p.err)) {
+                ok = false;
+                break;
+            }
+        }
+        const uint8_t* ptr;
+        unsigned bytes;
+        cursor_take(p, ld, ptr, bytes);
+        if (p.trace != nullptr && k < MK_TRACE_CHUNKS)
+            p.trace[static_cast<size_t>(blockIdx.x) * mk_trace_stride(p.L) + (p.L + 1) * MK_TRACE_PER_LAYER + k] = gtime();
         mbar_expect_tx(&sm.full[slot], bytes);
-        bulk_g2s(sm.ring[slot], ph.w + static_cast<size_t>(u) * ph.unit_bytes, bytes, &sm.full[slot], pol);
-    }
-}
-
-__device__ void producer(const MKParams& p, Smem& sm) {
-    const uint64_t pol = evict_first_policy();
-    long long k = 0;
-    bool ok = true;
-    for (int t = 0; t < p.steps && ok; ++t) {
-        for (int l = 0; l < p.L && ok; ++l)
-            for (int kind = K_QKV; kind <= K_D && ok; ++kind) produce_phase(p, sm, phase_of(p, l, kind), l, kind, k, pol, ok);
-        if (ok) produce_phase(p, sm, phase_of(p, 0, K_LM), 0, K_LM, k, pol, ok);
+        bulk_g2s(sm.ring[slot], ptr, bytes, &sm.full[slot], pol);
+        if (!pf.done) {
+            const uint8_t* pp;
+            unsigned pb;
+            cursor_take(p, pf, pp, pb);
+            prefetch_l2(pp, pb);
+        }
+        ++k;
     }
     // Never leave with copies in flight: wait (bounded) for the last fills to land.
     const long long first = k > SLOTS ? k - SLOTS : 0;
@@ -243,81 +389,85 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&w)[8]) {
     w[4] = c.x; w[5] = c.y; w[6] = d.x; w[7] = d.y;
 }
 
+// Stage K floats (already known ready) into x (and hraw), all consumer threads, 4 per load.
+//   norm_w == nullptr: x = v.
+//   norm_w != nullptr: hraw = v, x = v * w, per-warp sum of squares of v into red.
+//   emb != nullptr: v is the embedding row (layer 0) instead of `src`.
+// Ends with the CTA barrier.
 template <typename T>
-__device__ __forceinline__ float emb_at(const void* table, size_t idx) {
-    const T v = static_cast<const T*>(table)[idx];
-    return static_cast<float>(v);
-}
-
-// Stage the phase input into sm.x: RMSNorm of h (or of the token's embedding row) with weight w,
-// or a plain copy.  All consumer threads take part; ends with a named barrier.
-template <typename T>
-__device__ void stage(Smem& sm, const float* src, const void* emb_row_table, size_t emb_base, int K, const float* w,
-                      float eps, int ctid) {
+__device__ __forceinline__ void stage(const float* src, const void* emb, size_t emb_base, int K, const float* norm_w,
+                                   float* x, float* hraw, float* red, int ctid) {
     const int lane = ctid & 31, cw = ctid >> 5;
     float ss = 0.0f;
-    for (int i = ctid * 4; i < K; i += NC * 32 * 4) {
+    for (int i = 4 * ctid; i < K; i += 4 * CT) {
         float4 v;
-        if (src != nullptr) {
-            v = __ldcg(reinterpret_cast<const float4*>(src + i));
+        if (emb != nullptr) {
+            const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const T*>(emb) + emb_base + i);
+            const float2 a = WTraits<T>::pair(r.x), b = WTraits<T>::pair(r.y);
+            v = make_float4(a.x, a.y, b.x, b.y);
         } else {
-            v.x = emb_at<T>(emb_row_table, emb_base + i);
-            v.y = emb_at<T>(emb_row_table, emb_base + i + 1);
-            v.z = emb_at<T>(emb_row_table, emb_base + i + 2);
-            v.w = emb_at<T>(emb_row_table, emb_base + i + 3);
+            v = __ldcg(reinterpret_cast<const float4*>(src + i));
         }
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        *reinterpret_cast<float4*>(&sm.x[i]) = v;
+        if (norm_w) {
+            const float4 w = *reinterpret_cast<const float4*>(norm_w + i);
+            *reinterpret_cast<float4*>(hraw + i) = v;
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            *reinterpret_cast<float4*>(x + i) = make_float4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
+        } else {
+            *reinterpret_cast<float4*>(x + i) = v;
+        }
     }
-    if (w == nullptr) {
-        nbar();
-        return;
+    if (norm_w) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[cw] = ss;
     }
-    ss = warp_sum(ss);
-    if (lane == 0) sm.red[cw] = ss;
-    nbar();
-    float tot = 0.0f;
-#pragma unroll
-    for (int q = 0; q < NC; ++q) tot += sm.red[q];
-    const float s = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
-    for (int i = ctid; i < K; i += NC * 32) sm.x[i] = sm.x[i] * s * w[i];
     nbar();
 }
 
-template <int KI, typename T>
+__device__ __forceinline__ float norm_scale(const float* red, int K, float eps) {
+    float tot = 0.0f;
+#pragma unroll
+    for (int q = 0; q < NC; ++q) tot += red[q];
+    return 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
+}
+
+template <int KI, typename T, bool two>
 __device__ __forceinline__ void dot2(const uint8_t* r0, const uint8_t* r1, const float (&xr)[KI][8], int lane,
-                                     float& a0, float& a1, bool two) {
-    float s0 = 0.0f, s1 = 0.0f;
+                                     float& a0, float& a1) {
+    float s0 = 0.0f, s0b = 0.0f, s1 = 0.0f, s1b = 0.0f;
 #pragma unroll
     for (int it = 0; it < KI; ++it) {
         const int off = (it * 256 + lane * 8) * 2;
         float w[8];
         unpack8<T>(*reinterpret_cast<const uint4*>(r0 + off), w);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s0 += w[j] * xr[it][j];
+        s0 += w[0] * xr[it][0] + w[1] * xr[it][1] + w[2] * xr[it][2] + w[3] * xr[it][3];
+        s0b += w[4] * xr[it][4] + w[5] * xr[it][5] + w[6] * xr[it][6] + w[7] * xr[it][7];
         if (two) {
             unpack8<T>(*reinterpret_cast<const uint4*>(r1 + off), w);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) s1 += w[j] * xr[it][j];
+            s1 += w[0] * xr[it][0] + w[1] * xr[it][1] + w[2] * xr[it][2] + w[3] * xr[it][3];
+            s1b += w[4] * xr[it][4] + w[5] * xr[it][5] + w[6] * xr[it][6] + w[7] * xr[it][7];
         }
     }
-    a0 = warp_sum(s0);
-    a1 = two ? warp_sum(s1) : 0.0f;
+    a0 = warp_sum(s0 + s0b);
+    a1 = two ? warp_sum(s1 + s1b) : 0.0f;
 }
 
 struct StepCtx {
     int t, tok, pos;
 };
 
-// Consume one phase's chunks from the ring and apply its epilogue.
-template <int KI, typename T>
-__device__ void consume(const MKParams& p, Smem& sm, const Phase& ph, int l, int kind, long long& k, const StepCtx& sc,
-                        int cw, int lane, unsigned long long& wbest) {
+// Consume one phase's chunks from the ring and apply its epilogue.  `s` is the folded
+// RMSNorm scale (1 for phases without a norm), `hraw` the residual stream staged earlier.
+template <int KI, typename T, bool TWO>
+__device__ __forceinline__ void consume(const MKParams& p, Smem& sm, const Phase& ph, int l, int kind, long long& k,
+                                    const StepCtx& sc, const float* x, const float* hraw, float s, int tr_first,
+                                    int ctid, unsigned long long& wbest) {
+    const int cw = ctid >> 5, lane = ctid & 31;
     float xr[KI][8];
 #pragma unroll
     for (int it = 0; it < KI; ++it) {
-        const float4 u = *reinterpret_cast<const float4*>(&sm.x[it * 256 + lane * 8]);
-        const float4 v = *reinterpret_cast<const float4*>(&sm.x[it * 256 + lane * 8 + 4]);
+        const float4 u = *reinterpret_cast<const float4*>(&x[it * 256 + lane * 8]);
+        const float4 v = *reinterpret_cast<const float4*>(&x[it * 256 + lane * 8 + 4]);
         xr[it][0] = u.x; xr[it][1] = u.y; xr[it][2] = u.z; xr[it][3] = u.w;
         xr[it][4] = v.x; xr[it][5] = v.y; xr[it][6] = v.z; xr[it][7] = v.w;
     }
@@ -325,38 +475,59 @@ __device__ void consume(const MKParams& p, Smem& sm, const Phase& ph, int l, int
     cta_range(ph.units, blockIdx.x, gridDim.x, l, kind, a, b);
     const int cu = max(1, SLOT_BYTES / ph.unit_bytes);
     const int rowb = ph.K * 2;
+    bool first = true;
     for (int u = a; u < b; u += cu, ++k) {
         const int n = min(cu, b - u);
         const int slot = static_cast<int>(k % SLOTS);
+        if (p.trace != nullptr && k < MK_TRACE_CHUNKS && ctid == 0)
+            p.trace[static_cast<size_t>(blockIdx.x) * mk_trace_stride(p.L) + (p.L + 1) * MK_TRACE_PER_LAYER +
+                    2 * MK_TRACE_CHUNKS + k] = gtime();
         const bool ok = mbar_wait(&sm.full[slot], static_cast<unsigned>((k / SLOTS) & 1), p.err);
+        if (p.trace != nullptr && k < MK_TRACE_CHUNKS && ctid == 0)
+            p.trace[static_cast<size_t>(blockIdx.x) * mk_trace_stride(p.L) + (p.L + 1) * MK_TRACE_PER_LAYER +
+                    MK_TRACE_CHUNKS + k] = gtime();
+        if (first) {
+            MK_TR(kind == K_LM ? p.L : l, tr_first);
+            first = false;
+        }
         if (ok) {
-            for (int i = cw; i < n; i += NC) {
-                const uint8_t* base = sm.ring[slot] + static_cast<size_t>(i) * ph.unit_bytes;
-                const int unit = u + i;
-                if (kind == K_GU) {
+            // unit g of the phase belongs to warp (g - a) % NC, so the warps stay balanced over
+            // the whole phase even when a chunk's unit count is not a multiple of NC
+            const int i0 = ((cw - (u - a)) % NC + NC) % NC;
+            if (TWO) {
+                // (gate, up) row pairs: one unit per warp at a time
+                for (int i = i0; i < n; i += NC) {
+                    const uint8_t* base = sm.ring[slot] + static_cast<size_t>(i) * ph.unit_bytes;
                     float g, up;
-                    dot2<KI, T>(base, base + rowb, xr, lane, g, up, true);
-                    if (lane == 0) p.act[unit] = silu_f(g) * up;
-                } else if (kind == K_LM) {
-                    float y, unused;
-                    dot2<KI, T>(base, base, xr, lane, y, unused, false);
-                    if (lane == 0) {
-                        if (p.logits) p.logits[static_cast<size_t>(sc.t) * p.V + unit] = y;
-                        if (y == y) {
-                            const unsigned long long key = argmax_key(y, unit);
-                            wbest = key > wbest ? key : wbest;
-                        }
-                    }
-                } else {
-                    float y, unused;
-                    dot2<KI, T>(base, base, xr, lane, y, unused, false);
-                    if (lane == 0) {
-                        if (kind == K_QKV) {
-                            p.qkv[unit] = y;
-                        } else if (kind == K_O && l == 0) {
-                            p.h[unit] = emb_at<T>(p.embed, static_cast<size_t>(sc.tok) * p.H + unit) + y;
-                        } else {
-                            p.h[unit] = __ldcg(p.h + unit) + y;
+                    dot2<KI, T, true>(base, base + rowb, xr, lane, g, up);
+                    if (lane == 0) p.act[u + i] = silu_f(g * s) * (up * s);
+                }
+            } else {
+                // two independent rows per warp at a time (their loads and FMAs interleave)
+                for (int i = i0; i < n; i += 2 * NC) {
+                    const int i2 = i + NC;
+                    const bool has2 = i2 < n;
+                    const uint8_t* r0 = sm.ring[slot] + static_cast<size_t>(i) * ph.unit_bytes;
+                    const uint8_t* r1 = has2 ? sm.ring[slot] + static_cast<size_t>(i2) * ph.unit_bytes : r0;
+                    float y[2];
+                    dot2<KI, T, true>(r0, r1, xr, lane, y[0], y[1]);
+                    if (lane != 0) continue;
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        if (q == 1 && !has2) break;
+                        const int unit = u + (q == 0 ? i : i2);
+                        switch (kind) {
+                            case K_QKV: p.qkv[unit] = y[q] * s; break;
+                            case K_O:
+                            case K_D: p.h[unit] = hraw[unit] + y[q]; break;
+                            default: {
+                                const float yy = y[q] * s;
+                                if (p.logits) p.logits[static_cast<size_t>(sc.t) * p.V + unit] = yy;
+                                if (yy == yy) {
+                                    const unsigned long long key = argmax_key(yy, unit);
+                                    wbest = key > wbest ? key : wbest;
+                                }
+                            }
                         }
                     }
                 }
@@ -369,94 +540,134 @@ __device__ void consume(const MKParams& p, Smem& sm, const Phase& ph, int l, int
 
 template <typename T>
 __device__ void consume_k(const MKParams& p, Smem& sm, const Phase& ph, int l, int kind, long long& k,
-                          const StepCtx& sc, int cw, int lane, unsigned long long& wbest) {
+                          const StepCtx& sc, const float* x, const float* hraw, float s, int trf, int ctid,
+                          unsigned long long& wbest) {
+    if (kind == K_GU) {  // (gate, up) row pairs; K = hidden
+        switch (ph.K / 256) {
+            case 1: consume<1, T, true>(p, sm, ph, l, kind, k, sc, x, hraw, s, trf, ctid, wbest); break;
+            case 2: consume<2, T, true>(p, sm, ph, l, kind, k, sc, x, hraw, s, trf, ctid, wbest); break;
+            default: consume<4, T, true>(p, sm, ph, l, kind, k, sc, x, hraw, s, trf, ctid, wbest); break;
+        }
+        return;
+    }
     switch (ph.K / 256) {
-        case 1: consume<1, T>(p, sm, ph, l, kind, k, sc, cw, lane, wbest); break;
-        case 2: consume<2, T>(p, sm, ph, l, kind, k, sc, cw, lane, wbest); break;
-        case 4: consume<4, T>(p, sm, ph, l, kind, k, sc, cw, lane, wbest); break;
-        case 8: consume<8, T>(p, sm, ph, l, kind, k, sc, cw, lane, wbest); break;
-        case 12: consume<12, T>(p, sm, ph, l, kind, k, sc, cw, lane, wbest); break;
-        default: consume<16, T>(p, sm, ph, l, kind, k, sc, cw, lane, wbest); break;
+        case 1: consume<1, T, false>(p, sm, ph, l, kind, k, sc, x, hraw, s, trf, ctid, wbest); break;
+        case 2: consume<2, T, false>(p, sm, ph, l, kind, k, sc, x, hraw, s, trf, ctid, wbest); break;
+        case 4: consume<4, T, false>(p, sm, ph, l, kind, k, sc, x, hraw, s, trf, ctid, wbest); break;
+        case 8: consume<8, T, false>(p, sm, ph, l, kind, k, sc, x, hraw, s, trf, ctid, wbest); break;
+        default: consume<12, T, false>(p, sm, ph, l, kind, k, sc, x, hraw, s, trf, ctid, wbest); break;
     }
 }
 
-// q/k RMSNorm + rotate-half RoPE of one head held as DL dims per lane (dims lane*DL + j).
+// ------------------------------------------------------------------ attention
+template <int DL>
+struct KVRaw;
+template <>
+struct KVRaw<4> {
+    using type = uint2;
+};
+template <>
+struct KVRaw<2> {
+    using type = uint32_t;
+};
+
+__device__ __forceinline__ void unpack_kv(const uint2& r, float (&f)[4]) {
+    const float2 a = h2_to_f2(r.x), b = h2_to_f2(r.y);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+}
+__device__ __forceinline__ void unpack_kv(const uint32_t& r, float (&f)[2]) {
+    const float2 a = h2_to_f2(r);
+    f[0] = a.x; f[1] = a.y;
+}
+
+// Attention units of layer l on this CTA: unit u = (kv head j, split s), u < hkv * S.
+// Scratch: the x buffer `scr` (free between the qkv and o phases).
 template <int D>
-__device__ __forceinline__ void norm_rope(float (&v)[D / 32], const float* nw, const float2* cs_row, float eps, int lane) {
+__device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, const MKLayer& ly, int l, const StepCtx& sc,
+                                             float* scr, int ctid) {
     constexpr int DL = D / 32, HALF = D / 2;
-    float ss = 0.0f;
-#pragma unroll
-    for (int j = 0; j < DL; ++j) ss += v[j] * v[j];
-    ss = warp_sum(ss);
-    const float s = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-#pragma unroll
-    for (int j = 0; j < DL; ++j) v[j] = v[j] * s * nw[lane * DL + j];
-    const bool first = lane < 16;
-    float o[DL];
-#pragma unroll
-    for (int j = 0; j < DL; ++j) {
-        const float partner = __shfl_xor_sync(0xffffffffu, v[j], 16);
-        const float2 c = cs_row[(lane * DL + j) % HALF];
-        o[j] = first ? (v[j] * c.x - partner * c.y) : (partner * c.y + v[j] * c.x);
-    }
-#pragma unroll
-    for (int j = 0; j < DL; ++j) v[j] = o[j];
-}
-
-// Attention units of layer l for this CTA: unit u = (kv head j, split s), u < hkv * S.
-template <int D>
-__device__ void attention_phase(const MKParams& p, Smem& sm, int l, const StepCtx& sc, int cw, int lane, int ctid) {
-    constexpr int DL = D / 32;
+    using Raw = typename KVRaw<DL>::type;
+    const int cw = ctid >> 5, lane = ctid & 31;
     const int S = p.att_splits, G = p.hq / p.hkv, units = p.hkv * S;
     const int GRID = gridDim.x;
-    bool waited = false;
     __half* kp = p.kpool + l * p.kv_layer_stride;
     __half* vp = p.vpool + l * p.kv_layer_stride;
     const float scale = 1.0f / sqrtf(static_cast<float>(D));
     const int pos = sc.pos, nvis = pos + 1;
     const int chunk = ((nvis + S - 1) / S + 15) / 16 * 16;
-    float* qs = sm.x;                       // [MAXG][D] normalised + rotated queries
-    float* ks = sm.x + MAXG * D;            // [D] new key (fp16-rounded)
-    float* vs = sm.x + (MAXG + 1) * D;      // [D] new value (fp16-rounded)
-    float* merge = sm.x + (MAXG + 2) * D;   // [NC][G][D + 2]
+    float* qs = scr;                      // [MAXG][D] normalised + rotated queries
+    float* ks = scr + MAXG * D;           // [D] new key (fp16-rounded)
+    float* vs = scr + (MAXG + 1) * D;     // [D] new value (fp16-rounded)
+    float* merge = scr + (MAXG + 2) * D;  // [NC][G][D + 2]
     for (int u = 0; u < units; ++u) {
         if (static_cast<int>(static_cast<long long>(u) * GRID / units) != static_cast<int>(blockIdx.x)) continue;
-        if (!waited) {
-            cwait(&p.bars[bar_phase(l, 0)], static_cast<unsigned>(GRID * (sc.t + 1)), p.err, ctid);
-            waited = true;
-        }
         const int j = u / S, s = u % S;
         const int kb = s * chunk, ke = min(nvis, kb + chunk);
         const bool owns_new = pos >= kb && pos < ke;
-        const float2* cs_row = p.rope_cs + static_cast<size_t>(pos) * (D / 2);
-        const int page = p.page_table[pos / p.page_tokens];
-        const size_t new_off = ((static_cast<size_t>(page) * p.hkv + j) * p.page_tokens + pos % p.page_tokens) * D;
-        // warps 0..G-1: queries of the group; warp G: the new key / value
-        if (cw < G) {
-            float v[DL];
-            const float* src = p.qkv + (static_cast<size_t>(j) * G + cw) * D + lane * DL;
+        // -- loads that do not depend on this step's q/k/v: RoPE row, norm weights, cached keys
+        float2 cs[DL];
+        float nw[DL];
 #pragma unroll
-            for (int q = 0; q < DL; ++q) v[q] = __ldcg(src + q);
-            norm_rope<D>(v, p.layers[l].q_norm, cs_row, p.eps, lane);
+        for (int q = 0; q < DL; ++q) {
+            cs[q] = p.rope_cs[static_cast<size_t>(pos) * HALF + (lane * DL + q) % HALF];
+            nw[q] = (cw < G ? ly.q_norm : ly.k_norm)[lane * DL + q];
+        }
+        Raw kraw[KPF], vraw[KPF];
+        const int key0 = kb + cw;
 #pragma unroll
-            for (int q = 0; q < DL; ++q) qs[cw * D + lane * DL + q] = v[q];
-        } else if (cw == G && owns_new) {
-            float v[DL], w[DL];
-            const float* ksrc = p.qkv + static_cast<size_t>(p.hq) * D + static_cast<size_t>(j) * D + lane * DL;
-            const float* vsrc = p.qkv + static_cast<size_t>(p.hq + p.hkv) * D + static_cast<size_t>(j) * D + lane * DL;
-#pragma unroll
-            for (int q = 0; q < DL; ++q) {
-                v[q] = __ldcg(ksrc + q);
-                w[q] = __ldcg(vsrc + q);
+        for (int i = 0; i < KPF; ++i) {
+            const int key = key0 + NC * i;
+            if (key < ke && key != pos) {
+                const int pg = __ldg(p.page_table + key / p.page_tokens);
+                const size_t off =
+                    ((static_cast<size_t>(pg) * p.hkv + j) * p.page_tokens + key % p.page_tokens) * D + lane * DL;
+                kraw[i] = __ldcg(reinterpret_cast<const Raw*>(kp + off));
+                vraw[i] = __ldcg(reinterpret_cast<const Raw*>(vp + off));
             }
-            norm_rope<D>(v, p.layers[l].k_norm, cs_row, p.eps, lane);
+        }
+        // -- wait for this layer's q/k/v rows (every CTA's qkv part)
+        wait_ctr(ctr(p, l, E_QKV), static_cast<unsigned>(GRID * (sc.t + 1)), p.err, ctid);
+        MK_TR(l, 5);
+        if (cw < G || (cw == G && owns_new)) {
+            const int hrow = cw < G ? (j * G + cw) * D : (p.hq + j) * D;
+            float v[DL], vv[DL];
+#pragma unroll
+            for (int q = 0; q < DL; ++q) v[q] = __ldcg(p.qkv + hrow + lane * DL + q);
+            if (cw == G) {
+                const int vrow = (p.hq + p.hkv + j) * D;
+#pragma unroll
+                for (int q = 0; q < DL; ++q) vv[q] = __ldcg(p.qkv + vrow + lane * DL + q);
+            }
+            // per-head RMSNorm + rotate-half RoPE (dims lane*DL + q; partner in lane ^ 16)
+            float ssq = 0.0f;
+#pragma unroll
+            for (int q = 0; q < DL; ++q) ssq += v[q] * v[q];
+            ssq = warp_sum(ssq);
+            const float rs = 1.0f / sqrtf(ssq / static_cast<float>(D) + p.eps);
+#pragma unroll
+            for (int q = 0; q < DL; ++q) v[q] = v[q] * rs * nw[q];
+            const bool first = lane < 16;
+            float o[DL];
 #pragma unroll
             for (int q = 0; q < DL; ++q) {
-                const __half kh = __float2half_rn(v[q]), vh = __float2half_rn(w[q]);
-                kp[new_off + lane * DL + q] = kh;
-                vp[new_off + lane * DL + q] = vh;
-                ks[lane * DL + q] = __half2float(kh);
-                vs[lane * DL + q] = __half2float(vh);
+                const float partner = __shfl_xor_sync(0xffffffffu, v[q], 16);
+                o[q] = first ? (v[q] * cs[q].x - partner * cs[q].y) : (partner * cs[q].y + v[q] * cs[q].x);
+            }
+            if (cw < G) {
+#pragma unroll
+                for (int q = 0; q < DL; ++q) qs[cw * D + lane * DL + q] = o[q];
+            } else {
+                const int page = __ldg(p.page_table + pos / p.page_tokens);
+                const size_t off =
+                    ((static_cast<size_t>(page) * p.hkv + j) * p.page_tokens + pos % p.page_tokens) * D + lane * DL;
+#pragma unroll
+                for (int q = 0; q < DL; ++q) {
+                    const __half kh = __float2half_rn(o[q]), vh = __float2half_rn(vv[q]);
+                    kp[off + q] = kh;
+                    vp[off + q] = vh;
+                    ks[lane * DL + q] = __half2float(kh);
+                    vs[lane * DL + q] = __half2float(vh);
+                }
             }
         }
         nbar();
@@ -471,41 +682,53 @@ __device__ void attention_phase(const MKParams& p, Smem& sm, int l, const StepCt
                 qr[g][q] = g < G ? qs[g * D + lane * DL + q] : 0.0f;
             }
         }
-        for (int key = kb + cw; key < ke; key += NC) {
-            float kf[DL], vf[DL];
-            if (key == pos) {
+        for (int base = key0; base < ke; base += NC * KPF) {
+            if (base != key0) {
 #pragma unroll
-                for (int q = 0; q < DL; ++q) {
-                    kf[q] = ks[lane * DL + q];
-                    vf[q] = vs[lane * DL + q];
-                }
-            } else {
-                const int pg = p.page_table[key / p.page_tokens];
-                const size_t off = ((static_cast<size_t>(pg) * p.hkv + j) * p.page_tokens + key % p.page_tokens) * D +
-                                   lane * DL;
-#pragma unroll
-                for (int q = 0; q < DL; ++q) {
-                    kf[q] = __half2float(kp[off + q]);
-                    vf[q] = __half2float(vp[off + q]);
+                for (int i = 0; i < KPF; ++i) {
+                    const int key = base + NC * i;
+                    if (key < ke && key != pos) {
+                        const int pg = __ldg(p.page_table + key / p.page_tokens);
+                        const size_t off =
+                            ((static_cast<size_t>(pg) * p.hkv + j) * p.page_tokens + key % p.page_tokens) * D +
+                            lane * DL;
+                        kraw[i] = __ldcg(reinterpret_cast<const Raw*>(kp + off));
+                        vraw[i] = __ldcg(reinterpret_cast<const Raw*>(vp + off));
+                    }
                 }
             }
 #pragma unroll
-            for (int g = 0; g < MAXG; ++g) {
-                if (g >= G) break;
-                float sc_ = 0.0f;
+            for (int i = 0; i < KPF; ++i) {
+                const int key = base + NC * i;
+                if (key >= ke) break;
+                float kf[DL], vf[DL];
+                if (key == pos) {
 #pragma unroll
-                for (int q = 0; q < DL; ++q) sc_ += qr[g][q] * kf[q];
-                sc_ = warp_sum(sc_) * scale;
-                const float mn = fmaxf(m[g], sc_);
-                const float corr = expf(m[g] - mn);
-                const float pe = expf(sc_ - mn);
-                lsum[g] = lsum[g] * corr + pe;
+                    for (int q = 0; q < DL; ++q) {
+                        kf[q] = ks[lane * DL + q];
+                        vf[q] = vs[lane * DL + q];
+                    }
+                } else {
+                    unpack_kv(kraw[i], kf);
+                    unpack_kv(vraw[i], vf);
+                }
 #pragma unroll
-                for (int q = 0; q < DL; ++q) o[g][q] = o[g][q] * corr + pe * vf[q];
-                m[g] = mn;
+                for (int g = 0; g < MAXG; ++g) {
+                    if (g >= G) break;
+                    float d = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < DL; ++q) d += qr[g][q] * kf[q];
+                    d = warp_sum(d) * scale;
+                    const float mn = fmaxf(m[g], d);
+                    const float corr = expf(m[g] - mn);
+                    const float pe = expf(d - mn);
+                    lsum[g] = lsum[g] * corr + pe;
+#pragma unroll
+                    for (int q = 0; q < DL; ++q) o[g][q] = o[g][q] * corr + pe * vf[q];
+                    m[g] = mn;
+                }
             }
         }
-        // merge the warps
         for (int g = 0; g < G; ++g) {
             float* mr = merge + (cw * G + g) * (D + 2);
 #pragma unroll
@@ -517,7 +740,7 @@ __device__ void attention_phase(const MKParams& p, Smem& sm, int l, const StepCt
         }
         nbar();
         float* part = p.att_part + (static_cast<size_t>(j) * S + s) * G * (D + 2);
-        for (int idx = ctid; idx < G * D; idx += NC * 32) {
+        for (int idx = ctid; idx < G * D; idx += CT) {
             const int g = idx / D, d = idx % D;
             float M = -INFINITY;
             for (int w = 0; w < NC; ++w) M = fmaxf(M, merge[(w * G + g) * (D + 2) + D]);
@@ -540,22 +763,23 @@ __device__ void attention_phase(const MKParams& p, Smem& sm, int l, const StepCt
                 }
             }
         }
-        nbar();
         if (S == 1) {
-            if (ctid == 0) release_add(&p.bars[bar_phase(l, 1)]);
+            signal(ctr(p, l, E_ATT), ctid);
+            MK_TR(l, 6);
             continue;
         }
-        // split-K: the last CTA to finish a kv head combines its splits.
+        // split-K: the last CTA to finish kv head j combines its splits.
+        nbar();
         if (ctid == 0) {
             __threadfence();
-            const unsigned old = atomicAdd(&p.bars[bar_split(p, l, j)], 1u);
+            const unsigned old = atomicAdd(split_ctr(p, l, j), 1u);
             sm.flag = (old + 1 == static_cast<unsigned>(S * (sc.t + 1))) ? 1 : 0;
             __threadfence();
         }
         nbar();
         if (sm.flag) {
             const float* hp = p.att_part + static_cast<size_t>(j) * S * G * (D + 2);
-            for (int idx = ctid; idx < G * D; idx += NC * 32) {
+            for (int idx = ctid; idx < G * D; idx += CT) {
                 const int g = idx / D, d = idx % D;
                 float M = -INFINITY;
                 for (int q = 0; q < S; ++q) M = fmaxf(M, __ldcg(hp + (q * G + g) * (D + 2) + D));
@@ -571,83 +795,120 @@ __device__ void attention_phase(const MKParams& p, Smem& sm, int l, const StepCt
                 }
                 p.attn[(static_cast<size_t>(j) * G + g) * D + d] = L > 0.0f ? acc / L : 0.0f;
             }
-            nbar();
-            if (ctid == 0) release_add(&p.bars[bar_phase(l, 1)]);
+            signal(ctr(p, l, E_ATT), ctid);
+            MK_TR(l, 6);
         }
+        nbar();
     }
 }
 
 template <typename T>
 __device__ void consumers(const MKParams& p, Smem& sm, int cw, int lane) {
     const int ctid = cw * 32 + lane;
-    const unsigned GRID = gridDim.x;
+    const int GRID = gridDim.x;
+    const int me = blockIdx.x;
     long long k = 0;
     for (int t = 0; t < p.steps; ++t) {
         StepCtx sc;
         sc.t = t;
         sc.pos = p.start + t;
+        const unsigned full = static_cast<unsigned>(GRID * (t + 1));
         if (t == 0) {
             sc.tok = __ldcg(p.ids);
         } else {
-            cwait(&p.bars[bar_lm(p)], GRID * t, p.err, ctid);
-            const unsigned long long b = *reinterpret_cast<volatile unsigned long long*>(&p.best[t - 1]);
+            wait_ctr(ctr_lm(p), static_cast<unsigned>(GRID * t), p.err, ctid);
+            // every CTA reduces the per-CTA argmax keys of the previous step
+            unsigned long long b = 0ull;
+            for (int c = lane; c < GRID; c += 32) {
+                const unsigned long long kk = __ldcg(p.best + static_cast<size_t>(t - 1) * GRID + c);
+                b = kk > b ? kk : b;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+                b = other > b ? other : b;
+            }
             sc.tok = b == 0ull ? 0 : argmax_key_index(b);
-            if (blockIdx.x == 0 && ctid == 0) p.ids[t] = sc.tok;
+            if (me == 0 && ctid == 0) p.ids[t] = sc.tok;
         }
         unsigned long long wbest = 0ull;
         for (int l = 0; l < p.L; ++l) {
-            const MKLayer& ly = p.layers[l];
-            // qkv
-            if (l > 0) cwait(&p.bars[bar_phase(l - 1, 4)], GRID * (t + 1), p.err, ctid);
-            if (l == 0)
-                stage<T>(sm, nullptr, p.embed, static_cast<size_t>(sc.tok) * p.H, p.H, ly.in_norm, p.eps, ctid);
-            else
-                stage<T>(sm, p.h, nullptr, 0, p.H, ly.in_norm, p.eps, ctid);
-            consume_k<T>(p, sm, phase_of(p, l, K_QKV), l, K_QKV, k, sc, cw, lane, wbest);
-            nbar();
-            if (ctid == 0) release_add(&p.bars[bar_phase(l, 0)]);
-            // attention (its own wait on the qkv phase)
+            const MKLayer ly = p.layers[l];
+            MK_TR(l, 0);
+            // ---- qkv: stage h (or the embedding row) into x[0] / hraw[0]
+            if (l == 0) {
+                stage<T>(nullptr, p.embed, static_cast<size_t>(sc.tok) * p.H, p.H, ly.in_norm, sm.x[0], sm.hraw[0],
+                         sm.red[0], ctid);
+            } else {
+                wait_ctr(ctr(p, l - 1, E_HD), full, p.err, ctid);
+                MK_TR(l, 1);
+                stage<T>(p.h, nullptr, 0, p.H, ly.in_norm, sm.x[0], sm.hraw[0], sm.red[0], ctid);
+            }
+            MK_TR(l, 2);
+            const float s_in = norm_scale(sm.red[0], p.H, p.eps);
+            consume_k<T>(p, sm, phase_of(p, ly, K_QKV), l, K_QKV, k, sc, sm.x[0], sm.hraw[0], s_in, 3, ctid, wbest);
+            signal(ctr(p, l, E_QKV), ctid);
+            MK_TR(l, 4);
+            // ---- attention (scratch: x[1])
             if (p.D == 128)
-                attention_phase<128>(p, sm, l, sc, cw, lane, ctid);
+                attention_phase<128>(p, sm, ly, l, sc, sm.x[1], ctid);
             else
-                attention_phase<64>(p, sm, l, sc, cw, lane, ctid);
-            // o_proj + residual
-            cwait(&p.bars[bar_phase(l, 1)], static_cast<unsigned>(p.hkv * (t + 1)), p.err, ctid);
-            stage<T>(sm, p.attn, nullptr, 0, p.hq * p.D, nullptr, p.eps, ctid);
-            consume_k<T>(p, sm, phase_of(p, l, K_O), l, K_O, k, sc, cw, lane, wbest);
-            nbar();
-            if (ctid == 0) release_add(&p.bars[bar_phase(l, 2)]);
-            // gate/up + SwiGLU
-            cwait(&p.bars[bar_phase(l, 2)], GRID * (t + 1), p.err, ctid);
-            stage<T>(sm, p.h, nullptr, 0, p.H, ly.post_norm, p.eps, ctid);
-            consume_k<T>(p, sm, phase_of(p, l, K_GU), l, K_GU, k, sc, cw, lane, wbest);
-            nbar();
-            if (ctid == 0) release_add(&p.bars[bar_phase(l, 3)]);
-            // down + residual
-            cwait(&p.bars[bar_phase(l, 3)], GRID * (t + 1), p.err, ctid);
-            stage<T>(sm, p.act, nullptr, 0, p.I, nullptr, p.eps, ctid);
-            consume_k<T>(p, sm, phase_of(p, l, K_D), l, K_D, k, sc, cw, lane, wbest);
-            nbar();
-            if (ctid == 0) release_add(&p.bars[bar_phase(l, 4)]);
+                attention_phase<64>(p, sm, ly, l, sc, sm.x[1], ctid);
+            // ---- o_proj + residual: stage attn into x[1]; h = hraw[0] + W_o attn
+            wait_ctr(ctr(p, l, E_ATT), static_cast<unsigned>(p.hkv * (t + 1)), p.err, ctid);
+            MK_TR(l, 7);
+            stage<T>(p.attn, nullptr, 0, p.hq * p.D, nullptr, sm.x[1], nullptr, nullptr, ctid);
+            consume_k<T>(p, sm, phase_of(p, ly, K_O), l, K_O, k, sc, sm.x[1], sm.hraw[0], 1.0f, 8, ctid, wbest);
+            signal(ctr(p, l, E_HO), ctid);
+            MK_TR(l, 9);
+            // ---- gate/up + SwiGLU: stage h into x[0] / hraw[1]
+            wait_ctr(ctr(p, l, E_HO), full, p.err, ctid);
+            MK_TR(l, 10);
+            stage<T>(p.h, nullptr, 0, p.H, ly.post_norm, sm.x[0], sm.hraw[1], sm.red[1], ctid);
+            const float s_post = norm_scale(sm.red[1], p.H, p.eps);
+            consume_k<T>(p, sm, phase_of(p, ly, K_GU), l, K_GU, k, sc, sm.x[0], nullptr, s_post, 11, ctid, wbest);
+            signal(ctr(p, l, E_ACT), ctid);
+            MK_TR(l, 12);
+            // ---- down + residual: stage act into x[1]; h = hraw[1] + W_d act
+            wait_ctr(ctr(p, l, E_ACT), full, p.err, ctid);
+            MK_TR(l, 13);
+            stage<T>(p.act, nullptr, 0, p.I, nullptr, sm.x[1], nullptr, nullptr, ctid);
+            consume_k<T>(p, sm, phase_of(p, ly, K_D), l, K_D, k, sc, sm.x[1], sm.hraw[1], 1.0f, 14, ctid, wbest);
+            signal(ctr(p, l, E_HD), ctid);
+            MK_TR(l, 15);
         }
-        // final norm + lm_head + argmax
-        cwait(&p.bars[bar_phase(p.L - 1, 4)], GRID * (t + 1), p.err, ctid);
-        stage<T>(sm, p.h, nullptr, 0, p.H, p.final_norm, p.eps, ctid);
-        consume_k<T>(p, sm, phase_of(p, 0, K_LM), 0, K_LM, k, sc, cw, lane, wbest);
+        // ---- final norm + lm_head + argmax
+        wait_ctr(ctr(p, p.L - 1, E_HD), full, p.err, ctid);
+        MK_TR(p.L, 1);
+        stage<T>(p.h, nullptr, 0, p.H, p.final_norm, sm.x[0], sm.hraw[0], sm.red[0], ctid);
+        MK_TR(p.L, 2);
+        const float s_fin = norm_scale(sm.red[0], p.H, p.eps);
+        consume_k<T>(p, sm, phase_of(p, p.layers[0], K_LM), 0, K_LM, k, sc, sm.x[0], nullptr, s_fin, 3, ctid, wbest);
         if (lane == 0) sm.best[cw] = wbest;
         nbar();
         if (ctid == 0) {
             unsigned long long b = 0ull;
             for (int q = 0; q < NC; ++q) b = sm.best[q] > b ? sm.best[q] : b;
-            if (b != 0ull) atomicMax(&p.best[t], b);
-            release_add(&p.bars[bar_lm(p)]);
+            p.best[static_cast<size_t>(t) * GRID + me] = b;
+            red_release_add(ctr_lm(p));
         }
+        MK_TR(p.L, 4);
     }
-    if (blockIdx.x == 0) {
-        cwait(&p.bars[bar_lm(p)], GRID * p.steps, p.err, ctid);
-        if (ctid == 0) {
-            const unsigned long long b = *reinterpret_cast<volatile unsigned long long*>(&p.best[p.steps - 1]);
-            p.ids[p.steps] = b == 0ull ? 0 : argmax_key_index(b);
+    if (me == 0) {
+        const int t = p.steps - 1;
+        wait_ctr(ctr_lm(p), static_cast<unsigned>(GRID * p.steps), p.err, ctid);
+        if (cw == 0) {
+            unsigned long long b = 0ull;
+            for (int c = lane; c < GRID; c += 32) {
+                const unsigned long long kk = __ldcg(p.best + static_cast<size_t>(t) * GRID + c);
+                b = kk > b ? kk : b;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+                b = other > b ? other : b;
+            }
+            if (lane == 0) p.ids[p.steps] = b == 0ull ? 0 : argmax_key_index(b);
         }
     }
 }
@@ -675,21 +936,28 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_mk(MKParams p) {
 
 }  // namespace
 
-int mk_bar_count(int L, int hkv) { return L * 5 + 1 + L * hkv; }
+int mk_flag_count(int L, int hkv, int grid) { return L * 6 + 1 + L * hkv + 0 * grid; }
 
-bool mk_supported(int H, int I, int hq, int hkv, int D, int wfmt) {
-    auto ki_ok = [](int K) {
+size_t mk_vec_floats(int H, int I, int hq, int hkv, int D) {
+    return static_cast<size_t>(H) + static_cast<size_t>(hq + 2 * hkv) * D + static_cast<size_t>(hq) * D + I;
+}
+
+bool mk_supported(int H, int I, int hq, int hkv, int D, int wfmt, int grid) {
+    auto ki_ok = [](int K, bool pair) {
         const int ki = K / 256;
-        return K % 256 == 0 && (ki == 1 || ki == 2 || ki == 4 || ki == 8 || ki == 12 || ki == 16);
+        if (K % 256 != 0) return false;
+        return pair ? (ki == 1 || ki == 2 || ki == 4) : (ki == 1 || ki == 2 || ki == 4 || ki == 8 || ki == 12);
     };
     if (wfmt != WF_F16 && wfmt != WF_BF16) return false;
-    if (!ki_ok(H) || !ki_ok(I) || !ki_ok(hq * D)) return false;
+    if (!ki_ok(H, true) || !ki_ok(I, false) || !ki_ok(hq * D, false)) return false;
     if (D != 64 && D != 128) return false;
-    if (hq % hkv != 0 || hq / hkv > MAXG) return false;
-    if (hq * D > XBUF || I > XBUF || H > XBUF) return false;
-    if ((MAXG + 2) * D + NC * (hq / hkv) * (D + 2) > XBUF) return false;
+    if (hq % hkv != 0 || hq / hkv > MAXG || hq / hkv >= NC) return false;
+    if (H > HMAX || I > XMAX || hq * D > XMAX) return false;
+    if ((MAXG + 2) * D + NC * (hq / hkv) * (D + 2) > XMAX) return false;
     // one unit must fit a ring slot: (gate, up) pair rows and the widest single row
     if (2 * H * 2 > SLOT_BYTES || I * 2 > SLOT_BYTES || hq * D * 2 > SLOT_BYTES) return false;
+    // every CTA owns rows of every phase (the hand-offs rely on it); flags polled per lane
+    if (H < grid || I < grid || (hq + 2 * hkv) * D < grid || grid > 32 * MAXFL) return false;
     return true;
 }
 

@@ -36,21 +36,30 @@ struct MKParams {
     int start;
     int steps;
     float* logits;  // nullable: [steps, V]
-    // scratch (device)
-    float* h;         // [H] residual stream
-    float* qkv;       // [(hq + 2 hkv) D]
-    float* attn;      // [hq D]
-    float* act;       // [I]
-    float* att_part;  // [hkv][splits][G][D + 2]
-    unsigned int* bars;             // [mk_bar_count(L, hkv)], zeroed before launch
-    unsigned long long* best;       // [steps], zeroed before launch
+    // activation vectors shared between CTAs
+    float* h;                 // [H] residual stream
+    float* qkv;               // [(hq + 2 hkv) D]
+    float* attn;              // [hq D]
+    float* act;               // [I]
+    float* att_part;          // [hkv][splits][G][D + 2] split-K partials
+    unsigned int* flags;      // [mk_flag_count(L, hkv, grid)] phase flags, zeroed before launch
+    unsigned long long* best; // [steps][grid] per-CTA argmax keys
     int* err;
     int att_splits;
+    // optional phase trace of the first step (nullptr = off): %globaltimer stamps,
+    // [grid][mk_trace_stride(L)]; slots in decode_mk.cu
+    unsigned long long* trace;
 };
 
-int mk_bar_count(int L, int hkv);
-// Whether the persistent kernel supports this shape (else the graph path is used).
-bool mk_supported(int H, int I, int hq, int hkv, int D, int wfmt);
+constexpr int MK_TRACE_PER_LAYER = 16;
+constexpr int MK_TRACE_CHUNKS = 64;  // + per CTA: issue, consumer-arrival and ready stamps of the first 64 chunks
+__host__ __device__ inline size_t mk_trace_stride(int L) { return static_cast<size_t>(L + 1) * MK_TRACE_PER_LAYER + 3 * MK_TRACE_CHUNKS; }
+
+int mk_flag_count(int L, int hkv, int grid);
+// Floats of the four shared activation vectors (h, qkv, attn, act), in that order.
+size_t mk_vec_floats(int H, int I, int hq, int hkv, int D);
+// Whether the persistent kernel supports this shape on a grid of `grid` CTAs.
+bool mk_supported(int H, int I, int hq, int hkv, int D, int wfmt, int grid);
 int mk_grid(int device);
 void mk_launch(const MKParams& p, int grid, cudaStream_t st);
 

@@ -302,6 +302,8 @@ struct soc_model {
     float* mk_att_part = nullptr;
     size_t mk_att_part_floats = 0;
     int* mk_ids = nullptr;
+    float* mk_vec = nullptr;  // h | qkv | attn | act shared between the kernel's CTAs
+    size_t mk_vec_n = 0;
 
     void* dmalloc(size_t bytes) {
         void* p = nullptr;
@@ -494,7 +496,7 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
     ensure_workspace(m, 16);
     const int G = static_cast<int>(c.hq / c.hkv);
     const int hkv = static_cast<int>(c.hkv);
-    const int nb = mk_bar_count(static_cast<int>(c.layers), hkv);
+    const int nb = mk_flag_count(static_cast<int>(c.layers), hkv, m->mk_grid);
     if (nb > m->mk_bar_n) {
         m->dfree(m->mk_bars);
         m->mk_bars = static_cast<unsigned*>(m->dmalloc(sizeof(unsigned) * nb));
@@ -503,7 +505,8 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
     if (steps > m->mk_best_n) {
         m->dfree(m->mk_best);
         m->mk_best_n = std::max(steps, 64);
-        m->mk_best = static_cast<unsigned long long*>(m->dmalloc(sizeof(unsigned long long) * m->mk_best_n));
+        m->mk_best = static_cast<unsigned long long*>(
+            m->dmalloc(sizeof(unsigned long long) * m->mk_best_n * m->mk_grid));
     }
     // split-K over the key range: about 128 keys per CTA, at most one CTA per (kv head, split)
     const int max_ctx = start + steps;
@@ -516,7 +519,7 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
         m->mk_att_part_floats = part;
     }
     SOCB_CUDA(cudaMemsetAsync(m->mk_bars, 0, sizeof(unsigned) * nb, st));
-    SOCB_CUDA(cudaMemsetAsync(m->mk_best, 0, sizeof(unsigned long long) * steps, st));
+    SOCB_CUDA(cudaMemsetAsync(m->mk_best, 0, sizeof(unsigned long long) * steps * m->mk_grid, st));
     MKParams p{};
     p.L = static_cast<int>(c.layers);
     p.H = static_cast<int>(c.hidden);
@@ -543,17 +546,38 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
     p.start = start;
     p.steps = steps;
     p.logits = logits;
-    p.h = m->h;
-    p.qkv = m->qkv;
-    p.attn = m->att;
-    p.act = m->act;
+    p.h = m->mk_vec;
+    p.qkv = p.h + c.hidden;
+    p.attn = p.qkv + (c.hq + 2 * c.hkv) * c.hd;
+    p.act = p.attn + c.hq * c.hd;
     p.att_part = m->mk_att_part;
-    p.bars = m->mk_bars;
+    p.flags = m->mk_bars;
     p.best = m->mk_best;
     p.err = m->ctx->d_err;
     p.att_splits = S;
+    // Optional phase trace (SOC_B200_MK_TRACE=<file>): raw u64 %globaltimer stamps of the first step.
+    const char* trace_path = std::getenv("SOC_B200_MK_TRACE");
+    unsigned long long* trace = nullptr;
+    const size_t trace_n = static_cast<size_t>(m->mk_grid) * mk_trace_stride(static_cast<int>(c.layers));
+    if (trace_path && *trace_path) {
+        trace = static_cast<unsigned long long*>(m->dmalloc(trace_n * sizeof(unsigned long long)));
+        SOCB_CUDA(cudaMemsetAsync(trace, 0, trace_n * sizeof(unsigned long long), st));
+    }
+    p.trace = trace;
     mk_launch(p, m->mk_grid, st);
     count_launches(1);
+    if (trace) {
+        std::vector<unsigned long long> host(trace_n);
+        SOCB_CUDA(cudaMemcpyAsync(host.data(), trace, trace_n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, st));
+        SOCB_CUDA(cudaStreamSynchronize(st));
+        m->dfree(trace);
+        if (FILE* f = std::fopen(trace_path, "wb")) {
+            const int hdr[4] = {m->mk_grid, static_cast<int>(c.layers), MK_TRACE_PER_LAYER, steps};
+            std::fwrite(hdr, sizeof(int), 4, f);
+            std::fwrite(host.data(), sizeof(unsigned long long), trace_n, f);
+            std::fclose(f);
+        }
+    }
 }
 
 // `steps` decode steps of sequence `seq`, whose cache holds `start` tokens and whose
@@ -769,8 +793,9 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
         // caller asks for the graph path (SOC_B200_DECODE_PATH=graph).
         const char* path = std::getenv("SOC_B200_DECODE_PATH");
         const bool want_mk = !(path && std::string(path) == "graph");
+        const int grid = mk_grid(ctx->device);
         if (want_mk && mk_supported(static_cast<int>(H), static_cast<int>(I), static_cast<int>(c.hq),
-                                    static_cast<int>(c.hkv), static_cast<int>(D), fmt) &&
+                                    static_cast<int>(c.hkv), static_cast<int>(D), fmt, grid) &&
             m->efmt == fmt) {
             std::vector<MKLayer> ml(c.layers);
             for (size_t l = 0; l < c.layers; ++l) {
@@ -780,7 +805,10 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
             m->d_mk_layers = static_cast<MKLayer*>(m->dmalloc(sizeof(MKLayer) * c.layers));
             SOCB_CUDA(cudaMemcpy(m->d_mk_layers, ml.data(), sizeof(MKLayer) * c.layers, cudaMemcpyHostToDevice));
             m->mk_ids = static_cast<int*>(m->dmalloc(sizeof(int) * 2));
-            m->mk_grid = mk_grid(ctx->device);
+            m->mk_vec_n = mk_vec_floats(static_cast<int>(H), static_cast<int>(I), static_cast<int>(c.hq),
+                                        static_cast<int>(c.hkv), static_cast<int>(D));
+            m->mk_vec = static_cast<float*>(m->dmalloc(sizeof(float) * m->mk_vec_n));
+            m->mk_grid = grid;
             m->mk_ok = true;
         }
         SOCB_CUDA(cudaDeviceSynchronize());
@@ -1145,7 +1173,8 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         cudaStream_t st = m->ctx->stream;
         const int H = static_cast<int>(c.hidden), I = static_cast<int>(c.inter), hq = static_cast<int>(c.hq);
         const int hkv = static_cast<int>(c.hkv), D = static_cast<int>(c.hd), V = static_cast<int>(c.vocab);
-        if (!mk_supported(H, I, hq, hkv, D, m->wfmt) || m->efmt != m->wfmt)
+        const int grid = mk_grid(m->ctx->device);
+        if (!mk_supported(H, I, hq, hkv, D, m->wfmt, grid) || m->efmt != m->wfmt)
             throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: model shape not supported by the persistent decode kernel");
         kv->check_seq(seq);
         check_ids(m, &last_id, 1);
@@ -1154,11 +1183,10 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         if (pos + 1 > m->rope_len) throw Error(SOC_B200_ERR_CAPACITY, "decode position beyond the RoPE table");
         kv->reserve(seq, pos + 1, st);
 
-        const int grid = mk_grid(m->ctx->device);
         const int G = hq / hkv;
         int S = (pos + 1 + 127) / 128;
         S = std::max(1, std::min(S, grid / hkv));
-        const int nb = mk_bar_count(static_cast<int>(c.layers), hkv);
+        const int nb = mk_flag_count(static_cast<int>(c.layers), hkv, grid);
         // carve the array (256-byte aligned pieces)
         char* base = static_cast<char*>(noalloc_scratch(m->ctx->device));
         size_t off = 0;
@@ -1168,12 +1196,10 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
             return static_cast<void*>(q);
         };
         auto* bars = static_cast<unsigned*>(carve(sizeof(unsigned) * nb));
-        auto* best = static_cast<unsigned long long*>(carve(sizeof(unsigned long long)));
+        auto* best = static_cast<unsigned long long*>(carve(sizeof(unsigned long long) * grid));
         auto* ids = static_cast<int*>(carve(sizeof(int) * 2));
-        auto* h = static_cast<float*>(carve(sizeof(float) * H));
-        auto* qkv = static_cast<float*>(carve(sizeof(float) * (hq + 2 * hkv) * D));
-        auto* attn = static_cast<float*>(carve(sizeof(float) * hq * D));
-        auto* act = static_cast<float*>(carve(sizeof(float) * I));
+        const size_t nvec = mk_vec_floats(H, I, hq, hkv, D);
+        auto* vec = static_cast<float*>(carve(sizeof(float) * nvec));
         auto* part = static_cast<float*>(carve(sizeof(float) * static_cast<size_t>(hkv) * S * G * (D + 2)));
         auto* lg = static_cast<float*>(carve(sizeof(float) * V));
         if (off > kNoAllocScratchBytes)
@@ -1181,7 +1207,7 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
                                                    " bytes of scratch, above the static maximum of " +
                                                    std::to_string(kNoAllocScratchBytes));
         SOCB_CUDA(cudaMemsetAsync(bars, 0, sizeof(unsigned) * nb, st));
-        SOCB_CUDA(cudaMemsetAsync(best, 0, sizeof(unsigned long long), st));
+        SOCB_CUDA(cudaMemsetAsync(best, 0, sizeof(unsigned long long) * grid, st));
         SOCB_CUDA(cudaMemcpyAsync(ids, &last_id, sizeof(int), cudaMemcpyHostToDevice, st));
 
         MKParams p{};
@@ -1210,15 +1236,16 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         p.start = pos;
         p.steps = 1;
         p.logits = lg;
-        p.h = h;
-        p.qkv = qkv;
-        p.attn = attn;
-        p.act = act;
+        p.h = vec;
+        p.qkv = vec + H;
+        p.attn = p.qkv + (hq + 2 * hkv) * D;
+        p.act = p.attn + hq * D;
         p.att_part = part;
-        p.bars = bars;
+        p.flags = bars;
         p.best = best;
         p.err = m->ctx->d_err;
         p.att_splits = S;
+        p.trace = nullptr;
         if (p.layers == nullptr)
             throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: the model was loaded without the persistent decode kernel");
         mk_launch(p, grid, st);

@@ -337,6 +337,81 @@ def run_soc(args, rank, world, local):
         print(json.dumps(result), flush=True)
 
 
+# ------------------------------------------------------------- config 1 sweep
+SWEEP_SHAPES = {"q_proj": (2048, 1024), "k_proj": (1024, 1024), "o_proj": (1024, 2048), "gate_proj": (3072, 1024),
+                "down_proj": (1024, 3072), "lm_head": (151936, 1024)}
+SWEEP_FORMATS = ("fp16", "int8_g64", "int4_g32")
+SWEEP_BATCHES = (1, 4, 16, 64)
+
+
+def run_linear_sweep(args):
+    """Config 1: y = W x for every 0.6B linear shape x {fp16, int8 g64, int4 g32} x batch
+    {1, 4, 16, 64}, x ~ N(0, 1) seed 2, W ~ N(0, 0.02).  One JSON line per case: device time
+    of one soc_b200_linear launch (CUDA events over `steps` launches that rotate through
+    enough weight copies to exceed the 126 MB L2) and its algorithmic bytes / time."""
+    import torch
+    from soc_b200 import runtime as R
+    torch.cuda.set_device(0)
+    ctx = R.Context(0)
+    peaks = load_peaks()
+    fmt_code = {"fp16": R.WEIGHTS_F16, "int8_g64": R.WEIGHTS_INT8_G64, "int4_g32": R.WEIGHTS_INT4_G32}
+    g = torch.Generator(device="cuda").manual_seed(2)
+    stream = torch.cuda.ExternalStream(ctx.stream)  # the library's stream: events and launches on it
+    for name, (out_f, in_f) in SWEEP_SHAPES.items():
+        w32 = torch.randn(out_f, in_f, device="cuda", generator=g) * 0.02
+        for fmt in SWEEP_FORMATS:
+            if fmt == "fp16":
+                wq, sc = w32.half().view(torch.uint8), None
+            else:
+                grp, qmax = (64, 127.0) if fmt == "int8_g64" else (32, 7.0)
+                wg = w32.view(out_f, in_f // grp, grp)
+                sc = (wg.abs().amax(-1) / qmax).half()
+                q = torch.round(wg / sc.float().clamp_min(1e-30)[..., None]).clamp(-qmax, qmax).to(torch.int8)
+                q = q.view(out_f, in_f)
+                if fmt == "int4_g32":
+                    q = ((q[:, 0::2] & 0xF) | ((q[:, 1::2] & 0xF) << 4)).to(torch.uint8)
+                wq = q.view(torch.uint8).contiguous()
+            wbytes = wq.numel() + (sc.numel() * 2 if sc is not None else 0)
+            copies = max(1, min(256, -(-(256 << 20) // wbytes)))
+            ws = [wq.clone() for _ in range(copies)] if copies > 1 else [wq]
+            ss = [sc.clone() for _ in range(copies)] if (sc is not None and copies > 1) else [sc] * len(ws)
+            for batch in SWEEP_BATCHES:
+                x = torch.randn(batch, in_f, device="cuda", generator=g)
+                y = torch.empty(batch, out_f, device="cuda")
+
+                def launch(i):
+                    ctx.linear(fmt_code[fmt], ws[i % len(ws)].data_ptr(),
+                               ss[i % len(ss)].data_ptr() if ss[0] is not None else None,
+                               out_f, in_f, x.data_ptr(), batch, y.data_ptr(), stream.cuda_stream)
+
+                for i in range(max(args.warmup, 3)):
+                    launch(i)
+                reps = max(args.steps, len(ws))
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ctx.synchronize()
+                with torch.cuda.stream(stream):
+                    # keep the GPU busy while the host queues the launches, so the events
+                    # time the kernels and not the host's launch rate
+                    torch.cuda._sleep(4_000_000)
+                    e0.record(stream)
+                    for i in range(reps):
+                        launch(i)
+                    e1.record(stream)
+                ctx.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / reps
+                alg = wbytes + 4 * batch * (in_f + out_f)
+                gbs = alg / (us * 1e-6) / 1e9
+                print(json.dumps({"workload": "config1-linear", "shape": name, "out": out_f, "in": in_f, "format": fmt,
+                                  "batch": batch, "us": round(us, 3), "algorithmic_bytes": alg,
+                                  "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                                  "gflops": round(2 * out_f * in_f * batch / (us * 1e-6) / 1e9, 1),
+                                  "l2_rotation_copies": len(ws)}), flush=True)
+            del ws, ss
+        del w32
+        torch.cuda.empty_cache()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -344,8 +419,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="soc", choices=["soc", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config0", choices=["config0", "linear-sweep"],
+                    help="config0 (the headline line) or linear-sweep (config 1, one line per case)")
     args = ap.parse_args()
     rank, world, local = dist_env()
+    if args.workload == "linear-sweep":
+        run_linear_sweep(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:

@@ -341,6 +341,51 @@ def write_synthetic_bundle(
     return path
 
 
+def quantize_bundle(src_manifest: str | os.PathLike, out_dir: str | os.PathLike, quant: str) -> Path:
+    """Export an existing float bundle with its block linears group-quantised.
+
+    The exporter option of the quantised layout: every ``*_proj.weight`` record is
+    decoded to float32 (``float16``/``bfloat16``/``float32``), quantised with
+    ``quantize_groupwise`` and written as a ``quant`` record plus its ``.scales``
+    record; every other record and the tokenizer asset are copied unchanged.
+    Returns the new manifest path.
+    """
+    if quant not in QUANT_GROUP:
+        raise ValueError(f"unknown quantisation {quant}")
+    src = read_manifest(src_manifest)
+    out = Path(out_dir)
+    (out / "weights").mkdir(parents=True, exist_ok=True)
+    (out / "tokenizer").mkdir(parents=True, exist_ok=True)
+    used: set[str] = set()
+    records = []
+
+    def emit(name: str, data: np.ndarray, dt: str, shape: list[int]) -> None:
+        rel = f"weights/{sanitize_tensor_name(name, used)}.bin"
+        data = np.ascontiguousarray(data)
+        data.tofile(out / rel)
+        records.append({"name": name, "file": rel, "dtype": dt, "shape": shape, "byte_size": int(data.nbytes),
+                        "source_shard": "quantized.safetensors"})
+
+    for rec in src["tensors"]:
+        name = rec["name"]
+        arr = load_tensor(src, name)
+        if is_quantizable(name) and rec["dtype"] in ("float16", "bfloat16", "float32"):
+            w = bf16_bits_to_f32(arr) if rec["dtype"] == "bfloat16" else np.asarray(arr, dtype=np.float32)
+            q, s = quantize_groupwise(w, quant)
+            emit(name, q, quant, list(rec["shape"]))
+            emit(name + ".scales", s, "float16", list(s.shape))
+        else:
+            emit(name, np.asarray(arr), rec["dtype"], list(rec["shape"]))
+    tok_src = Path(src["_dir"]) / src["tokenizer_runtime_file"]
+    (out / "tokenizer" / "tokenizer_runtime.json").write_bytes(tok_src.read_bytes())
+    manifest = {k: v for k, v in src.items() if not k.startswith("_")}
+    manifest.update({"export_dtype": quant, "tensor_count": len(records), "tensors": records,
+                     "tokenizer_runtime_file": "tokenizer/tokenizer_runtime.json"})
+    path = out / "manifest.json"
+    path.write_text(json.dumps(manifest, indent=1))
+    return path
+
+
 def read_manifest(path: str | os.PathLike) -> dict[str, Any]:
     """Parse ``manifest.json`` and resolve tensor files against its directory."""
     p = Path(path)

@@ -85,6 +85,64 @@ struct WTraits<__nv_bfloat16> {
     static __device__ __forceinline__ float2 pair(uint32_t u) { return bf2_to_f2(u); }
 };
 
+// ------------------------------------------------ 16-byte weight vectors per format
+// A lane streams one 16-byte vector at a time: 8 fp16/bf16 elements, 16 int8 elements
+// (one fp16 scale per 64) or 32 int4 elements (one fp16 scale per 32; two per byte, low
+// nibble first, two's complement).  `part(u, p, w)` decodes elements [8p, 8p + 8) to exact
+// fp32 values; the group scale is applied to the 8..32-element partial sum afterwards.
+// Integer decode: the biased byte is placed in the mantissa of 2^23 with PRMT and the bias
+// is subtracted (exact for every value).
+__device__ __forceinline__ float biased_byte_f(uint32_t biased, int i, float bias) {
+    return __int_as_float(static_cast<int>(__byte_perm(biased, 0x4B000000u, 0x7540u | static_cast<uint32_t>(i)))) - bias;
+}
+__device__ __forceinline__ uint32_t u4_word(const uint4& u, int i) {
+    return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w;
+}
+
+template <int F>
+struct Codec;
+template <>
+struct Codec<WF_F16> {
+    static constexpr int EPV = 8, GROUP = 0;
+    static __device__ __forceinline__ void part(const uint4& u, int, float (&w)[8]) {
+        const float2 a = h2_to_f2(u.x), b = h2_to_f2(u.y), c = h2_to_f2(u.z), d = h2_to_f2(u.w);
+        w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y; w[4] = c.x; w[5] = c.y; w[6] = d.x; w[7] = d.y;
+    }
+};
+template <>
+struct Codec<WF_BF16> {
+    static constexpr int EPV = 8, GROUP = 0;
+    static __device__ __forceinline__ void part(const uint4& u, int, float (&w)[8]) {
+        const float2 a = bf2_to_f2(u.x), b = bf2_to_f2(u.y), c = bf2_to_f2(u.z), d = bf2_to_f2(u.w);
+        w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y; w[4] = c.x; w[5] = c.y; w[6] = d.x; w[7] = d.y;
+    }
+};
+template <>
+struct Codec<WF_I8G64> {
+    static constexpr int EPV = 16, GROUP = 64;
+    static __device__ __forceinline__ void part(const uint4& u, int p, float (&w)[8]) {
+        const uint32_t lo = u4_word(u, 2 * p) ^ 0x80808080u, hi = u4_word(u, 2 * p + 1) ^ 0x80808080u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w[i] = biased_byte_f(lo, i, 8388736.0f);  // 2^23 + 128
+            w[4 + i] = biased_byte_f(hi, i, 8388736.0f);
+        }
+    }
+};
+template <>
+struct Codec<WF_I4G32> {
+    static constexpr int EPV = 32, GROUP = 32;
+    static __device__ __forceinline__ void part(const uint4& u, int p, float (&w)[8]) {
+        const uint32_t v = u4_word(u, p);
+        const uint32_t ev = (v & 0x0F0F0F0Fu) ^ 0x08080808u, od = ((v >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w[2 * i] = biased_byte_f(ev, i, 8388616.0f);  // 2^23 + 8
+            w[2 * i + 1] = biased_byte_f(od, i, 8388616.0f);
+        }
+    }
+};
+
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 // Orderable key for (value, index) argmax with the lowest index winning ties.

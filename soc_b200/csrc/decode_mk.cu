@@ -118,15 +118,6 @@ __device__ __forceinline__ bool aborted(const int* err) {
     return (*reinterpret_cast<const volatile int*>(err) & DERR_WAIT_TIMEOUT) != 0;
 }
 
-__device__ __forceinline__ unsigned ld_flag(const unsigned* f) {
-    unsigned v;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_flag_release(unsigned* f, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
-}
-
 // Bounded wait on an mbarrier phase (non-blocking test + short sleep per try).
 __device__ __forceinline__ bool mbar_wait(unsigned long long* b, unsigned parity, int* err) {
     for (unsigned i = 0;; ++i) {
@@ -180,21 +171,6 @@ __device__ __forceinline__ void wait_ctr(const unsigned* c, unsigned target, int
 __device__ __forceinline__ void signal(unsigned* c, int ctid) {
     nbar();
     if (ctid == 0) red_release_add(c);
-}
-
-// Bounded acquire-wait until *c >= target (split-K counters).
-__device__ __forceinline__ bool wait_count(const unsigned* c, unsigned target, int* err) {
-    for (unsigned i = 0;; ++i) {
-        unsigned v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
-        if (v >= target) return true;
-        if (aborted(err)) return false;
-        if (i > SPIN_LIMIT) {
-            atomicOr(err, DERR_WAIT_TIMEOUT);
-            return false;
-        }
-        if (i > 8) __nanosleep(32);
-    }
 }
 
 // Trace slot `e` of layer `l` (first step only, consumer thread 0).  Slots per layer:

@@ -1,0 +1,401 @@
+// Persistent tcgen05 GEMM for sm_100a: y = epilogue(A W^T), A [M, K] activations and
+// W [N, K] weights (fp16 or bf16, K-major), fp32 accumulation in tensor memory.
+//
+// Restates Linear::Forward (Mac/cpu/src/linear.cpp:51-84) for many rows at once; the
+// SwiGLU epilogue is ApplySiLU * up (qwen_mlp.cpp:20-54), the residual epilogue the
+// AddTensors of the block (qwen_block.cpp:19-34).
+//
+// One CTA per SM walks the 128 x 256 output tiles (m fastest, so concurrently running CTAs
+// share the weight tile in L2).  Warp 0 lane 0 streams 64-column slices of A and W with
+// 2-D TMA (128-byte swizzle) into a 4-stage shared-memory ring; warp 1 owns 512 TMEM
+// columns (two 256-column accumulators) and lane 0 issues tcgen05.mma (M128 N256 K16, four
+// per slice), releasing each ring slot with tcgen05.commit; warps 2-5 drain the other
+// accumulator with tcgen05.ld while the next tile accumulates.  Every mbarrier wait is
+// bounded: on expiry the kernel records DERR_WAIT_TIMEOUT, stops issuing, frees TMEM and
+// returns.  No load uses cluster multicast.
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <mutex>
+
+#include "gemm_tc.h"
+#include "kernels.h"
+
+namespace socb {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2, W_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + W_BYTES;
+constexpr int TC_THREADS = 192;
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s
+constexpr size_t TC_SMEM = STAGES * STAGE_BYTES + 1024 /* barriers */ + 1024 /* alignment */;
+
+struct TcBars {
+    unsigned long long full[STAGES], empty[STAGES], acc_full[2], acc_empty[2];
+    uint32_t tmem;
+};
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(unsigned long long* b, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(unsigned long long* b, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait for the phase with `parity` (WAIT_NS of wall time); false once this or
+// another thread of the grid gave up.
+__device__ __forceinline__ bool mbar_wait(unsigned long long* b, unsigned parity, int* err) {
+    unsigned long long t0 = 0;
+    for (unsigned i = 0;; ++i) {
+        if (mbar_try(b, parity)) return true;
+        if ((i & 255u) == 255u) {
+            if (*reinterpret_cast<volatile int*>(err) & DERR_WAIT_TIMEOUT) return false;
+            const unsigned long long now = gtimer();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > WAIT_NS) {
+                atomicOr(err, DERR_WAIT_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* b, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, unsigned long long* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            su32(dst)),
+        "l"(map), "r"(su32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with 128-byte swizzle:
+// rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset), version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
+}
+// Instruction descriptor: fp32 accumulator, A/B type (0 fp16, 1 bf16), both K-major, N, M.
+__host__ __device__ constexpr uint32_t f16_idesc(uint32_t ab, int m, int n) {
+    return (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(unsigned long long* b) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
+                 : "memory");
+}
+// 32 lanes x 32 consecutive fp32 columns of tensor memory (one row per thread).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ T to_w(float f);
+template <>
+__device__ __forceinline__ __half to_w<__half>(float f) { return __float2half_rn(f); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_w<__nv_bfloat16>(float f) { return __float2bfloat16_rn(f); }
+
+template <typename T>
+__device__ __forceinline__ void epilogue(const float (&v)[32], int row, int col, int M, int N, void* y, int ldy,
+                                         int mode, int out_half) {
+    if (row >= M) return;
+    if (mode == LIN_SWIGLU) {
+        const int o = col >> 1, no = N >> 1;
+        if (out_half) {
+            T* yr = static_cast<T*>(y) + static_cast<size_t>(row) * ldy;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (o + j < no) yr[o + j] = to_w<T>(silu_f(v[2 * j]) * v[2 * j + 1]);
+        } else {
+            float* yr = static_cast<float*>(y) + static_cast<size_t>(row) * ldy;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (o + j < no) yr[o + j] = silu_f(v[2 * j]) * v[2 * j + 1];
+        }
+        return;
+    }
+    if (out_half) {
+        T* yr = static_cast<T*>(y) + static_cast<size_t>(row) * ldy;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (col + j < N) yr[col + j] = to_w<T>(v[j]);
+        return;
+    }
+    float* yr = static_cast<float*>(y) + static_cast<size_t>(row) * ldy + col;
+    const bool vec = col + 32 <= N && ((reinterpret_cast<uintptr_t>(yr) & 15) == 0);
+    if (vec) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            float4* p = reinterpret_cast<float4*>(yr + j);
+            float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            if (mode == LIN_RESIDUAL) {
+                const float4 q = *p;
+                o.x += q.x; o.y += q.y; o.z += q.z; o.w += q.w;
+            }
+            *p = o;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (col + j < N) yr[j] = mode == LIN_RESIDUAL ? yr[j] + v[j] : v[j];
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
+              void* __restrict__ y, int ldy, int mode, int out_half, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    TcBars* bars = reinterpret_cast<TcBars*>(smem + STAGES * STAGE_BYTES);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN, tiles = mt * nt, kbn = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->acc_full[b], 1);
+            mbar_init(&bars->acc_empty[b], 4);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(su32(&bars->tmem))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            unsigned it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int m0 = (t % mt) * BM, n0 = (t / mt) * BN;
+                for (int kb = 0; kb < kbn; ++kb, ++it) {
+                    const int s = static_cast<int>(it % STAGES);
+                    if (!mbar_wait(&bars->empty[s], ((it / STAGES) & 1u) ^ 1u, err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&bars->full[s], STAGE_BYTES);
+                    tma_load_2d(smem + s * STAGE_BYTES, &ta, &bars->full[s], kb * BK, m0);
+                    tma_load_2d(smem + s * STAGE_BYTES + A_BYTES, &tw, &bars->full[s], kb * BK, n0);
+                }
+            }
+            // Let the copies already issued land before the CTA can exit (bounded).
+            const unsigned issued = it;
+            for (unsigned j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+                mbar_wait(&bars->full[j % STAGES], (j / STAGES) & 1u, err);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = f16_idesc(sizeof(T) == 2 && __is_same(T, __nv_bfloat16) ? 1u : 0u, BM, BN);
+            unsigned it = 0, local = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++local) {
+                const unsigned b = local & 1u;
+                if (!mbar_wait(&bars->acc_empty[b], ((local >> 1) & 1u) ^ 1u, err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + b * BN;
+                for (int kb = 0; kb < kbn; ++kb, ++it) {
+                    const int s = static_cast<int>(it % STAGES);
+                    if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = su32(smem + s * STAGE_BYTES), w0 = a0 + A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        umma(d, sw128_desc(a0 + k * 32), sw128_desc(w0 + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+                    umma_commit(&bars->empty[s]);
+                }
+                umma_commit(&bars->acc_full[b]);
+            }
+        }
+    } else {  // epilogue warps 2..5: TMEM lane quarter = warp % 4
+        const int q = warp & 3;
+        unsigned local = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+            const unsigned b = local & 1u;
+            if (!mbar_wait(&bars->acc_full[b], (local >> 1) & 1u, err)) break;
+            tc_fence_after();
+            const int m0 = (t % mt) * BM, n0 = (t / mt) * BN;
+            const int row = m0 + q * 32 + lane;
+            const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                if (n0 + c >= N) break;
+                float v[32];
+                tmem_ld32(base + c, v);
+                epilogue<T>(v, row, n0 + c, M, N, y, ldy, mode, out_half);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc_empty[b]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+}
+
+// One CTA per row: optional RMSNorm (x * (1/sqrt(mean(x^2) + eps)) * w), cast to T.
+template <typename T>
+__global__ void __launch_bounds__(256) k_rows_to_half(const float* __restrict__ x, int ldx, int cols,
+                                                      const float* __restrict__ w, float eps, T* __restrict__ out,
+                                                      int ldo) {
+    __shared__ float red[8];
+    __shared__ float scale;
+    const float* xr = x + static_cast<size_t>(blockIdx.x) * ldx;
+    T* orow = out + static_cast<size_t>(blockIdx.x) * ldo;
+    float s = 1.0f;
+    if (w != nullptr) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < cols; i += blockDim.x) ss += xr[i] * xr[i];
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float t = 0.0f;
+            for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) t += red[i];
+            scale = 1.0f / sqrtf(t / static_cast<float>(cols) + eps);
+        }
+        __syncthreads();
+        s = scale;
+    }
+    for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+        const float v = w != nullptr ? xr[i] * s * w[i] : xr[i];
+        orow[i] = to_w<T>(v);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+}  // namespace
+
+bool tc_available() { return encode_fn() != nullptr; }
+
+int tc_min_rows() {
+    const char* e = std::getenv("SOC_B200_TC_MIN_ROWS");
+    return e && *e ? std::atoi(e) : 64;
+}
+
+void tc_make_map(CUtensorMap* map, const void* base, int wfmt, uint64_t rows, uint64_t cols, uint64_t ld,
+                 uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) throw Error(-2, "cuTensorMapEncodeTiled is not available from the driver");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0 || cols % 8 != 0)
+        throw Error(-1, "tensor-core GEMM operands need 16-byte aligned rows");
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {ld * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = fn(map, wfmt == WF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                          const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(-2, "cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r)));
+}
+
+void launch_gemm_tc(int wfmt, const CUtensorMap& a, const CUtensorMap& w, int M, int N, int K, void* y, int ldy,
+                    int mode, bool out_half, int* err, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return;
+    if (K <= 0 || K % BK != 0) throw Error(-1, "tensor-core GEMM needs K to be a multiple of 64");
+    if (mode == LIN_SWIGLU && N % 2 != 0) throw Error(-1, "SwiGLU GEMM needs an even number of rows");
+    if (mode == LIN_RESIDUAL && out_half) throw Error(-1, "residual GEMM output is fp32");
+    int dev = 0, sms = 0;
+    SOCB_CUDA(cudaGetDevice(&dev));
+    SOCB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int grid = tiles < sms ? tiles : sms;
+    if (wfmt == WF_BF16) {
+        static bool set = false;
+        if (!set) {
+            SOCB_CUDA(cudaFuncSetAttribute(k_gemm_tc<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(TC_SMEM)));
+            set = true;
+        }
+        k_gemm_tc<__nv_bfloat16><<<grid, TC_THREADS, TC_SMEM, st>>>(a, w, M, N, K, y, ldy, mode, out_half ? 1 : 0, err);
+    } else if (wfmt == WF_F16) {
+        static bool set = false;
+        if (!set) {
+            SOCB_CUDA(cudaFuncSetAttribute(k_gemm_tc<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(TC_SMEM)));
+            set = true;
+        }
+        k_gemm_tc<__half><<<grid, TC_THREADS, TC_SMEM, st>>>(a, w, M, N, K, y, ldy, mode, out_half ? 1 : 0, err);
+    } else {
+        throw Error(-1, "tensor-core GEMM supports fp16 and bf16 weights");
+    }
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+void launch_rows_to_half(int wfmt, const float* x, int ldx, int rows, int cols, const float* norm_w, float eps,
+                         void* out, int ldo, cudaStream_t st) {
+    if (rows <= 0) return;
+    if (wfmt == WF_BF16)
+        k_rows_to_half<__nv_bfloat16><<<rows, 256, 0, st>>>(x, ldx, cols, norm_w, eps,
+                                                            static_cast<__nv_bfloat16*>(out), ldo);
+    else
+        k_rows_to_half<__half><<<rows, 256, 0, st>>>(x, ldx, cols, norm_w, eps, static_cast<__half*>(out), ldo);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+}  // namespace socb

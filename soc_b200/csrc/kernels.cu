@@ -101,18 +101,36 @@ void launch_rmsnorm(const float* x, int rows, int n, const float* w, float eps, 
 
 // ------------------------------------------------------------------------ linear
 // One CTA = 8 warps = 16 output rows (a warp owns a row pair) x RB input rows staged in
-// shared memory.  Every lane streams 16-byte weight vectors (8 elements) with the
-// loads of UNR iterations issued before their FMAs, fp32 accumulation, warp-shuffle
-// reduction.  The RMSNorm of the input rows (when norm_w != nullptr) is computed in
-// the prologue, so the normalised activations never touch HBM.
+// shared memory.  Every lane streams 16-byte weight vectors (Codec<F>::EPV elements) with
+// the loads of UNR iterations issued before their FMAs, fp32 accumulation, warp-shuffle
+// reduction.  Group-quantised formats multiply the lane's partial sum over one group
+// slice by that group's fp16 scale.  The RMSNorm of the input rows (when norm_w !=
+// nullptr) is computed in the prologue, so the normalised activations never touch HBM.
+//
+// Shared-memory order of an input row: inside each block of 32*EPV elements (one warp
+// iteration) the 8 elements of part p of lane l sit at (p*32 + l)*8, so the float4 reads
+// of one part by the 32 lanes are consecutive (at most 2-way bank conflicts).
 constexpr int LIN_WARPS = 8;
 constexpr int LIN_THREADS = LIN_WARPS * 32;
 
-template <typename T, int RB>
-__global__ void __launch_bounds__(LIN_THREADS) k_linear(const T* __restrict__ W, int out_f, int in_f,
-                                                        const float* __restrict__ x, int ldx, int rows,
-                                                        const float* __restrict__ norm_w, float eps,
+template <int EPV>
+__host__ __device__ __forceinline__ int lin_padded(int in_f) {
+    return (in_f + 32 * EPV - 1) / (32 * EPV) * (32 * EPV);
+}
+template <int EPV>
+__device__ __forceinline__ int lin_slot(int k) {
+    const int blk = k / (32 * EPV), r = k - blk * (32 * EPV);
+    const int ln = r / EPV, e = r - ln * EPV;
+    return blk * (32 * EPV) + ((e >> 3) * 32 + ln) * 8 + (e & 7);
+}
+
+template <int F, int RB>
+__global__ void __launch_bounds__(LIN_THREADS) k_linear(const uint8_t* __restrict__ W, const __half* __restrict__ S,
+                                                        int out_f, int in_f, const float* __restrict__ x, int ldx,
+                                                        int rows, const float* __restrict__ norm_w, float eps,
                                                         float* __restrict__ y, int ldy, int mode) {
+    using C = Codec<F>;
+    constexpr int EPV = C::EPV, NP = EPV / 8, G = C::GROUP;
     extern __shared__ float4 xs4[];
     float* xs = reinterpret_cast<float*>(xs4);
     __shared__ float red[RB][LIN_WARPS];
@@ -120,15 +138,16 @@ __global__ void __launch_bounds__(LIN_THREADS) k_linear(const T* __restrict__ W,
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r0 = blockIdx.y * RB;
     const int nr = min(RB, rows - r0);
+    const int pin = lin_padded<EPV>(in_f);
 
-    // Stage the input rows (fp32) in shared memory.
+    // Stage the input rows (fp32) in shared memory, zero past in_f.
     for (int r = 0; r < RB; ++r) {
         float ss = 0.0f;
-        for (int i = tid * 4; i < in_f; i += LIN_THREADS * 4) {
-            float4 v = r < nr ? *reinterpret_cast<const float4*>(x + static_cast<size_t>(r0 + r) * ldx + i)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = tid * 4; i < pin; i += LIN_THREADS * 4) {
+            float4 v = (r < nr && i < in_f) ? *reinterpret_cast<const float4*>(x + static_cast<size_t>(r0 + r) * ldx + i)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
             ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-            xs4[(r * in_f + i) >> 2] = v;
+            xs4[(r * pin + lin_slot<EPV>(i)) >> 2] = v;
         }
         if (norm_w != nullptr) {
             ss = warp_sum(ss);
@@ -145,7 +164,10 @@ __global__ void __launch_bounds__(LIN_THREADS) k_linear(const T* __restrict__ W,
         __syncthreads();
         for (int r = 0; r < RB; ++r) {
             const float s = scale_s[r];
-            for (int i = tid; i < in_f; i += LIN_THREADS) xs[r * in_f + i] = xs[r * in_f + i] * s * norm_w[i];
+            for (int i = tid; i < in_f; i += LIN_THREADS) {
+                const int q = r * pin + lin_slot<EPV>(i);
+                xs[q] = xs[q] * s * norm_w[i];
+            }
         }
     }
     __syncthreads();
@@ -154,53 +176,73 @@ __global__ void __launch_bounds__(LIN_THREADS) k_linear(const T* __restrict__ W,
     const int o0 = 2 * pair;
     if (o0 >= out_f) return;
     const bool has1 = (o0 + 1) < out_f;
-    const T* w0 = W + static_cast<size_t>(o0) * in_f;
-    const T* w1 = has1 ? w0 + in_f : w0;
+    const size_t row_bytes = static_cast<size_t>(in_f) / EPV * 16;
+    const uint8_t* w0 = W + static_cast<size_t>(o0) * row_bytes;
+    const uint8_t* w1 = has1 ? w0 + row_bytes : w0;
+    const int ng = G ? in_f / G : 0;
+    const __half* s0 = G ? S + static_cast<size_t>(o0) * ng : nullptr;
+    const __half* s1 = (G && has1) ? s0 + ng : s0;
 
     float acc0[RB], acc1[RB];
 #pragma unroll
     for (int r = 0; r < RB; ++r) acc0[r] = acc1[r] = 0.0f;
 
-    constexpr int UNR = 4;
-    const int step = 32 * 8;
-    int k = lane * 8;
-    for (; k + (UNR - 1) * step < in_f; k += UNR * step) {
-        uint4 ua[UNR], ub[UNR];
+    // One 16-byte vector of each of the two rows: vector index vv (lane = vv % 32).
+    auto consume = [&](const uint4& ua, const uint4& ub, float sa, float sb, int vv) {
+        const int base = (vv >> 5) * (32 * EPV) + lane * 8;
+        float t0[RB], t1[RB];
 #pragma unroll
-        for (int u = 0; u < UNR; ++u) {
-            ua[u] = ld_nc16(w0 + k + u * step);
-            ub[u] = ld_nc16(w1 + k + u * step);
-        }
+        for (int r = 0; r < RB; ++r) t0[r] = t1[r] = 0.0f;
 #pragma unroll
-        for (int u = 0; u < UNR; ++u) {
+        for (int p = 0; p < NP; ++p) {
             float wa[8], wb[8];
-            unpack8<T>(ua[u], wa);
-            unpack8<T>(ub[u], wb);
-            const int kk = k + u * step;
+            C::part(ua, p, wa);
+            C::part(ub, p, wb);
+            const int off = base + p * 256;
 #pragma unroll
             for (int r = 0; r < RB; ++r) {
-                const float4 xa = xs4[(r * in_f + kk) >> 2];
-                const float4 xb = xs4[(r * in_f + kk + 4) >> 2];
-                acc0[r] += wa[0] * xa.x + wa[1] * xa.y + wa[2] * xa.z + wa[3] * xa.w + wa[4] * xb.x +
-                           wa[5] * xb.y + wa[6] * xb.z + wa[7] * xb.w;
-                acc1[r] += wb[0] * xa.x + wb[1] * xa.y + wb[2] * xa.z + wb[3] * xa.w + wb[4] * xb.x +
-                           wb[5] * xb.y + wb[6] * xb.z + wb[7] * xb.w;
+                const float4 xa = xs4[(r * pin + off) >> 2];
+                const float4 xb = xs4[(r * pin + off + 4) >> 2];
+                t0[r] += wa[0] * xa.x + wa[1] * xa.y + wa[2] * xa.z + wa[3] * xa.w + wa[4] * xb.x + wa[5] * xb.y +
+                         wa[6] * xb.z + wa[7] * xb.w;
+                t1[r] += wb[0] * xa.x + wb[1] * xa.y + wb[2] * xa.z + wb[3] * xa.w + wb[4] * xb.x + wb[5] * xb.y +
+                         wb[6] * xb.z + wb[7] * xb.w;
             }
         }
-    }
-    for (; k < in_f; k += step) {
-        float wa[8], wb[8];
-        unpack8<T>(ld_nc16(w0 + k), wa);
-        unpack8<T>(ld_nc16(w1 + k), wb);
 #pragma unroll
         for (int r = 0; r < RB; ++r) {
-            const float4 xa = xs4[(r * in_f + k) >> 2];
-            const float4 xb = xs4[(r * in_f + k + 4) >> 2];
-            acc0[r] += wa[0] * xa.x + wa[1] * xa.y + wa[2] * xa.z + wa[3] * xa.w + wa[4] * xb.x + wa[5] * xb.y +
-                       wa[6] * xb.z + wa[7] * xb.w;
-            acc1[r] += wb[0] * xa.x + wb[1] * xa.y + wb[2] * xa.z + wb[3] * xa.w + wb[4] * xb.x + wb[5] * xb.y +
-                       wb[6] * xb.z + wb[7] * xb.w;
+            if (G) {
+                acc0[r] = fmaf(sa, t0[r], acc0[r]);
+                acc1[r] = fmaf(sb, t1[r], acc1[r]);
+            } else {
+                acc0[r] += t0[r];
+                acc1[r] += t1[r];
+            }
         }
+    };
+
+    constexpr int UNR = EPV == 8 ? 4 : 2;
+    const int nv = in_f / EPV;
+    int v = lane;
+    for (; v + 32 * (UNR - 1) < nv; v += 32 * UNR) {
+        uint4 ua[UNR], ub[UNR];
+        float sa[UNR], sb[UNR];
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+            ua[u] = ld_nc16(w0 + static_cast<size_t>(v + 32 * u) * 16);
+            ub[u] = ld_nc16(w1 + static_cast<size_t>(v + 32 * u) * 16);
+            sa[u] = G ? __half2float(s0[(v + 32 * u) * EPV / (G ? G : 1)]) : 1.0f;
+            sb[u] = G ? __half2float(s1[(v + 32 * u) * EPV / (G ? G : 1)]) : 1.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) consume(ua[u], ub[u], sa[u], sb[u], v + 32 * u);
+    }
+    for (; v < nv; v += 32) {
+        const uint4 ua = ld_nc16(w0 + static_cast<size_t>(v) * 16);
+        const uint4 ub = ld_nc16(w1 + static_cast<size_t>(v) * 16);
+        const float sa = G ? __half2float(s0[v * EPV / (G ? G : 1)]) : 1.0f;
+        const float sb = G ? __half2float(s1[v * EPV / (G ? G : 1)]) : 1.0f;
+        consume(ua, ub, sa, sb, v);
     }
 #pragma unroll
     for (int r = 0; r < RB; ++r) {
@@ -226,49 +268,57 @@ __global__ void __launch_bounds__(LIN_THREADS) k_linear(const T* __restrict__ W,
     }
 }
 
-template <typename T, int RB>
-static void linear_rb(const T* W, int out_f, int in_f, const float* x, int ldx, int rows, const float* norm_w,
-                      float eps, float* y, int ldy, int mode, cudaStream_t st) {
-    const size_t smem = static_cast<size_t>(RB) * in_f * sizeof(float);
+constexpr size_t LIN_SMEM_CAP = 96 * 1024;  // fp32 staging budget that picks the row block
+
+template <int F, int RB>
+static void linear_rb(const void* W, const void* S, int out_f, int in_f, const float* x, int ldx, int rows,
+                      const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    const size_t smem = static_cast<size_t>(RB) * lin_padded<Codec<F>::EPV>(in_f) * sizeof(float);
     static bool attr_set = false;  // one attribute set per template instance
     if (!attr_set) {
-        SOCB_CUDA(cudaFuncSetAttribute(k_linear<T, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        SOCB_CUDA(cudaFuncSetAttribute(k_linear<F, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         attr_set = true;
     }
     const int pairs = (out_f + 1) / 2;
     dim3 grid((pairs + LIN_WARPS - 1) / LIN_WARPS, (rows + RB - 1) / RB);
-    k_linear<T, RB><<<grid, LIN_THREADS, smem, st>>>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode);
+    k_linear<F, RB><<<grid, LIN_THREADS, smem, st>>>(static_cast<const uint8_t*>(W), static_cast<const __half*>(S),
+                                                     out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }
 
-template <typename T>
-static void linear_t(const T* W, int out_f, int in_f, const float* x, int ldx, int rows, const float* norm_w,
-                     float eps, float* y, int ldy, int mode, cudaStream_t st) {
-    // Largest row block whose fp32 staging fits in 96 KB of shared memory.
-    const size_t cap = 96 * 1024 / (static_cast<size_t>(in_f) * sizeof(float));
+template <int F>
+static void linear_f(const void* W, const void* S, int out_f, int in_f, const float* x, int ldx, int rows,
+                     const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    constexpr int EPV = Codec<F>::EPV, G = Codec<F>::GROUP;
+    if (in_f % EPV != 0 || (G > 0 && in_f % (G > 0 ? G : 1) != 0))
+        throw Error(-1, "linear: in_features is not a multiple of the weight format's vector/group size");
+    if (G && S == nullptr) throw Error(-1, "linear: group-quantised weights need their scales");
+    const size_t row_smem = static_cast<size_t>(lin_padded<EPV>(in_f)) * sizeof(float);
+    if (row_smem > 200 * 1024) throw Error(-1, "linear: in_features too large");
+    // Largest row block whose fp32 staging fits the budget.
+    const size_t cap = LIN_SMEM_CAP / row_smem;
     if (rows >= 8 && cap >= 8)
-        linear_rb<T, 8>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+        linear_rb<F, 8>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
     else if (rows >= 4 && cap >= 4)
-        linear_rb<T, 4>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+        linear_rb<F, 4>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
     else if (rows >= 2 && cap >= 2)
-        linear_rb<T, 2>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+        linear_rb<F, 2>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
     else
-        linear_rb<T, 1>(W, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+        linear_rb<F, 1>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
 }
 
 void launch_linear(int wfmt, const void* W, const void* scales, int out_f, int in_f, const float* x, int ldx,
                    int rows, const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
-    (void)scales;
     if (rows <= 0 || out_f <= 0) return;
-    if (in_f % 8 != 0 || ldx % 4 != 0) throw Error(-1, "linear: in_features and ldx must be multiples of 8 and 4");
-    if (static_cast<size_t>(in_f) * sizeof(float) > 200 * 1024) throw Error(-1, "linear: in_features too large");
-    if (wfmt == WF_BF16)
-        linear_t(static_cast<const __nv_bfloat16*>(W), out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
-    else if (wfmt == WF_F16)
-        linear_t(static_cast<const __half*>(W), out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
-    else
-        throw Error(-1, "linear: unsupported weight format");
+    if (ldx % 4 != 0) throw Error(-1, "linear: ldx must be a multiple of 4");
+    switch (wfmt) {
+        case WF_F16: linear_f<WF_F16>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        case WF_BF16: linear_f<WF_BF16>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        case WF_I8G64: linear_f<WF_I8G64>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        case WF_I4G32: linear_f<WF_I4G32>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        default: throw Error(-1, "linear: unsupported weight format");
+    }
 }
 
 // ------------------------------------------------- q/k RMSNorm + RoPE + paged KV append

@@ -22,6 +22,7 @@
 #include "../../include/soc_b200.h"
 #include "common.cuh"
 #include "decode_mk.h"
+#include "gemm_tc.h"
 #include "json.hpp"
 #include "kernels.h"
 
@@ -243,6 +244,134 @@ uint16_t float_to_half_bits(float f) {
     return u;
 }
 
+
+// ------------------------------------------------- linear matrices in the device format
+// Group-wise quantised records (bundle extension): dtype "int8_g64" ([out, in] int8) or
+// "int4_g32" ([out, in/2] bytes, two's complement nibbles, low nibble = even column), each
+// with a "<name>.scales" float16 record [out, in/group].  Value = float(q) * float(scale).
+int quant_group(int fmt) { return fmt == WF_I8G64 ? 64 : fmt == WF_I4G32 ? 32 : 0; }
+size_t fmt_row_bytes(int fmt, size_t cols) {
+    return fmt == WF_I8G64 ? cols : fmt == WF_I4G32 ? cols / 2 : cols * 2;
+}
+int fmt_of_dtype(const std::string& d) {
+    if (d == "int8_g64") return WF_I8G64;
+    if (d == "int4_g32") return WF_I4G32;
+    if (d == "bfloat16") return WF_BF16;
+    if (d == "float16" || d == "float32") return WF_F16;
+    return 0;
+}
+
+struct HostMat {
+    std::vector<uint8_t> data;     // rows * fmt_row_bytes
+    std::vector<uint16_t> scales;  // rows * cols / group fp16 bits (quantised formats)
+};
+
+// Symmetric group quantisation, the per-group extension of QuantizeMatMulRhs8
+// (Mac/cpu/header/matrix_ops.h:42-73): s = fp16(max|w| / qmax), q = clamp(rint(w / s)).
+void quantize_rows(const float* w, size_t rows, size_t cols, int fmt, HostMat& out) {
+    const int g = quant_group(fmt);
+    const float qmax = fmt == WF_I8G64 ? 127.0f : 7.0f;
+    const size_t ng = cols / g;
+    out.data.assign(rows * fmt_row_bytes(fmt, cols), 0);
+    out.scales.assign(rows * ng, 0);
+    std::vector<int8_t> q(g);
+    for (size_t r = 0; r < rows; ++r) {
+        for (size_t gi = 0; gi < ng; ++gi) {
+            const float* wg = w + r * cols + gi * g;
+            float amax = 0.0f;
+            for (int i = 0; i < g; ++i) amax = std::max(amax, std::fabs(wg[i]));
+            const uint16_t sb = float_to_half_bits(amax / qmax);
+            const float s = half_bits_to_float(sb);
+            for (int i = 0; i < g; ++i) {
+                float v = s == 0.0f ? 0.0f : std::nearbyint(wg[i] / s);
+                v = std::min(qmax, std::max(-qmax, v));
+                q[i] = static_cast<int8_t>(v);
+            }
+            out.scales[r * ng + gi] = sb;
+            uint8_t* dst = out.data.data() + r * fmt_row_bytes(fmt, cols) + fmt_row_bytes(fmt, gi * g);
+            if (fmt == WF_I8G64) {
+                std::memcpy(dst, q.data(), g);
+            } else {
+                for (int i = 0; i < g; i += 2)
+                    dst[i / 2] = static_cast<uint8_t>((q[i] & 0xF) | ((q[i + 1] & 0xF) << 4));
+            }
+        }
+    }
+}
+
+std::vector<float> dequantize_rows(const std::vector<char>& b, const std::vector<char>& sb, size_t rows, size_t cols,
+                                   int fmt) {
+    const int g = quant_group(fmt);
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(sb.data());
+    const uint8_t* d = reinterpret_cast<const uint8_t*>(b.data());
+    std::vector<float> out(rows * cols);
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t c = 0; c < cols; ++c) {
+            int q;
+            if (fmt == WF_I8G64) {
+                q = static_cast<int8_t>(d[r * cols + c]);
+            } else {
+                const uint8_t byte = d[r * (cols / 2) + c / 2];
+                q = (c & 1) ? (byte >> 4) : (byte & 0xF);
+                if (q > 7) q -= 16;
+            }
+            out[r * cols + c] = static_cast<float>(q) * half_bits_to_float(sc[r * (cols / g) + c / g]);
+        }
+    return out;
+}
+
+// Reads linear `name` ([rows, cols]) and returns it in device format `fmt`.
+HostMat prepare_matrix(const Manifest& man, const std::string& name, size_t rows, size_t cols, int fmt) {
+    const TensorRecord& r = man.find(name);
+    HostMat out;
+    const int src = fmt_of_dtype(r.dtype);
+    std::vector<float> f32;
+    if (src == WF_I8G64 || src == WF_I4G32) {
+        if (r.shape != std::vector<size_t>{rows, cols})
+            throw_fmt("model loader encountered unexpected shape for: " + name);
+        const int g = quant_group(src);
+        if (cols % g != 0) throw_fmt("quantised tensor columns are not a multiple of the group for: " + name);
+        TensorRecord raw = r;
+        raw.dtype = "uint8";
+        raw.shape = {rows * fmt_row_bytes(src, cols)};
+        const std::vector<char> b = load_record(raw, raw.shape);
+        const TensorRecord& rs = man.find(name + ".scales");
+        if (rs.dtype != "float16") throw_fmt("quantisation scales must be float16 for: " + name);
+        const std::vector<char> sb = load_record(rs, {rows, cols / g});
+        if (src == fmt) {
+            out.data.assign(b.begin(), b.end());
+            out.scales.resize(rows * (cols / g));
+            std::memcpy(out.scales.data(), sb.data(), sb.size());
+            return out;
+        }
+        f32 = dequantize_rows(b, sb, rows, cols, src);
+    } else {
+        const std::vector<char> b = load_record(r, {rows, cols});
+        const bool same = (fmt == WF_F16 && r.dtype == "float16") || (fmt == WF_BF16 && r.dtype == "bfloat16");
+        if (same) {
+            out.data.assign(b.begin(), b.end());
+            return out;
+        }
+        f32 = to_f32(r, b);
+    }
+    if (fmt == WF_I8G64 || fmt == WF_I4G32) {
+        if (cols % quant_group(fmt) != 0) throw_fmt("in_features is not a multiple of the quantisation group: " + name);
+        quantize_rows(f32.data(), rows, cols, fmt, out);
+        return out;
+    }
+    out.data.resize(rows * cols * 2);
+    uint16_t* d = reinterpret_cast<uint16_t*>(out.data.data());
+    for (size_t i = 0; i < f32.size(); ++i) {
+        if (fmt == WF_F16) {
+            d[i] = float_to_half_bits(f32[i]);
+        } else {
+            const __nv_bfloat16 bb = __float2bfloat16_rn(f32[i]);
+            std::memcpy(&d[i], &bb, 2);
+        }
+    }
+    return out;
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------- objects
@@ -251,6 +380,8 @@ struct soc_ctx {
     cudaStream_t stream = nullptr;
     int sm_count = 0;
     int* d_err = nullptr;
+    void* lin_scratch = nullptr;  // fp16/bf16 copy of soc_b200_linear's input rows (tensor-core path)
+    size_t lin_scratch_bytes = 0;
 };
 
 struct LayerW {
@@ -258,6 +389,10 @@ struct LayerW {
     void* wo = nullptr;    // [hidden, hq * hd]
     void* wgu = nullptr;   // [2 * inter, hidden] rows (2j, 2j+1) = (gate_j, up_j)
     void* wd = nullptr;    // [hidden, inter]
+    // fp16 group scales [rows, in / group] of the same matrices (quantised formats only)
+    void *sqkv = nullptr, *so = nullptr, *sgu = nullptr, *sd = nullptr;
+    // TMA descriptors of the four matrices for the tensor-core GEMM (fp16 / bf16 only)
+    CUtensorMap tm_qkv{}, tm_o{}, tm_gu{}, tm_d{};
     float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
 };
 
@@ -277,6 +412,9 @@ struct soc_model {
     int ws_rows = 0;
     float *h = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
     int *d_tokens = nullptr, *d_seq = nullptr, *d_pos = nullptr, *d_next = nullptr;
+    void* xa = nullptr;    // [ws_rows, max(hidden, q width)] fp16/bf16 GEMM input rows
+    void* acth = nullptr;  // [ws_rows, inter] fp16/bf16 SwiGLU output (down_proj input)
+    bool tc_ok = false;    // tensor-core GEMM usable for this model's linears
     float* logits = nullptr;
     int logits_rows = 0;
     float* attn_scratch = nullptr;
@@ -381,6 +519,12 @@ void ensure_workspace(soc_model* m, int rows) {
     m->d_seq = static_cast<int*>(m->dmalloc(sizeof(int) * r));
     m->d_pos = static_cast<int*>(m->dmalloc(sizeof(int) * r));
     m->d_next = static_cast<int*>(m->dmalloc(sizeof(int) * r));
+    if (m->tc_ok) {
+        m->dfree(m->xa);
+        m->dfree(m->acth);
+        m->xa = m->dmalloc(2 * static_cast<size_t>(r) * std::max(c.hidden, c.hq * c.hd));
+        m->acth = m->dmalloc(2 * static_cast<size_t>(r) * c.inter);
+    }
     m->ws_rows = r;
 }
 
@@ -423,17 +567,39 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
     if (splits < 1) splits = attention_splits(n, static_cast<int>(c.hkv), max_visible);
     if (splits > 1) ensure_attn_scratch(m, static_cast<size_t>(n) * c.hq * splits * (c.hd + 2));
     launch_embed(m->efmt, m->embed, H, static_cast<int>(c.vocab), m->d_tokens, n, m->h, m->ctx->d_err, st);
+    // Tensor-core GEMMs for the block linears once there are enough rows to fill a tile.
+    const bool tc = m->tc_ok && tc_min_rows() > 0 && n >= tc_min_rows();
+    CUtensorMap a_h{}, a_att{}, a_act{};
+    if (tc) {
+        tc_make_map(&a_h, m->xa, m->wfmt, n, H, H, TC_BOX_A);
+        tc_make_map(&a_att, m->xa, m->wfmt, n, QW, QW, TC_BOX_A);
+        tc_make_map(&a_act, m->acth, m->wfmt, n, I, I, TC_BOX_A);
+    }
+    int* err = m->ctx->d_err;
     for (size_t l = 0; l < c.layers; ++l) {
         const LayerW& w = m->layers[l];
-        launch_linear(m->wfmt, w.wqkv, nullptr, QKV, H, m->h, H, n, w.in_norm, eps, m->qkv, QKV, LIN_STORE, st);
+        if (tc) {
+            launch_rows_to_half(m->wfmt, m->h, H, n, H, w.in_norm, eps, m->xa, H, st);
+            launch_gemm_tc(m->wfmt, a_h, w.tm_qkv, n, QKV, H, m->qkv, QKV, LIN_STORE, false, err, st);
+        } else {
+            launch_linear(m->wfmt, w.wqkv, w.sqkv, QKV, H, m->h, H, n, w.in_norm, eps, m->qkv, QKV, LIN_STORE, st);
+        }
         launch_qk_norm_rope_kv(m->qkv, rows, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
                                w.q_norm, w.k_norm, eps, m->rope_cs, m->rope_len, kv->view(static_cast<int>(l)), m->q,
                                m->ctx->d_err, st);
         launch_attention(m->q, rows, splits, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
                          kv->view(static_cast<int>(l)), m->att, m->attn_scratch, m->attn_scratch_floats, st);
-        launch_linear(m->wfmt, w.wo, nullptr, H, QW, m->att, QW, n, nullptr, eps, m->h, H, LIN_RESIDUAL, st);
-        launch_linear(m->wfmt, w.wgu, nullptr, 2 * I, H, m->h, H, n, w.post_norm, eps, m->act, I, LIN_SWIGLU, st);
-        launch_linear(m->wfmt, w.wd, nullptr, H, I, m->act, I, n, nullptr, eps, m->h, H, LIN_RESIDUAL, st);
+        if (tc) {
+            launch_rows_to_half(m->wfmt, m->att, QW, n, QW, nullptr, eps, m->xa, QW, st);
+            launch_gemm_tc(m->wfmt, a_att, w.tm_o, n, H, QW, m->h, H, LIN_RESIDUAL, false, err, st);
+            launch_rows_to_half(m->wfmt, m->h, H, n, H, w.post_norm, eps, m->xa, H, st);
+            launch_gemm_tc(m->wfmt, a_h, w.tm_gu, n, 2 * I, H, m->acth, I, LIN_SWIGLU, true, err, st);
+            launch_gemm_tc(m->wfmt, a_act, w.tm_d, n, H, I, m->h, H, LIN_RESIDUAL, false, err, st);
+        } else {
+            launch_linear(m->wfmt, w.wo, w.so, H, QW, m->att, QW, n, nullptr, eps, m->h, H, LIN_RESIDUAL, st);
+            launch_linear(m->wfmt, w.wgu, w.sgu, 2 * I, H, m->h, H, n, w.post_norm, eps, m->act, I, LIN_SWIGLU, st);
+            launch_linear(m->wfmt, w.wd, w.sd, H, I, m->act, I, n, nullptr, eps, m->h, H, LIN_RESIDUAL, st);
+        }
     }
     if (lm_rows > 0) {
         ensure_logits(m, lm_rows);
@@ -656,6 +822,7 @@ void soc_b200_close(soc_ctx* ctx) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->d_err);
+    if (ctx->lin_scratch) cudaFree(ctx->lin_scratch);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
 }
@@ -681,16 +848,19 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
         const Config& c = m->cfg;
         const size_t H = c.hidden, I = c.inter, D = c.hd, QW = c.hq * D, KW = c.hkv * D;
 
-        // Linear weight format: every block linear must share one float type.
+        // Linear weight format: the stored type of the block linears unless the caller asks
+        // for another one (float -> float conversion, or group quantisation at load time).
         const std::string lin_dtype = man.find("model.layers.0.self_attn.q_proj.weight").dtype;
-        int fmt = lin_dtype == "bfloat16" ? WF_BF16 : WF_F16;
-        if (lin_dtype != "float16" && lin_dtype != "bfloat16" && lin_dtype != "float32")
-            throw_fmt("model loader requires floating-point weights for: model.layers.0.self_attn.q_proj.weight");
+        int fmt = fmt_of_dtype(lin_dtype);
+        if (fmt == 0) throw_fmt("model loader requires floating-point weights for: model.layers.0.self_attn.q_proj.weight");
         if (weight_format == SOC_B200_WEIGHTS_F16) fmt = WF_F16;
         else if (weight_format == SOC_B200_WEIGHTS_BF16) fmt = WF_BF16;
+        else if (weight_format == SOC_B200_WEIGHTS_INT8_G64) fmt = WF_I8G64;
+        else if (weight_format == SOC_B200_WEIGHTS_INT4_G32) fmt = WF_I4G32;
         else if (weight_format != SOC_B200_WEIGHTS_NATIVE)
-            throw Error(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: weight_format not supported by this build");
+            throw Error(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: unknown weight_format");
         m->wfmt = fmt;
+        const bool quant = quant_group(fmt) != 0;
 
         // Converts a float tensor to the device element type `f` (bit copy when it already matches).
         auto upload_matrix = [&](const TensorRecord& r, const std::vector<char>& b, void* dst, int f) {
@@ -738,35 +908,57 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
             w.post_norm = upload_norm(p + "post_attention_layernorm.weight", H);
             w.q_norm = upload_norm(p + "self_attn.q_norm.weight", D);
             w.k_norm = upload_norm(p + "self_attn.k_norm.weight", D);
-            char* qkv = static_cast<char*>(m->dmalloc((QW + 2 * KW) * H * 2));
-            w.wqkv = qkv;
-            const TensorRecord& rq = man.find(p + "self_attn.q_proj.weight");
-            upload_matrix(rq, load_record(rq, {QW, H}), qkv, fmt);
-            const TensorRecord& rk = man.find(p + "self_attn.k_proj.weight");
-            upload_matrix(rk, load_record(rk, {KW, H}), qkv + QW * H * 2, fmt);
-            const TensorRecord& rv = man.find(p + "self_attn.v_proj.weight");
-            upload_matrix(rv, load_record(rv, {KW, H}), qkv + (QW + KW) * H * 2, fmt);
-            const TensorRecord& ro = man.find(p + "self_attn.o_proj.weight");
-            w.wo = m->dmalloc(H * QW * 2);
-            upload_matrix(ro, load_record(ro, {H, QW}), w.wo, fmt);
-            // gate / up interleaved by row: staged as two dense blocks, then shuffled on the host.
-            const TensorRecord& rg = man.find(p + "mlp.gate_proj.weight");
-            const TensorRecord& ru = man.find(p + "mlp.up_proj.weight");
-            void* tmp_g = m->dmalloc(I * H * 2);
-            void* tmp_u = m->dmalloc(I * H * 2);
-            upload_matrix(rg, load_record(rg, {I, H}), tmp_g, fmt);
-            upload_matrix(ru, load_record(ru, {I, H}), tmp_u, fmt);
-            w.wgu = m->dmalloc(2 * I * H * 2);
-            SOCB_CUDA(cudaMemcpy2D(w.wgu, 2 * H * 2, tmp_g, H * 2, H * 2, I, cudaMemcpyDeviceToDevice));
-            SOCB_CUDA(cudaMemcpy2D(static_cast<char*>(w.wgu) + H * 2, 2 * H * 2, tmp_u, H * 2, H * 2, I,
-                                   cudaMemcpyDeviceToDevice));
-            m->dfree(tmp_g);
-            m->dfree(tmp_u);
-            const TensorRecord& rd = man.find(p + "mlp.down_proj.weight");
-            w.wd = m->dmalloc(H * I * 2);
-            upload_matrix(rd, load_record(rd, {H, I}), w.wd, fmt);
+            // Uploads rows of one or more matrices (concatenated, or interleaved row by row).
+            auto upload_rows = [&](const std::vector<HostMat>& mats, const std::vector<size_t>& rows, size_t cols,
+                                   bool interleave, void** dst, void** sdst) {
+                const size_t rb = fmt_row_bytes(fmt, cols), sr = quant ? cols / quant_group(fmt) : 0;
+                size_t total = 0;
+                for (size_t r : rows) total += r;
+                std::vector<uint8_t> data(total * rb);
+                std::vector<uint16_t> sc(total * sr);
+                if (!interleave) {
+                    size_t at = 0;
+                    for (size_t i = 0; i < mats.size(); ++i) {
+                        std::memcpy(data.data() + at * rb, mats[i].data.data(), rows[i] * rb);
+                        if (quant) std::memcpy(sc.data() + at * sr, mats[i].scales.data(), rows[i] * sr * 2);
+                        at += rows[i];
+                    }
+                } else {  // rows (2j, 2j+1) = (mats[0] row j, mats[1] row j)
+                    for (size_t j = 0; j < rows[0]; ++j)
+                        for (int t = 0; t < 2; ++t) {
+                            std::memcpy(data.data() + (2 * j + t) * rb, mats[t].data.data() + j * rb, rb);
+                            if (quant)
+                                std::memcpy(sc.data() + (2 * j + t) * sr, mats[t].scales.data() + j * sr, sr * 2);
+                        }
+                }
+                *dst = m->dmalloc(data.size());
+                SOCB_CUDA(cudaMemcpy(*dst, data.data(), data.size(), cudaMemcpyHostToDevice));
+                if (quant) {
+                    *sdst = m->dmalloc(sc.size() * 2);
+                    SOCB_CUDA(cudaMemcpy(*sdst, sc.data(), sc.size() * 2, cudaMemcpyHostToDevice));
+                }
+            };
+            upload_rows({prepare_matrix(man, p + "self_attn.q_proj.weight", QW, H, fmt),
+                         prepare_matrix(man, p + "self_attn.k_proj.weight", KW, H, fmt),
+                         prepare_matrix(man, p + "self_attn.v_proj.weight", KW, H, fmt)},
+                        {QW, KW, KW}, H, false, &w.wqkv, &w.sqkv);
+            upload_rows({prepare_matrix(man, p + "self_attn.o_proj.weight", H, QW, fmt)}, {H}, QW, false, &w.wo, &w.so);
+            upload_rows({prepare_matrix(man, p + "mlp.gate_proj.weight", I, H, fmt),
+                         prepare_matrix(man, p + "mlp.up_proj.weight", I, H, fmt)},
+                        {I, I}, H, true, &w.wgu, &w.sgu);
+            upload_rows({prepare_matrix(man, p + "mlp.down_proj.weight", H, I, fmt)}, {H}, I, false, &w.wd, &w.sd);
         }
         m->final_norm = upload_norm("model.norm.weight", H);
+        // TMA descriptors of the block linears for the tensor-core GEMM.
+        m->tc_ok = (fmt == WF_F16 || fmt == WF_BF16) && tc_available();
+        if (m->tc_ok) {
+            for (auto& w : m->layers) {
+                tc_make_map(&w.tm_qkv, w.wqkv, fmt, QW + 2 * KW, H, H, TC_BOX_W);
+                tc_make_map(&w.tm_o, w.wo, fmt, H, QW, QW, TC_BOX_W);
+                tc_make_map(&w.tm_gu, w.wgu, fmt, 2 * I, H, H, TC_BOX_W);
+                tc_make_map(&w.tm_d, w.wd, fmt, H, I, I, TC_BOX_W);
+            }
+        }
         if (c.tied) {
             m->lm_head = m->embed;
         } else {
@@ -1111,13 +1303,34 @@ int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* 
     return guarded([&] {
         if (out_features <= 0 || in_features <= 0 || rows <= 0)
             throw Error(SOC_B200_ERR_INVALID, "linear: dimensions must be positive");
-        int f = weight_format == SOC_B200_WEIGHTS_BF16 ? WF_BF16
-                : weight_format == SOC_B200_WEIGHTS_F16 ? WF_F16
-                                                        : -1;
+        const int f = weight_format == SOC_B200_WEIGHTS_BF16       ? WF_BF16
+                      : weight_format == SOC_B200_WEIGHTS_F16      ? WF_F16
+                      : weight_format == SOC_B200_WEIGHTS_INT8_G64 ? WF_I8G64
+                      : weight_format == SOC_B200_WEIGHTS_INT4_G32 ? WF_I4G32
+                                                                   : -1;
         if (f < 0) throw Error(SOC_B200_ERR_INVALID, "linear: weight format not supported by this build");
         cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-        launch_linear(f, w, scales, out_features, in_features, x, in_features, rows, nullptr, 0.0f, y, out_features,
-                      LIN_STORE, st);
+        const bool tc = (f == WF_F16 || f == WF_BF16) && tc_min_rows() > 0 && rows >= tc_min_rows() &&
+                        in_features % 64 == 0 && tc_available();
+        if (!tc) {
+            launch_linear(f, w, scales, out_features, in_features, x, in_features, rows, nullptr, 0.0f, y,
+                          out_features, LIN_STORE, st);
+            return;
+        }
+        const size_t need = 2 * static_cast<size_t>(rows) * in_features;
+        if (need > ctx->lin_scratch_bytes) {
+            SOCB_CUDA(cudaStreamSynchronize(st));
+            if (ctx->lin_scratch) SOCB_CUDA(cudaFree(ctx->lin_scratch));
+            ctx->lin_scratch = nullptr;
+            ctx->lin_scratch_bytes = 0;
+            SOCB_CUDA(cudaMalloc(&ctx->lin_scratch, need));
+            ctx->lin_scratch_bytes = need;
+        }
+        CUtensorMap ta{}, tw{};
+        tc_make_map(&ta, ctx->lin_scratch, f, rows, in_features, in_features, TC_BOX_A);
+        tc_make_map(&tw, w, f, out_features, in_features, in_features, TC_BOX_W);
+        launch_rows_to_half(f, x, in_features, rows, in_features, nullptr, 0.0f, ctx->lin_scratch, in_features, st);
+        launch_gemm_tc(f, ta, tw, rows, out_features, in_features, y, out_features, LIN_STORE, false, ctx->d_err, st);
     });
 }
 

@@ -90,3 +90,23 @@ def test_reference_loads_synthetic_bundle(tmp_path):
     p = B.write_synthetic_bundle(tmp_path / "b", B.tiny_config(num_hidden_layers=1), seed=2)
     rm = O.RefModel(p, 8)
     assert rm.forward([1, 2], 0).shape == (2, 1000)
+
+
+@pytest.mark.parametrize("fmt", ["int8_g64", "int4_g32"])
+def test_quantize_bundle_exporter(tmp_path, fmt):
+    """The exporter option re-encodes only the block linears; the oracle decodes them."""
+    from oracle import oracle as O
+    src = B.write_synthetic_bundle(tmp_path / "src", B.tiny_config(), seed=2)
+    out = B.quantize_bundle(src, tmp_path / fmt, fmt)
+    ms, mq = B.read_manifest(src), B.read_manifest(out)
+    assert mq["export_dtype"] == fmt
+    recs = {r["name"]: r for r in mq["tensors"]}
+    name = "model.layers.1.mlp.down_proj.weight"
+    assert recs[name]["dtype"] == fmt and recs[name + ".scales"]["dtype"] == "float16"
+    assert recs["model.embed_tokens.weight"]["dtype"] == "float16"
+    w = np.asarray(B.load_tensor(ms, name), dtype=np.float32)
+    q, s = B.quantize_groupwise(w, fmt)
+    assert np.array_equal(np.asarray(B.load_tensor(mq, name)), q)
+    assert np.array_equal(np.asarray(B.load_tensor(mq, name + ".scales")), s)
+    lg = O.OracleModel(out, 32).forward([5, 6, 7], 0, last_only=True)[0]
+    assert np.isfinite(lg).all()

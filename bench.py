@@ -337,6 +337,83 @@ def run_soc(args, rank, world, local):
         print(json.dumps(result), flush=True)
 
 
+# ------------------------------------------------------------------- config 2
+C2_PROMPT, C2_NEW = 2048, 129  # 1 id from the prefill + 128 decode steps
+
+
+def config2_flops(cfg: dict, n: int) -> float:
+    """Algorithmic FLOPs of an n-token causal prefill (linears, attention, last-row lm_head)."""
+    H, I, L, D = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["head_dim"]
+    hq, hkv, V = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["vocab_size"]
+    lin = L * (H * (hq + 2 * hkv) * D + H * hq * D + 3 * H * I)
+    attn = L * hq * D * 2 * 2 * (n * (n + 1) / 2)  # QK^T and PV over the causal triangle
+    return 2.0 * lin * n + attn + 2.0 * V * H
+
+
+def run_config2(args):
+    """Config 2: Qwen3-0.6B fp16 (weights as config 0), one 2048-token prompt (ids seed 3)
+    prefilled, then 128 greedy decode steps against the 2048-entry KV cache.  Prints one JSON
+    line: prefill time and its tensor-roofline fraction, decode tokens/s at context 2048-2176
+    and its HBM-roofline fraction."""
+    import torch
+    from soc_b200 import runtime as R
+    from soc_b200.bundle import QWEN3_0_6B
+    torch.cuda.set_device(0)
+    p = config0_bundle(0, 1, lambda: None)
+    ctx = R.Context(0)
+    model = R.Model(ctx, p)
+    kv = R.KVCache(model, 1, C2_PROMPT + C2_NEW + 16)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    prompt = np.random.default_rng(3).integers(0, QWEN3_0_6B["vocab_size"], C2_PROMPT).astype(np.int32)
+    d_prompt = torch.from_numpy(prompt).cuda()
+    d_out = torch.zeros(C2_NEW, dtype=torch.int32, device="cuda")
+
+    def job(max_new):
+        model.generate_device(kv, 0, d_prompt.data_ptr(), C2_PROMPT, max_new, d_out.data_ptr())
+
+    for _ in range(max(args.warmup, 3)):
+        job(C2_NEW)
+    ctx.synchronize()
+
+    def timed(max_new, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ctx.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            job(max_new)
+        e1.record(stream)
+        ctx.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    reps = max(1, min(args.steps, 10))
+    launches0 = R.kernel_launches()
+    with ClockSampler(0) as clk:
+        ms_job = timed(C2_NEW, reps)
+        ms_prefill = timed(1, reps)
+    launches = (R.kernel_launches() - launches0) // (2 * reps)
+    greedy = d_out.cpu().tolist()
+    cfg = QWEN3_0_6B
+    flops = config2_flops(cfg, C2_PROMPT)
+    decode_ms = (ms_job - ms_prefill) / (C2_NEW - 1)
+    alg_bytes = float(np.mean([qwen06_bytes_per_decode_step(cfg, C2_PROMPT + i) for i in range(C2_NEW - 1)]))
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tc_peak = peaks.get("bf16_tflops", 1590.0)
+    hbm = load_peaks()["hbm_gbs"]
+    print(json.dumps({
+        "workload": "config2: Qwen3-0.6B fp16, prefill 2048 ids (seed 3) + 128 greedy decode steps",
+        "prefill_ms": ms_prefill, "prefill_tokens_per_s": C2_PROMPT / (ms_prefill * 1e-3),
+        "prefill_tflops": flops / (ms_prefill * 1e-3) / 1e12, "prefill_algorithmic_flop": flops,
+        "prefill_frac_of_measured_bf16": flops / (ms_prefill * 1e-3) / 1e12 / tc_peak,
+        "decode_ms_per_token": decode_ms, "decode_tokens_per_s": 1e3 / decode_ms,
+        "decode_gbs": alg_bytes / (decode_ms * 1e-3) / 1e9,
+        "decode_frac_of_measured_hbm": alg_bytes / (decode_ms * 1e-3) / 1e9 / hbm,
+        "job_ms": ms_job, "kernels_per_job": int(launches), "clocks": clk.summary(),
+        "greedy_ids_head": greedy[:8]}), flush=True)
+    kv.free()
+    model.free()
+    ctx.close()
+
+
 # ------------------------------------------------------------- config 1 sweep
 SWEEP_SHAPES = {"q_proj": (2048, 1024), "k_proj": (1024, 1024), "o_proj": (1024, 2048), "gate_proj": (3072, 1024),
                 "down_proj": (1024, 3072), "lm_head": (151936, 1024)}
@@ -419,12 +496,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="soc", choices=["soc", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config0", choices=["config0", "linear-sweep"],
-                    help="config0 (the headline line) or linear-sweep (config 1, one line per case)")
+    ap.add_argument("--workload", default="config0", choices=["config0", "linear-sweep", "config2"],
+                    help="config0 (the headline line), linear-sweep (config 1, one line per case) or config2")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.workload == "linear-sweep":
         run_linear_sweep(args)
+        return
+    if args.workload == "config2":
+        run_config2(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

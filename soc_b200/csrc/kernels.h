@@ -44,6 +44,11 @@ void launch_attention(const float* q, const Rows& rows, int splits, int hq, int 
                       const KVLayerView& kv, float* out, float* scratch, size_t scratch_floats, cudaStream_t st);
 int attention_splits(int rows, int hkv, int max_visible);
 
+// Causal attention of the n rows of one prefill chunk (row r = position start + r of
+// sequence `seq`) on tensor cores (attn_prefill.cu).  Same output layout as launch_attention.
+void launch_flash_prefill(const float* q, int n, int hq, int hkv, int head_dim, int seq, int start,
+                          const KVLayerView& kv, float* out, cudaStream_t st);
+
 void launch_argmax(const float* logits, int vocab, int ld, int rows, int* next_ids, cudaStream_t st);
 
 void launch_rmsnorm(const float* x, int rows, int n, const float* w, float eps, float* y, cudaStream_t st);

@@ -557,7 +557,17 @@ void check_device_error(soc_model* m) {
 // Run rows [0, n) (tokens/seq/pos already in m->d_tokens/d_seq/d_pos) through all layers.
 // Afterwards m->h holds the residual stream; when lm_rows > 0 the logits of rows
 // [lm_first, lm_first + lm_rows) go to m->logits and their greedy ids to m->d_next.
-void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first, int lm_rows, int splits) {
+// Rows from which a prefill chunk's attention runs on the tensor-core flash kernel
+// (default 32; SOC_B200_FLASH_MIN_ROWS overrides it, 0 disables it).
+int flash_min_rows() {
+    const char* e = std::getenv("SOC_B200_FLASH_MIN_ROWS");
+    return e && *e ? std::atoi(e) : 32;
+}
+
+// pf_seq >= 0: the rows are positions pf_start .. pf_start + n - 1 of sequence pf_seq (a
+// prefill chunk), which lets the attention use the flash kernel.
+void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first, int lm_rows, int splits,
+                  int pf_seq = -1, int pf_start = 0) {
     const Config& c = m->cfg;
     cudaStream_t st = m->ctx->stream;
     const float eps = static_cast<float>(c.eps);
@@ -576,6 +586,7 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
         tc_make_map(&a_act, m->acth, m->wfmt, n, I, I, TC_BOX_A);
     }
     int* err = m->ctx->d_err;
+    const bool flash = pf_seq >= 0 && flash_min_rows() > 0 && n >= flash_min_rows();
     for (size_t l = 0; l < c.layers; ++l) {
         const LayerW& w = m->layers[l];
         if (tc) {
@@ -587,8 +598,13 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
         launch_qk_norm_rope_kv(m->qkv, rows, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
                                w.q_norm, w.k_norm, eps, m->rope_cs, m->rope_len, kv->view(static_cast<int>(l)), m->q,
                                m->ctx->d_err, st);
-        launch_attention(m->q, rows, splits, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
-                         kv->view(static_cast<int>(l)), m->att, m->attn_scratch, m->attn_scratch_floats, st);
+        if (flash)
+            launch_flash_prefill(m->q, n, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
+                                 pf_seq, pf_start, kv->view(static_cast<int>(l)), m->att, st);
+        else
+            launch_attention(m->q, rows, splits, static_cast<int>(c.hq), static_cast<int>(c.hkv),
+                             static_cast<int>(c.hd), kv->view(static_cast<int>(l)), m->att, m->attn_scratch,
+                             m->attn_scratch_floats, st);
         if (tc) {
             launch_rows_to_half(m->wfmt, m->att, QW, n, QW, nullptr, eps, m->xa, QW, st);
             launch_gemm_tc(m->wfmt, a_att, w.tm_o, n, H, QW, m->h, H, LIN_RESIDUAL, false, err, st);
@@ -636,7 +652,7 @@ void prefill_impl(soc_model* m, soc_kv* kv, int seq, const int32_t* ids, int n, 
         SOCB_CUDA(cudaMemcpyAsync(m->d_pos, ps.data(), sizeof(int) * cn, cudaMemcpyHostToDevice, st));
         const bool last = off + cn == n;
         // (the pageable host vectors are staged by the driver before cudaMemcpyAsync returns)
-        forward_rows(m, kv, cn, start + off + cn, last ? cn - 1 : 0, last ? 1 : 0, 1);
+        forward_rows(m, kv, cn, start + off + cn, last ? cn - 1 : 0, last ? 1 : 0, 1, seq, start + off);
     }
     kv->lengths[seq] = start + n;
 }

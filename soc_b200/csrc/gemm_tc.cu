@@ -15,6 +15,7 @@
 // returns.  No load uses cluster multicast.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 
@@ -24,14 +25,23 @@
 namespace socb {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2, W_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + W_BYTES;
+constexpr int BM = 128, BN = 256, BK = 64, MAX_STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2, W_BYTES = BN * BK * 2;
+// Split mode carries the activations as hi + lo halves (x = hi + lo, both fp16/bf16) and
+// issues two MMAs per K step, which keeps about twice the input significand bits.
+template <bool SPLIT>
+struct TcCfg {
+    static constexpr int A_TILES = SPLIT ? 2 : 1;
+    static constexpr int STAGE_BYTES = A_TILES * A_BYTES + W_BYTES;
+    static constexpr int STAGES = SPLIT ? 3 : 4;
+};
+static_assert(TcCfg<true>::STAGES * TcCfg<true>::STAGE_BYTES <= MAX_STAGES * (A_BYTES + W_BYTES), "ring size");
 constexpr int TC_THREADS = 192;
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s
-constexpr size_t TC_SMEM = STAGES * STAGE_BYTES + 1024 /* barriers */ + 1024 /* alignment */;
+constexpr size_t TC_SMEM = MAX_STAGES * (A_BYTES + W_BYTES) + 1024 /* barriers */ + 1024 /* alignment */;
 
 struct TcBars {
-    unsigned long long full[STAGES], empty[STAGES], acc_full[2], acc_empty[2];
+    unsigned long long full[MAX_STAGES], empty[MAX_STAGES], acc_full[2], acc_empty[2];
     uint32_t tmem;
 };
 
@@ -128,16 +138,24 @@ template <>
 __device__ __forceinline__ __nv_bfloat16 to_w<__nv_bfloat16>(float f) { return __float2bfloat16_rn(f); }
 
 template <typename T>
-__device__ __forceinline__ void epilogue(const float (&v)[32], int row, int col, int M, int N, void* y, int ldy,
-                                         int mode, int out_half) {
+__device__ __forceinline__ void store_half(T* hi, T* lo, size_t i, float f) {
+    const T h = to_w<T>(f);
+    hi[i] = h;
+    if (lo != nullptr) lo[i] = to_w<T>(f - static_cast<float>(h));
+}
+
+template <typename T>
+__device__ __forceinline__ void epilogue(const float (&v)[32], int row, int col, int M, int N, void* y, void* y_lo,
+                                         int ldy, int mode, int out_half) {
     if (row >= M) return;
     if (mode == LIN_SWIGLU) {
         const int o = col >> 1, no = N >> 1;
         if (out_half) {
             T* yr = static_cast<T*>(y) + static_cast<size_t>(row) * ldy;
+            T* yl = y_lo ? static_cast<T*>(y_lo) + static_cast<size_t>(row) * ldy : nullptr;
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-                if (o + j < no) yr[o + j] = to_w<T>(silu_f(v[2 * j]) * v[2 * j + 1]);
+                if (o + j < no) store_half<T>(yr, yl, o + j, silu_f(v[2 * j]) * v[2 * j + 1]);
         } else {
             float* yr = static_cast<float*>(y) + static_cast<size_t>(row) * ldy;
 #pragma unroll
@@ -148,9 +166,10 @@ __device__ __forceinline__ void epilogue(const float (&v)[32], int row, int col,
     }
     if (out_half) {
         T* yr = static_cast<T*>(y) + static_cast<size_t>(row) * ldy;
+        T* yl = y_lo ? static_cast<T*>(y_lo) + static_cast<size_t>(row) * ldy : nullptr;
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-            if (col + j < N) yr[col + j] = to_w<T>(v[j]);
+            if (col + j < N) store_half<T>(yr, yl, col + j, v[j]);
         return;
     }
     float* yr = static_cast<float*>(y) + static_cast<size_t>(row) * ldy + col;
@@ -173,15 +192,21 @@ __device__ __forceinline__ void epilogue(const float (&v)[32], int row, int col,
     }
 }
 
-template <typename T>
+template <typename T, bool SPLIT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
-              void* __restrict__ y, int ldy, int mode, int out_half, int* err) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap ta_lo,
+              const __grid_constant__ CUtensorMap tw, int M, int N, int K, void* __restrict__ y,
+              void* __restrict__ y_lo, int ldy, int mode, int out_half, int ksplit, int* err) {
+    using Cfg = TcCfg<SPLIT>;
+    constexpr int STAGES = Cfg::STAGES, STAGE_BYTES = Cfg::STAGE_BYTES, W_OFF = Cfg::A_TILES * A_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     TcBars* bars = reinterpret_cast<TcBars*>(smem + STAGES * STAGE_BYTES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN, tiles = mt * nt, kbn = (K + BK - 1) / BK;
+    // Work unit u = (tile u % tiles, K slice u / tiles); with ksplit > 1 every slice writes
+    // its fp32 partial tile to y + slice * M * N (ld N) for a separate reduction.
+    const int kper = (kbn + ksplit - 1) / ksplit, units = tiles * ksplit;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -209,9 +234,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) {  // TMA producer
             unsigned it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                const int t = u % tiles, kb0 = (u / tiles) * kper, kb1 = min(kbn, kb0 + kper);
                 const int m0 = (t % mt) * BM, n0 = (t / mt) * BN;
-                for (int kb = 0; kb < kbn; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = static_cast<int>(it % STAGES);
                     if (!mbar_wait(&bars->empty[s], ((it / STAGES) & 1u) ^ 1u, err)) {
                         ok = false;
@@ -219,7 +245,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                     mbar_expect_tx(&bars->full[s], STAGE_BYTES);
                     tma_load_2d(smem + s * STAGE_BYTES, &ta, &bars->full[s], kb * BK, m0);
-                    tma_load_2d(smem + s * STAGE_BYTES + A_BYTES, &tw, &bars->full[s], kb * BK, n0);
+                    if (SPLIT) tma_load_2d(smem + s * STAGE_BYTES + A_BYTES, &ta_lo, &bars->full[s], kb * BK, m0);
+                    tma_load_2d(smem + s * STAGE_BYTES + W_OFF, &tw, &bars->full[s], kb * BK, n0);
                 }
             }
             // Let the copies already issued land before the CTA can exit (bounded).
@@ -232,22 +259,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             constexpr uint32_t idesc = f16_idesc(sizeof(T) == 2 && __is_same(T, __nv_bfloat16) ? 1u : 0u, BM, BN);
             unsigned it = 0, local = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++local) {
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+                const int kb0 = (u / tiles) * kper, kb1 = min(kbn, kb0 + kper);
                 const unsigned b = local & 1u;
                 if (!mbar_wait(&bars->acc_empty[b], ((local >> 1) & 1u) ^ 1u, err)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + b * BN;
-                for (int kb = 0; kb < kbn; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = static_cast<int>(it % STAGES);
                     if (!mbar_wait(&bars->full[s], (it / STAGES) & 1u, err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = su32(smem + s * STAGE_BYTES), w0 = a0 + A_BYTES;
+                    const uint32_t a0 = su32(smem + s * STAGE_BYTES), w0 = a0 + W_OFF;
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k)
-                        umma(d, sw128_desc(a0 + k * 32), sw128_desc(w0 + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+                    for (int k = 0; k < BK / 16; ++k) {
+                        umma(d, sw128_desc(a0 + k * 32), sw128_desc(w0 + k * 32), idesc,
+                             (kb != kb0 || k != 0) ? 1u : 0u);
+                        if (SPLIT) umma(d, sw128_desc(a0 + A_BYTES + k * 32), sw128_desc(w0 + k * 32), idesc, 1u);
+                    }
                     umma_commit(&bars->empty[s]);
                 }
                 umma_commit(&bars->acc_full[b]);
@@ -256,11 +287,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else {  // epilogue warps 2..5: TMEM lane quarter = warp % 4
         const int q = warp & 3;
         unsigned local = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+        const bool partial = ksplit > 1;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+            const int t = u % tiles;
             const unsigned b = local & 1u;
             if (!mbar_wait(&bars->acc_full[b], (local >> 1) & 1u, err)) break;
             tc_fence_after();
             const int m0 = (t % mt) * BM, n0 = (t / mt) * BN;
+            void* yy = partial ? static_cast<void*>(static_cast<float*>(y) + static_cast<size_t>(u / tiles) * M * N) : y;
             const int row = m0 + q * 32 + lane;
             const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
 #pragma unroll 1
@@ -268,7 +302,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (n0 + c >= N) break;
                 float v[32];
                 tmem_ld32(base + c, v);
-                epilogue<T>(v, row, n0 + c, M, N, y, ldy, mode, out_half);
+                if (partial)
+                    epilogue<T>(v, row, n0 + c, M, N, yy, nullptr, N, LIN_STORE, 0);
+                else
+                    epilogue<T>(v, row, n0 + c, M, N, y, y_lo, ldy, mode, out_half);
             }
             tc_fence_before();
             __syncwarp();
@@ -283,15 +320,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
-// One CTA per row: optional RMSNorm (x * (1/sqrt(mean(x^2) + eps)) * w), cast to T.
+// One CTA per row: optional RMSNorm (x * (1/sqrt(mean(x^2) + eps)) * w), cast to T; with
+// out_lo also the remainder x' - float(T(x')) cast to T.
 template <typename T>
 __global__ void __launch_bounds__(256) k_rows_to_half(const float* __restrict__ x, int ldx, int cols,
                                                       const float* __restrict__ w, float eps, T* __restrict__ out,
-                                                      int ldo) {
+                                                      T* __restrict__ out_lo, int ldo) {
     __shared__ float red[8];
     __shared__ float scale;
     const float* xr = x + static_cast<size_t>(blockIdx.x) * ldx;
     T* orow = out + static_cast<size_t>(blockIdx.x) * ldo;
+    T* lrow = out_lo ? out_lo + static_cast<size_t>(blockIdx.x) * ldo : nullptr;
     float s = 1.0f;
     if (w != nullptr) {
         float ss = 0.0f;
@@ -309,7 +348,78 @@ __global__ void __launch_bounds__(256) k_rows_to_half(const float* __restrict__ 
     }
     for (int i = threadIdx.x; i < cols; i += blockDim.x) {
         const float v = w != nullptr ? xr[i] * s * w[i] : xr[i];
-        orow[i] = to_w<T>(v);
+        store_half<T>(orow, lrow, i, v);
+    }
+}
+
+// Group-quantised [rows, cols] matrix -> T (q * scale rounded once), one 16-byte vector
+// per thread per step.
+template <int F, typename T>
+__global__ void k_dequant(const uint8_t* __restrict__ W, const __half* __restrict__ S, size_t rows, int cols,
+                          T* __restrict__ out) {
+    using C = Codec<F>;
+    const size_t vpr = static_cast<size_t>(cols) / C::EPV, total = rows * vpr;
+    const int ng = cols / C::GROUP;
+    for (size_t v = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; v < total;
+         v += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t r = v / vpr, vi = v - r * vpr;
+        const uint4 u = *reinterpret_cast<const uint4*>(W + v * 16);
+        const float sc = __half2float(S[r * ng + vi * C::EPV / C::GROUP]);
+        T* o = out + r * cols + vi * C::EPV;
+#pragma unroll
+        for (int p = 0; p < C::EPV / 8; ++p) {
+            float w8[8];
+            C::part(u, p, w8);
+            uint4 pk;
+            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const T lo = to_w<T>(w8[2 * j] * sc), hi = to_w<T>(w8[2 * j + 1] * sc);
+                pw[j] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+                        (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+            }
+            *reinterpret_cast<uint4*>(o + p * 8) = pk;
+        }
+    }
+}
+
+// Sum of the ksplit fp32 partial tiles [ksplit][M][N] followed by the GEMM epilogue; one
+// thread per pair of columns.
+template <typename T>
+__global__ void k_splitk_reduce(const float* __restrict__ ws, int ksplit, int M, int N, void* __restrict__ y,
+                                void* __restrict__ y_lo, int ldy, int mode, int out_half) {
+    const size_t pairs = static_cast<size_t>(M) * (N / 2);
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < pairs;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int row = static_cast<int>(i / (N / 2)), p = static_cast<int>(i % (N / 2));
+        float2 acc = make_float2(0.f, 0.f);
+        for (int k = 0; k < ksplit; ++k) {
+            const float2 v = *reinterpret_cast<const float2*>(ws + (static_cast<size_t>(k) * M + row) * N + 2 * p);
+            acc.x += v.x;
+            acc.y += v.y;
+        }
+        if (mode == LIN_SWIGLU) {
+            const float g = silu_f(acc.x) * acc.y;
+            if (out_half)
+                store_half<T>(static_cast<T*>(y) + static_cast<size_t>(row) * ldy,
+                              y_lo ? static_cast<T*>(y_lo) + static_cast<size_t>(row) * ldy : nullptr, p, g);
+            else
+                static_cast<float*>(y)[static_cast<size_t>(row) * ldy + p] = g;
+        } else if (out_half) {
+            T* yr = static_cast<T*>(y) + static_cast<size_t>(row) * ldy;
+            T* yl = y_lo ? static_cast<T*>(y_lo) + static_cast<size_t>(row) * ldy : nullptr;
+            store_half<T>(yr, yl, 2 * p, acc.x);
+            store_half<T>(yr, yl, 2 * p + 1, acc.y);
+        } else {
+            float* yr = static_cast<float*>(y) + static_cast<size_t>(row) * ldy + 2 * p;
+            if (mode == LIN_RESIDUAL) {
+                yr[0] += acc.x;
+                yr[1] += acc.y;
+            } else {
+                yr[0] = acc.x;
+                yr[1] = acc.y;
+            }
+        }
     }
 }
 
@@ -332,7 +442,12 @@ bool tc_available() { return encode_fn() != nullptr; }
 
 int tc_min_rows() {
     const char* e = std::getenv("SOC_B200_TC_MIN_ROWS");
-    return e && *e ? std::atoi(e) : 64;
+    return e && *e ? std::atoi(e) : 4;
+}
+
+int tc_split_max_rows() {
+    const char* e = std::getenv("SOC_B200_TC_SPLIT_MAX_ROWS");
+    return e && *e ? std::atoi(e) : 512;
 }
 
 void tc_make_map(CUtensorMap* map, const void* base, int wfmt, uint64_t rows, uint64_t cols, uint64_t ld,
@@ -352,48 +467,99 @@ void tc_make_map(CUtensorMap* map, const void* base, int wfmt, uint64_t rows, ui
     if (r != CUDA_SUCCESS) throw Error(-2, "cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r)));
 }
 
-void launch_gemm_tc(int wfmt, const CUtensorMap& a, const CUtensorMap& w, int M, int N, int K, void* y, int ldy,
-                    int mode, bool out_half, int* err, cudaStream_t st) {
+template <typename T, bool SPLIT>
+static void gemm_t(const CUtensorMap& a, const CUtensorMap& a_lo, const CUtensorMap& w, int M, int N, int K, void* y,
+                   void* y_lo, int ldy, int mode, bool out_half, int ksplit, float* ws, int* err, int grid,
+                   cudaStream_t st) {
+    static bool set = false;
+    if (!set) {
+        SOCB_CUDA(cudaFuncSetAttribute(k_gemm_tc<T, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(TC_SMEM)));
+        set = true;
+    }
+    if (ksplit <= 1) {
+        k_gemm_tc<T, SPLIT><<<grid, TC_THREADS, TC_SMEM, st>>>(a, a_lo, w, M, N, K, y, y_lo, ldy, mode,
+                                                               out_half ? 1 : 0, 1, err);
+        return;
+    }
+    k_gemm_tc<T, SPLIT><<<grid, TC_THREADS, TC_SMEM, st>>>(a, a_lo, w, M, N, K, ws, nullptr, N, LIN_STORE, 0, ksplit,
+                                                           err);
+    const size_t pairs = static_cast<size_t>(M) * (N / 2);
+    const int rgrid = static_cast<int>(std::min<size_t>((pairs + 255) / 256, 148 * 16));
+    k_splitk_reduce<T><<<rgrid, 256, 0, st>>>(ws, ksplit, M, N, y, y_lo, ldy, mode, out_half ? 1 : 0);
+}
+
+void launch_gemm_tc(int wfmt, const CUtensorMap& a, const CUtensorMap* a_lo, const CUtensorMap& w, int M, int N,
+                    int K, void* y, int ldy, int mode, bool out_half, void* y_lo, float* ws, size_t ws_floats,
+                    int* err, cudaStream_t st) {
     if (M <= 0 || N <= 0) return;
     if (K <= 0 || K % BK != 0) throw Error(-1, "tensor-core GEMM needs K to be a multiple of 64");
     if (mode == LIN_SWIGLU && N % 2 != 0) throw Error(-1, "SwiGLU GEMM needs an even number of rows");
     if (mode == LIN_RESIDUAL && out_half) throw Error(-1, "residual GEMM output is fp32");
+    if (y_lo != nullptr && !out_half) throw Error(-1, "a low-half output needs a half output");
     int dev = 0, sms = 0;
     SOCB_CUDA(cudaGetDevice(&dev));
     SOCB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    const int grid = tiles < sms ? tiles : sms;
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN), kbn = K / BK;
+    // Split K when the output tiles cannot occupy the SMs (small M): partial tiles go to
+    // the fp32 workspace and a reduction applies the epilogue.
+    int ks = 1;
+    if (ws != nullptr && tiles * 2 <= sms && N % 2 == 0) {
+        ks = std::min(kbn, sms / tiles);
+        while (ks > 1 && static_cast<size_t>(ks) * M * N > ws_floats) --ks;
+        if (ks > 1) {
+            const int kper = (kbn + ks - 1) / ks;
+            ks = (kbn + kper - 1) / kper;  // no empty slices
+        }
+    }
+    const int units = tiles * ks;
+    const int grid = units < sms ? units : sms;
+    const bool split = a_lo != nullptr;
     if (wfmt == WF_BF16) {
-        static bool set = false;
-        if (!set) {
-            SOCB_CUDA(cudaFuncSetAttribute(k_gemm_tc<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(TC_SMEM)));
-            set = true;
-        }
-        k_gemm_tc<__nv_bfloat16><<<grid, TC_THREADS, TC_SMEM, st>>>(a, w, M, N, K, y, ldy, mode, out_half ? 1 : 0, err);
+        if (split)
+            gemm_t<__nv_bfloat16, true>(a, *a_lo, w, M, N, K, y, y_lo, ldy, mode, out_half, ks, ws, err, grid, st);
+        else
+            gemm_t<__nv_bfloat16, false>(a, a, w, M, N, K, y, y_lo, ldy, mode, out_half, ks, ws, err, grid, st);
     } else if (wfmt == WF_F16) {
-        static bool set = false;
-        if (!set) {
-            SOCB_CUDA(cudaFuncSetAttribute(k_gemm_tc<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(TC_SMEM)));
-            set = true;
-        }
-        k_gemm_tc<__half><<<grid, TC_THREADS, TC_SMEM, st>>>(a, w, M, N, K, y, ldy, mode, out_half ? 1 : 0, err);
+        if (split)
+            gemm_t<__half, true>(a, *a_lo, w, M, N, K, y, y_lo, ldy, mode, out_half, ks, ws, err, grid, st);
+        else
+            gemm_t<__half, false>(a, a, w, M, N, K, y, y_lo, ldy, mode, out_half, ks, ws, err, grid, st);
     } else {
         throw Error(-1, "tensor-core GEMM supports fp16 and bf16 weights");
     }
     SOCB_CUDA(cudaGetLastError());
-    count_launches(1);
+    count_launches(ks > 1 ? 2 : 1);
 }
 
 void launch_rows_to_half(int wfmt, const float* x, int ldx, int rows, int cols, const float* norm_w, float eps,
-                         void* out, int ldo, cudaStream_t st) {
+                         void* out, void* out_lo, int ldo, cudaStream_t st) {
     if (rows <= 0) return;
     if (wfmt == WF_BF16)
         k_rows_to_half<__nv_bfloat16><<<rows, 256, 0, st>>>(x, ldx, cols, norm_w, eps,
-                                                            static_cast<__nv_bfloat16*>(out), ldo);
+                                                            static_cast<__nv_bfloat16*>(out),
+                                                            static_cast<__nv_bfloat16*>(out_lo), ldo);
     else
-        k_rows_to_half<__half><<<rows, 256, 0, st>>>(x, ldx, cols, norm_w, eps, static_cast<__half*>(out), ldo);
+        k_rows_to_half<__half><<<rows, 256, 0, st>>>(x, ldx, cols, norm_w, eps, static_cast<__half*>(out),
+                                                     static_cast<__half*>(out_lo), ldo);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+void launch_dequant(int wfmt, const void* W, const void* scales, int rows, int cols, int out_fmt, void* out,
+                    cudaStream_t st) {
+    const int grid = 148 * 8;
+    if (out_fmt != WF_F16) throw Error(-1, "dequantisation writes fp16");
+    if (wfmt == WF_I8G64)
+        k_dequant<WF_I8G64, __half><<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(W),
+                                                          static_cast<const __half*>(scales), rows, cols,
+                                                          static_cast<__half*>(out));
+    else if (wfmt == WF_I4G32)
+        k_dequant<WF_I4G32, __half><<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(W),
+                                                          static_cast<const __half*>(scales), rows, cols,
+                                                          static_cast<__half*>(out));
+    else
+        throw Error(-1, "dequantisation needs a group-quantised format");
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }

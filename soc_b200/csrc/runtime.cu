@@ -7,6 +7,7 @@
 //   prefill / decode / generate <-> GenerationContext            (Mac/gpu/src/runtime/generation_context.cpp)
 #include <sys/stat.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -380,8 +381,13 @@ struct soc_ctx {
     cudaStream_t stream = nullptr;
     int sm_count = 0;
     int* d_err = nullptr;
-    void* lin_scratch = nullptr;  // fp16/bf16 copy of soc_b200_linear's input rows (tensor-core path)
+    void* lin_scratch = nullptr;  // soc_b200_linear tensor-core path: input rows (hi, lo) + fp16 weights
     size_t lin_scratch_bytes = 0;
+    float* gemm_ws = nullptr;     // split-K partial tiles of the tensor-core GEMM (TC_WS_FLOATS)
+    float* ws() {
+        if (!gemm_ws) SOCB_CUDA(cudaMalloc(&gemm_ws, TC_WS_FLOATS * sizeof(float)));
+        return gemm_ws;
+    }
 };
 
 struct LayerW {
@@ -412,9 +418,13 @@ struct soc_model {
     int ws_rows = 0;
     float *h = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
     int *d_tokens = nullptr, *d_seq = nullptr, *d_pos = nullptr, *d_next = nullptr;
-    void* xa = nullptr;    // [ws_rows, max(hidden, q width)] fp16/bf16 GEMM input rows
-    void* acth = nullptr;  // [ws_rows, inter] fp16/bf16 SwiGLU output (down_proj input)
-    bool tc_ok = false;    // tensor-core GEMM usable for this model's linears
+    // tensor-core GEMM path (gemm_tc.cu)
+    bool tc_ok = false;
+    int gfmt = WF_F16;                         // GEMM element type (fp16 for fp16 and quantised models)
+    void *xa = nullptr, *xa_lo = nullptr;      // [ws_rows, max(hidden, q width)] GEMM input rows (hi, lo)
+    void *acth = nullptr, *acth_lo = nullptr;  // [ws_rows, inter] SwiGLU output = down_proj input (hi, lo)
+    void* wdq = nullptr;                       // fp16 expansion of one quantised matrix (quantised models)
+    CUtensorMap tm_dq_qkv{}, tm_dq_o{}, tm_dq_gu{}, tm_dq_d{};  // descriptors over wdq, one per shape
     float* logits = nullptr;
     int logits_rows = 0;
     float* attn_scratch = nullptr;
@@ -520,10 +530,11 @@ void ensure_workspace(soc_model* m, int rows) {
     m->d_pos = static_cast<int*>(m->dmalloc(sizeof(int) * r));
     m->d_next = static_cast<int*>(m->dmalloc(sizeof(int) * r));
     if (m->tc_ok) {
-        m->dfree(m->xa);
-        m->dfree(m->acth);
+        for (void* p : {m->xa, m->xa_lo, m->acth, m->acth_lo}) m->dfree(p);
         m->xa = m->dmalloc(2 * static_cast<size_t>(r) * std::max(c.hidden, c.hq * c.hd));
+        m->xa_lo = m->dmalloc(2 * static_cast<size_t>(r) * std::max(c.hidden, c.hq * c.hd));
         m->acth = m->dmalloc(2 * static_cast<size_t>(r) * c.inter);
+        m->acth_lo = m->dmalloc(2 * static_cast<size_t>(r) * c.inter);
     }
     m->ws_rows = r;
 }
@@ -577,21 +588,41 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
     if (splits < 1) splits = attention_splits(n, static_cast<int>(c.hkv), max_visible);
     if (splits > 1) ensure_attn_scratch(m, static_cast<size_t>(n) * c.hq * splits * (c.hd + 2));
     launch_embed(m->efmt, m->embed, H, static_cast<int>(c.vocab), m->d_tokens, n, m->h, m->ctx->d_err, st);
-    // Tensor-core GEMMs for the block linears once there are enough rows to fill a tile.
-    const bool tc = m->tc_ok && tc_min_rows() > 0 && n >= tc_min_rows();
-    CUtensorMap a_h{}, a_att{}, a_act{};
+    // Tensor-core GEMMs for the block linears once there are enough rows (group-quantised
+    // weights are first expanded to fp16, one matrix at a time, into m->wdq).
+    const bool quant = m->wfmt == WF_I8G64 || m->wfmt == WF_I4G32;
+    const int tmin = tc_min_rows();
+    const bool tc = m->tc_ok && tmin > 0 && n >= (quant ? 4 * tmin : tmin);
+    const bool split = n <= tc_split_max_rows();
+    const int gf = m->gfmt;
+    CUtensorMap a_h{}, a_att{}, a_act{}, a_h_lo{}, a_att_lo{}, a_act_lo{};
     if (tc) {
-        tc_make_map(&a_h, m->xa, m->wfmt, n, H, H, TC_BOX_A);
-        tc_make_map(&a_att, m->xa, m->wfmt, n, QW, QW, TC_BOX_A);
-        tc_make_map(&a_act, m->acth, m->wfmt, n, I, I, TC_BOX_A);
+        tc_make_map(&a_h, m->xa, gf, n, H, H, TC_BOX_A);
+        tc_make_map(&a_att, m->xa, gf, n, QW, QW, TC_BOX_A);
+        tc_make_map(&a_act, m->acth, gf, n, I, I, TC_BOX_A);
+        if (split) {
+            tc_make_map(&a_h_lo, m->xa_lo, gf, n, H, H, TC_BOX_A);
+            tc_make_map(&a_att_lo, m->xa_lo, gf, n, QW, QW, TC_BOX_A);
+            tc_make_map(&a_act_lo, m->acth_lo, gf, n, I, I, TC_BOX_A);
+        }
     }
+    void* xlo = split ? m->xa_lo : nullptr;
+    float* gws = tc ? m->ctx->ws() : nullptr;
+    // Weight operand of one linear: its own descriptor, or the fp16 expansion of a quantised matrix.
+    auto wmap = [&](const CUtensorMap& own, const void* w, const void* sc, int rows_w, int cols_w,
+                    const CUtensorMap& dq) -> const CUtensorMap& {
+        if (!quant) return own;
+        launch_dequant(m->wfmt, w, sc, rows_w, cols_w, WF_F16, m->wdq, st);
+        return dq;
+    };
     int* err = m->ctx->d_err;
     const bool flash = pf_seq >= 0 && flash_min_rows() > 0 && n >= flash_min_rows();
     for (size_t l = 0; l < c.layers; ++l) {
         const LayerW& w = m->layers[l];
         if (tc) {
-            launch_rows_to_half(m->wfmt, m->h, H, n, H, w.in_norm, eps, m->xa, H, st);
-            launch_gemm_tc(m->wfmt, a_h, w.tm_qkv, n, QKV, H, m->qkv, QKV, LIN_STORE, false, err, st);
+            launch_rows_to_half(gf, m->h, H, n, H, w.in_norm, eps, m->xa, xlo, H, st);
+            launch_gemm_tc(gf, a_h, split ? &a_h_lo : nullptr, wmap(w.tm_qkv, w.wqkv, w.sqkv, QKV, H, m->tm_dq_qkv),
+                           n, QKV, H, m->qkv, QKV, LIN_STORE, false, nullptr, gws, TC_WS_FLOATS, err, st);
         } else {
             launch_linear(m->wfmt, w.wqkv, w.sqkv, QKV, H, m->h, H, n, w.in_norm, eps, m->qkv, QKV, LIN_STORE, st);
         }
@@ -606,11 +637,15 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
                              static_cast<int>(c.hd), kv->view(static_cast<int>(l)), m->att, m->attn_scratch,
                              m->attn_scratch_floats, st);
         if (tc) {
-            launch_rows_to_half(m->wfmt, m->att, QW, n, QW, nullptr, eps, m->xa, QW, st);
-            launch_gemm_tc(m->wfmt, a_att, w.tm_o, n, H, QW, m->h, H, LIN_RESIDUAL, false, err, st);
-            launch_rows_to_half(m->wfmt, m->h, H, n, H, w.post_norm, eps, m->xa, H, st);
-            launch_gemm_tc(m->wfmt, a_h, w.tm_gu, n, 2 * I, H, m->acth, I, LIN_SWIGLU, true, err, st);
-            launch_gemm_tc(m->wfmt, a_act, w.tm_d, n, H, I, m->h, H, LIN_RESIDUAL, false, err, st);
+            launch_rows_to_half(gf, m->att, QW, n, QW, nullptr, eps, m->xa, xlo, QW, st);
+            launch_gemm_tc(gf, a_att, split ? &a_att_lo : nullptr, wmap(w.tm_o, w.wo, w.so, H, QW, m->tm_dq_o), n, H,
+                           QW, m->h, H, LIN_RESIDUAL, false, nullptr, gws, TC_WS_FLOATS, err, st);
+            launch_rows_to_half(gf, m->h, H, n, H, w.post_norm, eps, m->xa, xlo, H, st);
+            launch_gemm_tc(gf, a_h, split ? &a_h_lo : nullptr, wmap(w.tm_gu, w.wgu, w.sgu, 2 * I, H, m->tm_dq_gu), n,
+                           2 * I, H, m->acth, I, LIN_SWIGLU, true, split ? m->acth_lo : nullptr, gws, TC_WS_FLOATS,
+                           err, st);
+            launch_gemm_tc(gf, a_act, split ? &a_act_lo : nullptr, wmap(w.tm_d, w.wd, w.sd, H, I, m->tm_dq_d), n, H, I,
+                           m->h, H, LIN_RESIDUAL, false, nullptr, gws, TC_WS_FLOATS, err, st);
         } else {
             launch_linear(m->wfmt, w.wo, w.so, H, QW, m->att, QW, n, nullptr, eps, m->h, H, LIN_RESIDUAL, st);
             launch_linear(m->wfmt, w.wgu, w.sgu, 2 * I, H, m->h, H, n, w.post_norm, eps, m->act, I, LIN_SWIGLU, st);
@@ -839,6 +874,7 @@ void soc_b200_close(soc_ctx* ctx) {
     cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->d_err);
     if (ctx->lin_scratch) cudaFree(ctx->lin_scratch);
+    if (ctx->gemm_ws) cudaFree(ctx->gemm_ws);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
 }
@@ -965,15 +1001,24 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
             upload_rows({prepare_matrix(man, p + "mlp.down_proj.weight", H, I, fmt)}, {H}, I, false, &w.wd, &w.sd);
         }
         m->final_norm = upload_norm("model.norm.weight", H);
-        // TMA descriptors of the block linears for the tensor-core GEMM.
-        m->tc_ok = (fmt == WF_F16 || fmt == WF_BF16) && tc_available();
-        if (m->tc_ok) {
+        // TMA descriptors of the block linears for the tensor-core GEMM (for quantised
+        // models: of the fp16 expansion buffer, one per matrix shape).
+        m->tc_ok = tc_available();
+        m->gfmt = fmt == WF_BF16 ? WF_BF16 : WF_F16;
+        if (m->tc_ok && !quant) {
             for (auto& w : m->layers) {
                 tc_make_map(&w.tm_qkv, w.wqkv, fmt, QW + 2 * KW, H, H, TC_BOX_W);
                 tc_make_map(&w.tm_o, w.wo, fmt, H, QW, QW, TC_BOX_W);
                 tc_make_map(&w.tm_gu, w.wgu, fmt, 2 * I, H, H, TC_BOX_W);
                 tc_make_map(&w.tm_d, w.wd, fmt, H, I, I, TC_BOX_W);
             }
+        } else if (m->tc_ok) {
+            const size_t most = std::max({(QW + 2 * KW) * H, H * QW, 2 * I * H, H * I});
+            m->wdq = m->dmalloc(most * 2);
+            tc_make_map(&m->tm_dq_qkv, m->wdq, WF_F16, QW + 2 * KW, H, H, TC_BOX_W);
+            tc_make_map(&m->tm_dq_o, m->wdq, WF_F16, H, QW, QW, TC_BOX_W);
+            tc_make_map(&m->tm_dq_gu, m->wdq, WF_F16, 2 * I, H, H, TC_BOX_W);
+            tc_make_map(&m->tm_dq_d, m->wdq, WF_F16, H, I, I, TC_BOX_W);
         }
         if (c.tied) {
             m->lm_head = m->embed;
@@ -1326,14 +1371,21 @@ int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* 
                                                                    : -1;
         if (f < 0) throw Error(SOC_B200_ERR_INVALID, "linear: weight format not supported by this build");
         cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-        const bool tc = (f == WF_F16 || f == WF_BF16) && tc_min_rows() > 0 && rows >= tc_min_rows() &&
-                        in_features % 64 == 0 && tc_available();
+        const bool quant = f == WF_I8G64 || f == WF_I4G32;
+        const int tmin = tc_min_rows();
+        const bool tc = tmin > 0 && rows >= (quant ? 4 * tmin : tmin) && in_features % 64 == 0 && tc_available();
         if (!tc) {
             launch_linear(f, w, scales, out_features, in_features, x, in_features, rows, nullptr, 0.0f, y,
                           out_features, LIN_STORE, st);
             return;
         }
-        const size_t need = 2 * static_cast<size_t>(rows) * in_features;
+        if (quant && scales == nullptr) throw Error(SOC_B200_ERR_INVALID, "linear: group-quantised weights need scales");
+        // scratch: input rows hi | lo (GEMM type), then the fp16 expansion of quantised weights
+        const int gf = f == WF_BF16 ? WF_BF16 : WF_F16;
+        const bool split = rows <= tc_split_max_rows();
+        const size_t xbytes = 2 * static_cast<size_t>(rows) * in_features;
+        const size_t xoff = (xbytes + 255) / 256 * 256;
+        const size_t need = 2 * xoff + (quant ? 2 * static_cast<size_t>(out_features) * in_features : 0);
         if (need > ctx->lin_scratch_bytes) {
             SOCB_CUDA(cudaStreamSynchronize(st));
             if (ctx->lin_scratch) SOCB_CUDA(cudaFree(ctx->lin_scratch));
@@ -1342,11 +1394,21 @@ int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* 
             SOCB_CUDA(cudaMalloc(&ctx->lin_scratch, need));
             ctx->lin_scratch_bytes = need;
         }
-        CUtensorMap ta{}, tw{};
-        tc_make_map(&ta, ctx->lin_scratch, f, rows, in_features, in_features, TC_BOX_A);
-        tc_make_map(&tw, w, f, out_features, in_features, in_features, TC_BOX_W);
-        launch_rows_to_half(f, x, in_features, rows, in_features, nullptr, 0.0f, ctx->lin_scratch, in_features, st);
-        launch_gemm_tc(f, ta, tw, rows, out_features, in_features, y, out_features, LIN_STORE, false, ctx->d_err, st);
+        char* base = static_cast<char*>(ctx->lin_scratch);
+        void *xh = base, *xl = base + xoff, *wq = base + 2 * xoff;
+        const void* wsrc = w;
+        if (quant) {
+            launch_dequant(f, w, scales, out_features, in_features, WF_F16, wq, st);
+            wsrc = wq;
+        }
+        CUtensorMap ta{}, tl{}, tw{};
+        tc_make_map(&ta, xh, gf, rows, in_features, in_features, TC_BOX_A);
+        if (split) tc_make_map(&tl, xl, gf, rows, in_features, in_features, TC_BOX_A);
+        tc_make_map(&tw, wsrc, gf, out_features, in_features, in_features, TC_BOX_W);
+        launch_rows_to_half(gf, x, in_features, rows, in_features, nullptr, 0.0f, xh, split ? xl : nullptr,
+                            in_features, st);
+        launch_gemm_tc(gf, ta, split ? &tl : nullptr, tw, rows, out_features, in_features, y, out_features, LIN_STORE,
+                       false, nullptr, ctx->ws(), TC_WS_FLOATS, ctx->d_err, st);
     });
 }
 

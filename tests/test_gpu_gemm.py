@@ -1,9 +1,10 @@
 """Tensor-core (tcgen05) GEMM of the prefill / batched-row linears.
 
-soc_b200_linear and the forward switch to the tcgen05 kernel from 64 rows (fp16/bf16
-weights).  Its input rows are rounded to the weight type (fp16: 11-bit, bf16: 8-bit
-significand) and accumulated in fp32, so the kernel cases compare against an fp64 product
-with tolerances scaled by that rounding; the model cases compare prefill logits with the
+soc_b200_linear and the forward switch to the tcgen05 kernel from 4 rows (fp16/bf16
+weights; 16 rows for int8/int4, expanded to fp16 first).  Up to 512 rows the input rows are
+carried as hi + lo halves (fp32-level products); above that they are rounded once to the
+weight type (fp16: 11-bit, bf16: 8-bit significand) and accumulated in fp32, so the kernel
+cases compare against an fp64 product with tolerances scaled by that rounding; the model cases compare prefill logits with the
 CPU oracle at the 2e-2 logit tolerance and greedy ids exactly.
 """
 import os
@@ -19,7 +20,7 @@ pytestmark = pytest.mark.gpu
 LOGIT_TOL = 2e-2
 
 
-@pytest.mark.parametrize("rows", [64, 100, 256, 1000])
+@pytest.mark.parametrize("rows", [4, 16, 64, 100, 256, 1000])
 @pytest.mark.parametrize("shape", [(2048, 1024), (1024, 2048), (6144, 1024), (1024, 3072), (1000, 1024), (4096, 4096)],
                          ids=["q", "o", "gate_up", "down", "ragged_n", "h4096"])
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
@@ -42,10 +43,14 @@ def test_tc_linear_against_fp64(gpu_ctx, dtype, rows, shape):
     torch.cuda.synchronize()
     yc = y.double().cpu()
     assert torch.isfinite(yc).all()
-    # fp32 accumulation of exactly-rounded products
-    assert (yc - ref_r).abs().max().item() <= 2e-5 * in_f ** 0.5
-    rel = 2.0 ** -11 if dtype == "fp16" else 2.0 ** -8
-    assert (yc - ref).abs().max().item() <= 6 * rel * 0.02 * in_f ** 0.5 + 2e-5 * in_f ** 0.5
+    if rows <= 512:
+        # hi + lo input halves: fp32-level agreement with the exact product
+        assert (yc - ref).abs().max().item() <= 2e-5 * in_f ** 0.5
+    else:
+        # one rounded half per input: fp32 accumulation of exactly-rounded products
+        assert (yc - ref_r).abs().max().item() <= 2e-5 * in_f ** 0.5
+        rel = 2.0 ** -11 if dtype == "fp16" else 2.0 ** -8
+        assert (yc - ref).abs().max().item() <= 6 * rel * 0.02 * in_f ** 0.5 + 2e-5 * in_f ** 0.5
 
 
 CASES = {

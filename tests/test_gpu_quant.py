@@ -124,3 +124,22 @@ def test_load_time_quantisation_equals_exported_bundle(gpu_ctx, make_bundle, tmp
         m_.free()
     a.free()
     b.free()
+
+
+@pytest.mark.parametrize("quant", sorted(FORMATS))
+def test_quantized_prefill_tensor_core_path(qmodels, quant):
+    """40 prompt rows (>= 16): the quantised linears run as an fp16 expansion of each
+    matrix feeding the tensor-core GEMM.  Logits vs the oracle, then greedy decode."""
+    p, m = qmodels("qwen06_shape_2layer", quant)
+    prompt = np.random.default_rng(31).integers(0, QWEN3_0_6B["vocab_size"], 40).astype(np.int32)
+    om = O.OracleModel(p, 128)
+    ref = om.forward(prompt, 0, last_only=True)[0]
+    kv = R.KVCache(m, 1, 128)
+    lg, nid = m.forward_logits_cached(kv, 0, prompt)
+    assert np.abs(lg - ref).max() <= LOGIT_TOL
+    assert nid == O.argmax(ref)
+    kv.free()
+    toks, _ = O.OracleModel(p, 128).generate(prompt, 8)
+    kv = R.KVCache(m, 1, 128)
+    assert m.generate(kv, 0, prompt, 8) == toks
+    kv.free()

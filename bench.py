@@ -414,6 +414,111 @@ def run_config2(args):
     ctx.close()
 
 
+# ------------------------------------------------------------------- config 3
+C3_SEQS, C3_STEPS = 256, 64
+
+
+def config3_contexts() -> np.ndarray:
+    return np.random.default_rng(4).integers(128, 4097, C3_SEQS)
+
+
+def run_config3(args, rank, world, local):
+    """Config 3: batched ragged decode, Qwen3-0.6B with int8 group-64 linears (the config-0
+    fp16 weights quantised at load time; embeddings, norms and the tied lm_head stay fp16).
+    256 sequences with contexts U[128, 4096] (seed 4) of seeded ~N(0, 1) fp16 KV written on
+    the device (soc_b200_kv_fill_random, seed 4000 + sequence index), sequences split evenly
+    over the ranks, `steps` greedy decode steps of every local sequence per timed run (one
+    soc_b200_decode call per step: host ids in, host ids out).  Prints one JSON line (rank 0)
+    with the max-over-ranks time."""
+    import torch
+    import torch.distributed as dist
+    from soc_b200 import runtime as R
+    from soc_b200.bundle import QWEN3_0_6B
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    cfg = QWEN3_0_6B
+    p = config0_bundle(rank, world, barrier)
+    ctx = R.Context(local)
+    model = R.Model(ctx, p, weight_format=R.WEIGHTS_INT8_G64)
+    ctxs = config3_contexts()
+    per = C3_SEQS // world
+    mine = list(range(rank * per, (rank + 1) * per if rank < world - 1 else C3_SEQS))
+    n = len(mine)
+    steps, warmup = args.steps, max(args.warmup, 3)
+    cap = int(sum(-(-(int(ctxs[g]) + steps + warmup + 1) // 16) * 16 for g in mine))
+    kv = R.KVCache(model, n, cap)
+    for i, g in enumerate(mine):
+        kv.fill_random(i, int(ctxs[g]), 4000 + g)
+    ctx.synchronize()
+    toks = np.random.default_rng(5).integers(0, cfg["vocab_size"], C3_SEQS).astype(np.int32)[mine]
+    seqs = list(range(n))
+    for _ in range(warmup):
+        _, toks = model.decode(kv, seqs, toks, want_logits=False)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx_before = np.array([kv.length(i) for i in seqs])
+    barrier()
+    ctx.synchronize()
+    launches0 = R.kernel_launches()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            _, toks = model.decode(kv, seqs, toks, want_logits=False)
+        e1.record(stream)
+        ctx.synchronize()
+        wall = time.perf_counter() - t0
+    launches = R.kernel_launches() - launches0
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms, wall], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, wall = t.tolist()
+    # algorithmic bytes per step on this rank: int8 linears + fp16 lm_head + the KV read
+    H, I, L, D = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["head_dim"]
+    hq, hkv, V = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["vocab_size"]
+    lin = L * (H * (hq + 2 * hkv) * D + H * hq * D + 3 * H * I)
+    kv_tok = L * 2 * hkv * D * 2
+    mean_ctx = float(np.mean([c + 1 + i for c in ctx_before for i in range(steps)])) if n else 0.0
+    bytes_step = lin * (1 + 2 / 64) + 2 * V * H + kv_tok * mean_ctx * n
+    achieved = bytes_step * steps / (ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": C3_SEQS * steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "i8w-f32a", "data": "synthetic", "impl": "soc_b200",
+            "config": {"workload": "config3: 256 sequences, contexts U[128,4096] seed 4, random N(0,1) fp16 KV, "
+                                   "Qwen3-0.6B int8 g64 linears, batched greedy decode",
+                       "global_batch": C3_SEQS, "seq_len": int(ctxs.max()) + steps + warmup,
+                       "parallelism": f"sequence-sharded{world}",
+                       "l2": "KV 63 GB per step > 126 MB L2; no flush needed"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"], "traffic": None,
+                         "unit_of_work": "one batched decode step of this rank's sequences",
+                         "algorithmic_bytes_per_step_rank0": bytes_step},
+            "e2e": {"value": C3_SEQS * steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 8 * n,
+                    "d2h_bytes_per_step": 4 * n},
+            "gpu_launches": int(launches), "clocks": clk.summary(),
+        }
+    kv.free()
+    model.free()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
 # ------------------------------------------------------------- config 1 sweep
 SWEEP_SHAPES = {"q_proj": (2048, 1024), "k_proj": (1024, 1024), "o_proj": (1024, 2048), "gate_proj": (3072, 1024),
                 "down_proj": (1024, 3072), "lm_head": (151936, 1024)}
@@ -496,8 +601,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="soc", choices=["soc", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config0", choices=["config0", "linear-sweep", "config2"],
-                    help="config0 (the headline line), linear-sweep (config 1, one line per case) or config2")
+    ap.add_argument("--workload", default="config0", choices=["config0", "linear-sweep", "config2", "config3"],
+                    help="config0 (the headline line), linear-sweep (config 1, one line per case), config2, "
+                         "config3 (batched ragged decode, sequence-sharded over --gpus)")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.workload == "linear-sweep":
@@ -505,6 +611,9 @@ def main():
         return
     if args.workload == "config2":
         run_config2(args)
+        return
+    if args.workload == "config3":
+        run_config3(args, rank, world, local)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -88,6 +88,7 @@ SOC_B200_API int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, i
 SOC_B200_API int soc_b200_model_info(const soc_model* model, soc_model_info* out);
 SOC_B200_API void soc_b200_free_model(soc_model* model);
 
+
 /* Paged fp16 KV cache for up to max_seqs sequences and max_tokens cached
  * tokens in total, page_tokens per page (16).  Replaces TensorKVCache
  * (Mac/cpu/src/kv_cache.cpp:20-44) and the Metal KVCache::CreateShared. */
@@ -103,6 +104,15 @@ SOC_B200_API int soc_b200_kv_read(soc_kv* kv, int seq, int layer, int start, int
 /* Write positions [start, end) of one layer from float32 host rows (rounded to
  * fp16); extends the sequence length to `end` (TensorKVCache::Write, kv_cache.cpp:50-78). */
 SOC_B200_API int soc_b200_kv_write(soc_kv* kv, int seq, int layer, int start, int end, const float* k, const float* v);
+
+/* Benchmark and test helper; it has no counterpart in the reference.  Replaces sequence
+ * `seq` of the cache by n_tokens positions whose K and V (every layer and kv head) are
+ * seeded pseudo-random values of about N(0, 1) rounded to fp16: element e = (pos * kv_heads
+ * + head) * head_dim + d of stream s = (seq * layers + layer) * 2 + (0 for K, 1 for V) is
+ * sum / 65536 - 6, where sum adds the twelve 16-bit fields of splitmix64 outputs at
+ * x, x + 1, x + 2 with x = seed + s * 0xD1B54A32D192ED03 + 3 e (all arithmetic mod 2^64).
+ * Queued on the context stream without a host synchronisation. */
+SOC_B200_API int soc_b200_kv_fill_random(soc_kv* kv, int seq, int n_tokens, unsigned long long seed);
 
 /* Append n tokens to sequence `seq` at its current length and run them
  * through the model (QwenCausalLM::ForwardLogitsCached with position_offset =

@@ -241,6 +241,16 @@ class OracleModel:
             raise ValueError("kv cache write position out of range")
         return out
 
+    def set_cache(self, layer, k, v):
+        """Overwrite positions [0, S) of `layer` with [S, Hkv, D] K and V (TensorKVCache::Write
+        of a whole prefix, kv_cache.cpp:50-80); set_length() then makes them visible."""
+        S = k.shape[0]
+        self.kc[layer, :, :S, :] = np.asarray(k, dtype=np.float32).transpose(1, 0, 2)
+        self.vc[layer, :, :S, :] = np.asarray(v, dtype=np.float32).transpose(1, 0, 2)
+
+    def set_length(self, n):
+        self.s.length = int(n)
+
     def kv_read(self, layer, start, end):
         """[S, Hkv, D] float32 K and V, like TensorKVCache::Read."""
         if end > self.length or start > end:
@@ -342,3 +352,27 @@ def ref_attention(q, k, v, prefix):
 
 def host_cores() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count() or 1
+
+
+def _mix64(x: np.ndarray) -> np.ndarray:
+    """splitmix64 output function of x + 0x9E3779B97F4A7C15 (uint64, wrapping)."""
+    z = x + np.uint64(0x9E3779B97F4A7C15)
+    z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+    z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return z ^ (z >> np.uint64(31))
+
+
+def kv_random(seed: int, seq: int, layer: int, kind: int, n_tokens: int, hkv: int, hd: int, layers: int) -> np.ndarray:
+    """The seeded K (kind 0) or V (kind 1) contents that soc_b200_kv_fill_random writes for
+    one layer of one sequence, [n_tokens, hkv, hd] float16 (restated for the parity tests)."""
+    with np.errstate(over="ignore"):
+        stream = np.uint64((seq * layers + layer) * 2 + kind)
+        e = np.arange(n_tokens * hkv * hd, dtype=np.uint64)
+        x = np.uint64(seed) + stream * np.uint64(0xD1B54A32D192ED03) + np.uint64(3) * e
+        total = np.zeros(e.shape, dtype=np.uint64)
+        for w in range(3):
+            z = _mix64(x + np.uint64(w))
+            for sh in (0, 16, 32, 48):
+                total += (z >> np.uint64(sh)) & np.uint64(0xFFFF)
+    val = total.astype(np.float32) * np.float32(1.0 / 65536.0) - np.float32(6.0)
+    return val.astype(np.float16).reshape(n_tokens, hkv, hd)

@@ -571,6 +571,68 @@ void launch_attention(const float* q, const Rows& rows, int splits, int hq, int 
     count_launches(splits > 1 ? 2 : 1);
 }
 
+// ------------------------------------------------------- seeded random KV contents
+// splitmix64 output function (Steele, Lea and Flood, 2014) applied to x + 0x9E3779B97F4A7C15.
+__device__ __forceinline__ unsigned long long mix64(unsigned long long x) {
+    unsigned long long z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Element e = (pos * hkv + head) * D + d of stream (seq * L + layer) * 2 + kind (0 = K,
+// 1 = V): the twelve 16-bit fields of mix64(x), mix64(x + 1), mix64(x + 2) with
+// x = seed + stream * 0xD1B54A32D192ED03 + 3 e are summed and mapped to sum / 65536 - 6
+// (Irwin-Hall approximation of N(0, 1), exact in fp32) and rounded to fp16.
+__global__ void k_kv_fill_random(__half* __restrict__ kpool, __half* __restrict__ vpool, size_t layer_stride,
+                                 const int* __restrict__ pages, int page_tokens, int hkv, int D, int L, int n_tokens,
+                                 int seq, unsigned long long seed) {
+    const int d8n = D / 8;
+    const size_t total = static_cast<size_t>(L) * 2 * n_tokens * hkv * d8n;
+    for (size_t v = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; v < total;
+         v += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        size_t r = v;
+        const int d8 = static_cast<int>(r % d8n);
+        r /= d8n;
+        const int head = static_cast<int>(r % hkv);
+        r /= hkv;
+        const int pos = static_cast<int>(r % n_tokens);
+        r /= n_tokens;
+        const int kind = static_cast<int>(r % 2);
+        const int layer = static_cast<int>(r / 2);
+        const unsigned long long stream = (static_cast<unsigned long long>(seq) * L + layer) * 2 + kind;
+        uint32_t packed[4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const unsigned long long e = (static_cast<unsigned long long>(pos) * hkv + head) * D + d8 * 8 + j;
+            const unsigned long long x = seed + stream * 0xD1B54A32D192ED03ull + 3ull * e;
+            unsigned sum = 0;
+#pragma unroll
+            for (int w = 0; w < 3; ++w) {
+                const unsigned long long z = mix64(x + w);
+                sum += static_cast<unsigned>(z & 0xFFFF) + static_cast<unsigned>((z >> 16) & 0xFFFF) +
+                       static_cast<unsigned>((z >> 32) & 0xFFFF) + static_cast<unsigned>(z >> 48);
+            }
+            const __half h = __float2half_rn(static_cast<float>(sum) * (1.0f / 65536.0f) - 6.0f);
+            const uint32_t hb = *reinterpret_cast<const uint16_t*>(&h);
+            packed[j >> 1] = (j & 1) ? (packed[j >> 1] | (hb << 16)) : hb;
+        }
+        const int page = pages[pos / page_tokens];
+        __half* pool = (kind == 0 ? kpool : vpool) + layer * layer_stride;
+        __half* dst = pool + ((static_cast<size_t>(page) * hkv + head) * page_tokens + pos % page_tokens) * D + d8 * 8;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+}
+
+void launch_kv_fill_random(__half* kpool, __half* vpool, size_t layer_stride, const int* pages, int page_tokens,
+                           int hkv, int D, int L, int n_tokens, int seq, unsigned long long seed, cudaStream_t st) {
+    if (n_tokens <= 0) return;
+    k_kv_fill_random<<<148 * 16, 256, 0, st>>>(kpool, vpool, layer_stride, pages, page_tokens, hkv, D, L, n_tokens,
+                                               seq, seed);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
 // ------------------------------------------------------------------------ argmax
 // Greedy pick per row: maximum logit, lowest index on ties (the reference's
 // partial_sort with top_k = 1 keeps the first strict maximum).  NaNs never win.

@@ -49,6 +49,11 @@ int attention_splits(int rows, int hkv, int max_visible);
 void launch_flash_prefill(const float* q, int n, int hq, int hkv, int head_dim, int seq, int start,
                           const KVLayerView& kv, float* out, cudaStream_t st);
 
+// Seeded pseudo-random K and V (about N(0, 1), fp16) for positions [0, n_tokens) of sequence
+// `seq` in every layer; `pages` = that sequence's page-table row.
+void launch_kv_fill_random(__half* kpool, __half* vpool, size_t layer_stride, const int* pages, int page_tokens,
+                           int hkv, int D, int L, int n_tokens, int seq, unsigned long long seed, cudaStream_t st);
+
 void launch_argmax(const float* logits, int vocab, int ld, int rows, int* next_ids, cudaStream_t st);
 
 void launch_rmsnorm(const float* x, int rows, int n, const float* w, float eps, float* y, cudaStream_t st);

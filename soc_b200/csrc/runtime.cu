@@ -1198,6 +1198,23 @@ int soc_b200_kv_read(soc_kv* kv, int seq, int layer, int start, int end, float* 
     });
 }
 
+int soc_b200_kv_fill_random(soc_kv* kv, int seq, int n_tokens, unsigned long long seed) {
+    if (!kv) return fail(SOC_B200_ERR_INVALID, "null argument");
+    return guarded([&] {
+        soc_model* m = kv->m;
+        kv->check_seq(seq);
+        if (n_tokens < 0) throw Error(SOC_B200_ERR_INVALID, "kv fill length must not be negative");
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        cudaStream_t st = m->ctx->stream;
+        kv->reset(seq);
+        kv->reserve(seq, n_tokens, st);
+        launch_kv_fill_random(kv->k, kv->v, kv->layer_stride(), kv->d_page_table + static_cast<size_t>(seq) * kv->max_pages,
+                              kv->page_tokens, static_cast<int>(m->cfg.hkv), static_cast<int>(m->cfg.hd),
+                              static_cast<int>(m->cfg.layers), n_tokens, seq, seed, st);
+        kv->lengths[seq] = n_tokens;
+    });
+}
+
 int soc_b200_kv_write(soc_kv* kv, int seq, int layer, int start, int end, const float* k, const float* v) {
     if (!kv || !k || !v) return fail(SOC_B200_ERR_INVALID, "null argument");
     return guarded([&] {

@@ -67,6 +67,7 @@ _SIGNATURES = {
     "soc_b200_kv_length": (C.c_int, [_VP, C.c_int]),
     "soc_b200_kv_read": (C.c_int, [_VP, C.c_int, C.c_int, C.c_int, C.c_int, _FP, _FP]),
     "soc_b200_kv_write": (C.c_int, [_VP, C.c_int, C.c_int, C.c_int, C.c_int, _FP, _FP]),
+    "soc_b200_kv_fill_random": (C.c_int, [_VP, C.c_int, C.c_int, C.c_ulonglong]),
     "soc_b200_prefill": (C.c_int, [_VP, _VP, C.c_int, _I32P, C.c_int, _FP, _I32P]),
     "soc_b200_decode": (C.c_int, [_VP, _VP, C.c_int, _I32P, _I32P, _FP, _I32P]),
     "soc_b200_generate": (C.c_int, [_VP, _VP, C.c_int, _I32P, C.c_int, C.c_int, C.c_int, _I32P,
@@ -225,6 +226,10 @@ class KVCache:
         k = np.ascontiguousarray(k, dtype=np.float32)
         v = np.ascontiguousarray(v, dtype=np.float32)
         _check(lib().soc_b200_kv_write(self.h, seq, layer, start, start + k.shape[0], _fp(k), _fp(v)))
+
+    def fill_random(self, seq: int, n_tokens: int, seed: int):
+        """Replace `seq` by n_tokens positions of seeded ~N(0, 1) fp16 K/V (soc_b200_kv_fill_random)."""
+        _check(lib().soc_b200_kv_fill_random(self.h, seq, n_tokens, seed))
 
 
 @dataclass

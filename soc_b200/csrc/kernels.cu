@@ -539,9 +539,170 @@ __global__ void k_attn_combine(const float* __restrict__ part, int hq, int n_spl
     out[(static_cast<size_t>(row) * hq + h) * D + d] = L > 0.0f ? acc / L : 0.0f;
 }
 
+// Decode-shaped attention (few rows per sequence): CTA = (row, kv head, key split), 4
+// warps; a group of LPK lanes owns one key at a time (LPK = 8, or 16 for 8 query heads per
+// kv head), each lane DPL = D / LPK dims of it, so 32 / LPK keys are in flight per warp
+// step and the K/V rows are read as contiguous 16-byte vectors.  Every group keeps its own
+// online-softmax state for the G query heads of the kv head (base-2 exponent, log2(e)
+// folded into the query scale); the groups and warps are merged in shared memory at the
+// end.  The next key's K/V vectors are loaded before the current key is consumed.
+template <int D, int G>
+__global__ void __launch_bounds__(128) k_attn_rows(const float* __restrict__ q, const int* __restrict__ row_seq,
+                                                   const int* __restrict__ row_pos, int hq, int hkv, KVLayerView kv,
+                                                   int n_splits, float* __restrict__ out, float* __restrict__ part) {
+    constexpr int LPK = (G >= 8 && D >= 128) ? 16 : 8, DPL = D / LPK, KPW = 32 / LPK, NW = 4, NS = NW * KPW;
+    constexpr int NV = DPL / 8;  // 16-byte vectors per lane per key row
+    __shared__ float sm_m[NS][G], sm_l[NS][G];
+    __shared__ float sm_o[NS][G][D];
+    const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int grp = lane / LPK, sub = lane % LPK;
+    const int seq = row_seq[row];
+    const int nvis = row_pos[row] + 1;
+    const int chunk = ((nvis + n_splits - 1) / n_splits + 15) / 16 * 16;
+    const int kb = split * chunk;
+    const int ke = min(nvis, kb + chunk);
+    const float qs = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+
+    float qr[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float* qp = q + (static_cast<size_t>(row) * hq + kvh * G + g) * D + sub * DPL;
+#pragma unroll
+        for (int j = 0; j < DPL; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(qp + j);
+            qr[g][j] = v.x * qs;
+            qr[g][j + 1] = v.y * qs;
+            qr[g][j + 2] = v.z * qs;
+            qr[g][j + 3] = v.w * qs;
+        }
+    }
+    float m[G], l[G], o[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) o[g][j] = 0.0f;
+    }
+    const int* pt = kv.page_table + static_cast<size_t>(seq) * kv.max_pages;
+    auto load = [&](int p, uint4 (&kx)[NV], uint4 (&vx)[NV]) {
+        if (p < ke) {
+            const int page = pt[p / kv.page_tokens];
+            const size_t off =
+                ((static_cast<size_t>(page) * hkv + kvh) * kv.page_tokens + (p % kv.page_tokens)) * D + sub * DPL;
+#pragma unroll
+            for (int c = 0; c < NV; ++c) {
+                kx[c] = ld_nc16(kv.k + off + c * 8);
+                vx[c] = ld_nc16(kv.v + off + c * 8);
+            }
+        }
+    };
+    int p = kb + warp * KPW + grp;
+    uint4 kc[NV], vc[NV];
+    load(p, kc, vc);
+    for (; p - grp < ke; p += NS) {
+        uint4 kn[NV], vn[NV];
+        load(p + NS, kn, vn);
+        if (p < ke) {
+            float kf[DPL], vf[DPL];
+#pragma unroll
+            for (int c = 0; c < NV; ++c) {
+                float w8[8];
+                Codec<WF_F16>::part(kc[c], 0, w8);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) kf[c * 8 + j] = w8[j];
+                Codec<WF_F16>::part(vc[c], 0, w8);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) vf[c * 8 + j] = w8[j];
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float sc = 0.0f;
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) sc += qr[g][j] * kf[j];
+#pragma unroll
+                for (int off = 1; off < LPK; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+                const float mn = fmaxf(m[g], sc);
+                const float corr = exp2f(m[g] - mn);
+                const float pe = exp2f(sc - mn);
+                l[g] = l[g] * corr + pe;
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) o[g][j] = o[g][j] * corr + pe * vf[j];
+                m[g] = mn;
+            }
+        } else {
+            // keep the shuffles of the other groups of this warp matched
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float sc = 0.0f;
+#pragma unroll
+                for (int off = 1; off < LPK; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < NV; ++c) {
+            kc[c] = kn[c];
+            vc[c] = vn[c];
+        }
+    }
+    const int slot = warp * KPW + grp;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        if (sub == 0) {
+            sm_m[slot][g] = m[g];
+            sm_l[slot][g] = l[g];
+        }
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) sm_o[slot][g][sub * DPL + j] = o[g][j];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * D; idx += NW * 32) {
+        const int g = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (int w = 0; w < NS; ++w) M = fmaxf(M, sm_m[w][g]);
+        float Lt = 0.0f, acc = 0.0f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < NS; ++w) {
+                const float f = sm_m[w][g] == -INFINITY ? 0.0f : exp2f(sm_m[w][g] - M);
+                Lt += sm_l[w][g] * f;
+                acc += sm_o[w][g][d] * f;
+            }
+        }
+        const int h = kvh * G + g;
+        if (n_splits == 1) {
+            out[(static_cast<size_t>(row) * hq + h) * D + d] = Lt > 0.0f ? acc / Lt : 0.0f;
+        } else {
+            // partial in natural-exponent units for the combine kernel: M * ln(2)
+            float* pp = part + ((static_cast<size_t>(row) * hq + h) * n_splits + split) * (D + 2);
+            pp[d] = acc;
+            if (d == 0) {
+                pp[D] = M == -INFINITY ? -INFINITY : M * 0.6931471805599453f;
+                pp[D + 1] = Lt;
+            }
+        }
+    }
+}
+
+template <int D>
+static bool attn_rows_d(int G, dim3 grid, const float* q, const Rows& rows, int hq, int hkv, const KVLayerView& kv,
+                        int splits, float* out, float* scratch, cudaStream_t st) {
+    switch (G) {
+        case 1: k_attn_rows<D, 1><<<grid, 128, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out, scratch); return true;
+        case 2: k_attn_rows<D, 2><<<grid, 128, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out, scratch); return true;
+        case 4: k_attn_rows<D, 4><<<grid, 128, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out, scratch); return true;
+        case 8: k_attn_rows<D, 8><<<grid, 128, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out, scratch); return true;
+        default: return false;
+    }
+}
+
 int attention_splits(int rows, int hkv, int max_visible) {
+    // enough CTAs for two waves, and no split longer than 512 keys (long contexts of a
+    // ragged batch would otherwise form the tail)
     const int ctas = rows * hkv;
     int splits = (2 * 148 + ctas - 1) / ctas;
+    const int by_chunk = (max_visible + 511) / 512;
+    if (splits < by_chunk) splits = by_chunk;
     const int max_by_len = (max_visible + 63) / 64;
     if (splits > max_by_len) splits = max_by_len;
     if (splits < 1) splits = 1;
@@ -556,7 +717,16 @@ void launch_attention(const float* q, const Rows& rows, int splits, int hq, int 
     const size_t need = static_cast<size_t>(rows.n) * hq * splits * (head_dim + 2);
     if (splits > 1 && (scratch == nullptr || need > scratch_floats)) throw Error(-5, "attention: split-K scratch too small");
     dim3 grid(rows.n, hkv, splits);
-    if (head_dim == 128) {
+    const int G = hq / hkv;
+    bool done = false;
+    if (head_dim == 128) done = attn_rows_d<128>(G, grid, q, rows, hq, hkv, kv, splits, out, scratch, st);
+    else if (head_dim == 64) done = attn_rows_d<64>(G, grid, q, rows, hq, hkv, kv, splits, out, scratch, st);
+    if (done) {
+        if (splits > 1) {
+            if (head_dim == 128) k_attn_combine<128><<<dim3(rows.n, hq), 128, 0, st>>>(scratch, hq, splits, out);
+            else k_attn_combine<64><<<dim3(rows.n, hq), 64, 0, st>>>(scratch, hq, splits, out);
+        }
+    } else if (head_dim == 128) {
         k_attention<128><<<grid, ATT_WARPS * 32, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out,
                                                           scratch);
         if (splits > 1) k_attn_combine<128><<<dim3(rows.n, hq), 128, 0, st>>>(scratch, hq, splits, out);

@@ -58,6 +58,9 @@ typedef struct {
     int max_position;      /* rows of the RoPE table */
     float rms_norm_eps;
     double rope_theta;
+    int tp_rank;           /* tensor-parallel rank of this shard (0 without tensor parallelism) */
+    int tp_size;           /* ranks sharing the model (1 without tensor parallelism); the head,
+                              intermediate and vocab counts above are the whole model's */
 } soc_model_info;
 
 /* Message of the last failed call on this thread ("" if none). */
@@ -81,8 +84,13 @@ SOC_B200_API void* soc_b200_stream(soc_ctx* ctx);
  * error text follow ManifestLoader::LoadFromFile + StartupValidator::
  * ValidateManifest + QwenModelLoader::LoadModel (Mac/cpu/src/runtime_assets.cpp:
  * 138-168, startup_validator.cpp:5-23, qwen_model_loader.cpp:35-93) and
- * WeightLoader::LoadTensor (weight_loader.cpp:17-30).  tp_size must be 1 in
- * this version (tp_rank 0, nccl_comm NULL). */
+ * WeightLoader::LoadTensor (weight_loader.cpp:17-30).  Without tensor
+ * parallelism tp_rank = 0, tp_size = 1, nccl_comm = NULL.  With tp_size > 1 this
+ * rank keeps heads [tp_rank * hq / tp_size, ...) of q (and the matching kv heads),
+ * rows of gate/up and columns of o_proj/down_proj, and vocab rows [tp_rank * V /
+ * tp_size, ...) of the lm_head; nccl_comm is that group's ncclComm_t
+ * (soc_b200_nccl_comm_create or the caller's own); the KV cache then holds the
+ * local kv heads. */
 SOC_B200_API int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_format, int tp_rank, int tp_size,
                          void* nccl_comm, soc_model** out);
 SOC_B200_API int soc_b200_model_info(const soc_model* model, soc_model_info* out);
@@ -140,6 +148,16 @@ SOC_B200_API int soc_b200_generate(soc_model* model, soc_kv* kv, int seq, const 
  * context stream). */
 SOC_B200_API int soc_b200_generate_device(soc_model* model, soc_kv* kv, int seq, const int32_t* d_prompt, int n_prompt,
                              int max_new, int32_t* d_out);
+
+/* Tensor parallelism plumbing (the reference is single-device; these have no counterpart
+ * in it).  NCCL is loaded at run time from libnccl.so.2.  Rank 0 creates the id, every rank
+ * receives its 128 bytes out of band and creates the communicator on its own context's
+ * device; the communicator is then passed to soc_b200_load_bundle with tp_rank / tp_size.
+ * Every rank of a tensor-parallel model must make the same calls in the same order (the
+ * forward runs collectives), including the same choice of NULL / non-NULL logits outputs. */
+SOC_B200_API int soc_b200_nccl_unique_id(void* id_out /* 128 bytes */);
+SOC_B200_API int soc_b200_nccl_comm_create(soc_ctx* ctx, int nranks, int rank, const void* id, void** comm_out);
+SOC_B200_API int soc_b200_nccl_comm_destroy(void* comm);
 
 /* Kernel-level linear: y[r, :] = W x[r, :] for r < rows, all DEVICE pointers,
  * W [out_features, in_features] in `weight_format` (scales [out, in/group] fp16

@@ -19,7 +19,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xcompiler", "-fvisibility=hidden"]
 
-SOURCES = ["runtime.cu", "kernels.cu", "decode_mk.cu", "gemm_tc.cu", "attn_prefill.cu"]
+SOURCES = ["runtime.cu", "kernels.cu", "decode_mk.cu", "gemm_tc.cu", "attn_prefill.cu", "nccl_rt.cu"]
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:
@@ -45,7 +45,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
                 print(" ".join(cmd), flush=True)
             subprocess.run(cmd, check=True)
     if force or _stale(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda", "-ldl"]
         subprocess.run(cmd, check=True)
     return LIB
 

@@ -750,13 +750,13 @@ __device__ __forceinline__ unsigned long long mix64(unsigned long long x) {
     return z ^ (z >> 31);
 }
 
-// Element e = (pos * hkv + head) * D + d of stream (seq * L + layer) * 2 + kind (0 = K,
+// Element e = (pos * hkv_total + global head) * D + d of stream (seq * L + layer) * 2 + kind (0 = K,
 // 1 = V): the twelve 16-bit fields of mix64(x), mix64(x + 1), mix64(x + 2) with
 // x = seed + stream * 0xD1B54A32D192ED03 + 3 e are summed and mapped to sum / 65536 - 6
 // (Irwin-Hall approximation of N(0, 1), exact in fp32) and rounded to fp16.
 __global__ void k_kv_fill_random(__half* __restrict__ kpool, __half* __restrict__ vpool, size_t layer_stride,
-                                 const int* __restrict__ pages, int page_tokens, int hkv, int D, int L, int n_tokens,
-                                 int seq, unsigned long long seed) {
+                                 const int* __restrict__ pages, int page_tokens, int hkv, int hkv_total, int head_off,
+                                 int D, int L, int n_tokens, int seq, unsigned long long seed) {
     const int d8n = D / 8;
     const size_t total = static_cast<size_t>(L) * 2 * n_tokens * hkv * d8n;
     for (size_t v = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; v < total;
@@ -774,7 +774,8 @@ __global__ void k_kv_fill_random(__half* __restrict__ kpool, __half* __restrict_
         uint32_t packed[4];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const unsigned long long e = (static_cast<unsigned long long>(pos) * hkv + head) * D + d8 * 8 + j;
+            const unsigned long long e =
+                (static_cast<unsigned long long>(pos) * hkv_total + head_off + head) * D + d8 * 8 + j;
             const unsigned long long x = seed + stream * 0xD1B54A32D192ED03ull + 3ull * e;
             unsigned sum = 0;
 #pragma unroll
@@ -795,10 +796,11 @@ __global__ void k_kv_fill_random(__half* __restrict__ kpool, __half* __restrict_
 }
 
 void launch_kv_fill_random(__half* kpool, __half* vpool, size_t layer_stride, const int* pages, int page_tokens,
-                           int hkv, int D, int L, int n_tokens, int seq, unsigned long long seed, cudaStream_t st) {
+                           int hkv, int hkv_total, int head_off, int D, int L, int n_tokens, int seq,
+                           unsigned long long seed, cudaStream_t st) {
     if (n_tokens <= 0) return;
-    k_kv_fill_random<<<148 * 16, 256, 0, st>>>(kpool, vpool, layer_stride, pages, page_tokens, hkv, D, L, n_tokens,
-                                               seq, seed);
+    k_kv_fill_random<<<148 * 16, 256, 0, st>>>(kpool, vpool, layer_stride, pages, page_tokens, hkv, hkv_total,
+                                               head_off, D, L, n_tokens, seq, seed);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }
@@ -806,14 +808,17 @@ void launch_kv_fill_random(__half* kpool, __half* vpool, size_t layer_stride, co
 // ------------------------------------------------------------------------ argmax
 // Greedy pick per row: maximum logit, lowest index on ties (the reference's
 // partial_sort with top_k = 1 keeps the first strict maximum).  NaNs never win.
-__global__ void k_argmax(const float* __restrict__ logits, int V, int ld, int* __restrict__ next_ids) {
+// keys != nullptr: write the row's best (value, global index) key instead of the id, for a
+// vocab shard whose first global index is v_off (merged across shards by k_argmax_merge).
+__global__ void k_argmax(const float* __restrict__ logits, int V, int ld, int v_off, int* __restrict__ next_ids,
+                         unsigned long long* __restrict__ keys) {
     __shared__ unsigned long long red[32];
     const float* row = logits + static_cast<size_t>(blockIdx.x) * ld;
     unsigned long long best = 0ull;
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
         const float v = row[i];
         if (v != v) continue;
-        const unsigned long long k = argmax_key(v, i);
+        const unsigned long long k = argmax_key(v, v_off + i);
         best = k > best ? k : best;
     }
 #pragma unroll
@@ -830,13 +835,46 @@ __global__ void k_argmax(const float* __restrict__ logits, int V, int ld, int* _
             const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
             b = other > b ? other : b;
         }
-        if (threadIdx.x == 0) next_ids[blockIdx.x] = b == 0ull ? 0 : argmax_key_index(b);
+        if (threadIdx.x == 0) {
+            if (keys != nullptr)
+                keys[blockIdx.x] = b;
+            else
+                next_ids[blockIdx.x] = b == 0ull ? 0 : argmax_key_index(b);
+        }
     }
+}
+
+// keys_all [shards][rows] -> id of the largest key per row (ties: lowest global index).
+__global__ void k_argmax_merge(const unsigned long long* __restrict__ keys_all, int shards, int rows,
+                               int* __restrict__ next_ids) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    unsigned long long b = 0ull;
+    for (int s = 0; s < shards; ++s) {
+        const unsigned long long k = keys_all[static_cast<size_t>(s) * rows + r];
+        b = k > b ? k : b;
+    }
+    next_ids[r] = b == 0ull ? 0 : argmax_key_index(b);
 }
 
 void launch_argmax(const float* logits, int vocab, int ld, int rows, int* next_ids, cudaStream_t st) {
     if (rows <= 0) return;
-    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, next_ids);
+    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, 0, next_ids, nullptr);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_off, unsigned long long* keys,
+                        cudaStream_t st) {
+    if (rows <= 0) return;
+    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, v_off, nullptr, keys);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+void launch_argmax_merge(const unsigned long long* keys_all, int shards, int rows, int* next_ids, cudaStream_t st) {
+    if (rows <= 0) return;
+    k_argmax_merge<<<(rows + 127) / 128, 128, 0, st>>>(keys_all, shards, rows, next_ids);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }

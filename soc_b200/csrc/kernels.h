@@ -51,10 +51,17 @@ void launch_flash_prefill(const float* q, int n, int hq, int hkv, int head_dim, 
 
 // Seeded pseudo-random K and V (about N(0, 1), fp16) for positions [0, n_tokens) of sequence
 // `seq` in every layer; `pages` = that sequence's page-table row.
+// hkv = kv heads held here, heads [head_off, head_off + hkv) of hkv_total (tensor parallelism).
 void launch_kv_fill_random(__half* kpool, __half* vpool, size_t layer_stride, const int* pages, int page_tokens,
-                           int hkv, int D, int L, int n_tokens, int seq, unsigned long long seed, cudaStream_t st);
+                           int hkv, int hkv_total, int head_off, int D, int L, int n_tokens, int seq,
+                           unsigned long long seed, cudaStream_t st);
 
 void launch_argmax(const float* logits, int vocab, int ld, int rows, int* next_ids, cudaStream_t st);
+// Vocab-parallel greedy pick: per-row (value, global index) keys of one shard, and the merge
+// of all shards' keys [shards][rows] (lowest global index wins ties, as above).
+void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_off, unsigned long long* keys,
+                        cudaStream_t st);
+void launch_argmax_merge(const unsigned long long* keys_all, int shards, int rows, int* next_ids, cudaStream_t st);
 
 void launch_rmsnorm(const float* x, int rows, int n, const float* w, float eps, float* y, cudaStream_t st);
 

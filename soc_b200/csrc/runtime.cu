@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "decode_mk.h"
 #include "gemm_tc.h"
+#include "nccl_rt.h"
 #include "json.hpp"
 #include "kernels.h"
 
@@ -321,33 +322,57 @@ std::vector<float> dequantize_rows(const std::vector<char>& b, const std::vector
     return out;
 }
 
-// Reads linear `name` ([rows, cols]) and returns it in device format `fmt`.
-HostMat prepare_matrix(const Manifest& man, const std::string& name, size_t rows, size_t cols, int fmt) {
+// Sub-block [r0, r0 + nr) x [c0, c0 + nc) of a row-major matrix (tensor-parallel shard).
+struct Block {
+    size_t r0 = 0, nr = 0, c0 = 0, nc = 0;
+};
+
+// Row-major bytes of `blk` from a matrix whose rows hold `cols` elements of `row_bytes(cols)`.
+template <typename RB>
+std::vector<char> cut(const std::vector<char>& b, size_t cols, const Block& blk, RB row_bytes) {
+    const size_t rb = row_bytes(cols), ob = row_bytes(blk.nc), off = row_bytes(blk.c0);
+    std::vector<char> o(blk.nr * ob);
+    for (size_t r = 0; r < blk.nr; ++r) std::memcpy(o.data() + r * ob, b.data() + (blk.r0 + r) * rb + off, ob);
+    return o;
+}
+
+// Reads linear `name` ([rows, cols]), keeps the block `blk` (default: all of it) and
+// returns it in device format `fmt`.
+HostMat prepare_matrix(const Manifest& man, const std::string& name, size_t rows, size_t cols, int fmt,
+                       Block blk = Block{}) {
     const TensorRecord& r = man.find(name);
+    if (blk.nr == 0) blk = Block{0, rows, 0, cols};
+    if (blk.r0 + blk.nr > rows || blk.c0 + blk.nc > cols) throw Error(SOC_B200_ERR_INVALID, "shard outside " + name);
     HostMat out;
     const int src = fmt_of_dtype(r.dtype);
     std::vector<float> f32;
+    const size_t nr = blk.nr, nc = blk.nc;
     if (src == WF_I8G64 || src == WF_I4G32) {
         if (r.shape != std::vector<size_t>{rows, cols})
             throw_fmt("model loader encountered unexpected shape for: " + name);
         const int g = quant_group(src);
         if (cols % g != 0) throw_fmt("quantised tensor columns are not a multiple of the group for: " + name);
+        if (blk.c0 % g != 0 || nc % g != 0) throw Error(SOC_B200_ERR_INVALID, "shard splits a quantisation group: " + name);
         TensorRecord raw = r;
         raw.dtype = "uint8";
         raw.shape = {rows * fmt_row_bytes(src, cols)};
-        const std::vector<char> b = load_record(raw, raw.shape);
+        const std::vector<char> b = cut(load_record(raw, raw.shape), cols, blk,
+                                        [&](size_t c) { return fmt_row_bytes(src, c); });
         const TensorRecord& rs = man.find(name + ".scales");
         if (rs.dtype != "float16") throw_fmt("quantisation scales must be float16 for: " + name);
-        const std::vector<char> sb = load_record(rs, {rows, cols / g});
+        const std::vector<char> sb = cut(load_record(rs, {rows, cols / g}), cols, blk,
+                                         [&](size_t c) { return c / g * 2; });
         if (src == fmt) {
             out.data.assign(b.begin(), b.end());
-            out.scales.resize(rows * (cols / g));
+            out.scales.resize(nr * (nc / g));
             std::memcpy(out.scales.data(), sb.data(), sb.size());
             return out;
         }
-        f32 = dequantize_rows(b, sb, rows, cols, src);
+        f32 = dequantize_rows(b, sb, nr, nc, src);
     } else {
-        const std::vector<char> b = load_record(r, {rows, cols});
+        const size_t w = dtype_width(r.dtype);
+        std::vector<char> b = load_record(r, {rows, cols});
+        if (nr != rows || nc != cols) b = cut(b, cols, blk, [&](size_t c) { return c * w; });
         const bool same = (fmt == WF_F16 && r.dtype == "float16") || (fmt == WF_BF16 && r.dtype == "bfloat16");
         if (same) {
             out.data.assign(b.begin(), b.end());
@@ -356,11 +381,11 @@ HostMat prepare_matrix(const Manifest& man, const std::string& name, size_t rows
         f32 = to_f32(r, b);
     }
     if (fmt == WF_I8G64 || fmt == WF_I4G32) {
-        if (cols % quant_group(fmt) != 0) throw_fmt("in_features is not a multiple of the quantisation group: " + name);
-        quantize_rows(f32.data(), rows, cols, fmt, out);
+        if (nc % quant_group(fmt) != 0) throw_fmt("in_features is not a multiple of the quantisation group: " + name);
+        quantize_rows(f32.data(), nr, nc, fmt, out);
         return out;
     }
-    out.data.resize(rows * cols * 2);
+    out.data.resize(nr * nc * 2);
     uint16_t* d = reinterpret_cast<uint16_t*>(out.data.data());
     for (size_t i = 0; i < f32.size(); ++i) {
         if (fmt == WF_F16) {
@@ -404,7 +429,17 @@ struct LayerW {
 
 struct soc_model {
     soc_ctx* ctx = nullptr;
-    Config cfg;
+    Config cfg;       // this rank's shard: q/kv heads and intermediate divided by tp_size
+    Config cfg_full;  // the whole model
+    // tensor parallelism (Megatron-style): column-parallel q/k/v and gate/up, row-parallel
+    // o_proj and down_proj followed by an all-reduce of the residual stream, vocab-parallel
+    // lm_head with a merged argmax
+    int tp_rank = 0, tp_size = 1;
+    ncclComm_t comm = nullptr;
+    int v_loc = 0, v_off = 0;                 // lm_head rows held here
+    float* logits_all = nullptr;              // [tp][rows][v_loc] gathered logits
+    int logits_all_rows = 0;
+    unsigned long long* d_keys = nullptr;     // [tp][rows] argmax keys (this rank's at tp_rank)
     int wfmt = WF_F16;  // block linears
     int efmt = WF_F16;  // embedding / lm_head
     void* embed = nullptr;
@@ -424,6 +459,7 @@ struct soc_model {
     void *xa = nullptr, *xa_lo = nullptr;      // [ws_rows, max(hidden, q width)] GEMM input rows (hi, lo)
     void *acth = nullptr, *acth_lo = nullptr;  // [ws_rows, inter] SwiGLU output = down_proj input (hi, lo)
     void* wdq = nullptr;                       // fp16 expansion of one quantised matrix (quantised models)
+    CUtensorMap tm_lm{};                       // descriptor of the lm_head rows held here
     CUtensorMap tm_dq_qkv{}, tm_dq_o{}, tm_dq_gu{}, tm_dq_d{};  // descriptors over wdq, one per shape
     float* logits = nullptr;
     int logits_rows = 0;
@@ -542,8 +578,12 @@ void ensure_workspace(soc_model* m, int rows) {
 void ensure_logits(soc_model* m, int rows) {
     if (rows <= m->logits_rows) return;
     m->dfree(m->logits);
-    m->logits = static_cast<float*>(m->dmalloc(sizeof(float) * rows * m->cfg.vocab));
+    m->logits = static_cast<float*>(m->dmalloc(sizeof(float) * rows * m->v_loc));
     m->logits_rows = rows;
+    if (m->tp_size > 1) {
+        m->dfree(m->d_keys);
+        m->d_keys = static_cast<unsigned long long*>(m->dmalloc(sizeof(unsigned long long) * rows * m->tp_size));
+    }
 }
 
 void ensure_attn_scratch(soc_model* m, size_t floats) {
@@ -616,6 +656,14 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
         return dq;
     };
     int* err = m->ctx->d_err;
+    // Row-parallel o_proj / down_proj: rank 0 adds its partial product to the residual
+    // stream, the other ranks store theirs, and the all-reduce sums them.
+    const int res_mode = m->tp_rank == 0 ? LIN_RESIDUAL : LIN_STORE;
+    auto tp_sum = [&] {
+        if (m->tp_size > 1)
+            nccl_check(nccl().all_reduce(m->h, m->h, static_cast<size_t>(n) * H, ncclFloat32, ncclSum, m->comm, st),
+                       "residual all-reduce");
+    };
     const bool flash = pf_seq >= 0 && flash_min_rows() > 0 && n >= flash_min_rows();
     for (size_t l = 0; l < c.layers; ++l) {
         const LayerW& w = m->layers[l];
@@ -639,24 +687,47 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
         if (tc) {
             launch_rows_to_half(gf, m->att, QW, n, QW, nullptr, eps, m->xa, xlo, QW, st);
             launch_gemm_tc(gf, a_att, split ? &a_att_lo : nullptr, wmap(w.tm_o, w.wo, w.so, H, QW, m->tm_dq_o), n, H,
-                           QW, m->h, H, LIN_RESIDUAL, false, nullptr, gws, TC_WS_FLOATS, err, st);
+                           QW, m->h, H, res_mode, false, nullptr, gws, TC_WS_FLOATS, err, st);
+            tp_sum();
             launch_rows_to_half(gf, m->h, H, n, H, w.post_norm, eps, m->xa, xlo, H, st);
             launch_gemm_tc(gf, a_h, split ? &a_h_lo : nullptr, wmap(w.tm_gu, w.wgu, w.sgu, 2 * I, H, m->tm_dq_gu), n,
                            2 * I, H, m->acth, I, LIN_SWIGLU, true, split ? m->acth_lo : nullptr, gws, TC_WS_FLOATS,
                            err, st);
             launch_gemm_tc(gf, a_act, split ? &a_act_lo : nullptr, wmap(w.tm_d, w.wd, w.sd, H, I, m->tm_dq_d), n, H, I,
-                           m->h, H, LIN_RESIDUAL, false, nullptr, gws, TC_WS_FLOATS, err, st);
+                           m->h, H, res_mode, false, nullptr, gws, TC_WS_FLOATS, err, st);
+            tp_sum();
         } else {
-            launch_linear(m->wfmt, w.wo, w.so, H, QW, m->att, QW, n, nullptr, eps, m->h, H, LIN_RESIDUAL, st);
+            launch_linear(m->wfmt, w.wo, w.so, H, QW, m->att, QW, n, nullptr, eps, m->h, H, res_mode, st);
+            tp_sum();
             launch_linear(m->wfmt, w.wgu, w.sgu, 2 * I, H, m->h, H, n, w.post_norm, eps, m->act, I, LIN_SWIGLU, st);
-            launch_linear(m->wfmt, w.wd, w.sd, H, I, m->act, I, n, nullptr, eps, m->h, H, LIN_RESIDUAL, st);
+            launch_linear(m->wfmt, w.wd, w.sd, H, I, m->act, I, n, nullptr, eps, m->h, H, res_mode, st);
+            tp_sum();
         }
     }
     if (lm_rows > 0) {
         ensure_logits(m, lm_rows);
-        launch_linear(m->efmt, m->lm_head, nullptr, static_cast<int>(c.vocab), H, m->h + static_cast<size_t>(lm_first) * H,
-                      H, lm_rows, m->final_norm, eps, m->logits, static_cast<int>(c.vocab), LIN_STORE, st);
-        launch_argmax(m->logits, static_cast<int>(c.vocab), static_cast<int>(c.vocab), lm_rows, m->d_next, st);
+        if (m->tc_ok && tmin > 0 && lm_rows >= tmin) {
+            // many rows (batched decode): tensor-core GEMM over the vocab rows
+            const bool lsplit = lm_rows <= tc_split_max_rows();
+            CUtensorMap a_lm{}, a_lm_lo{};
+            tc_make_map(&a_lm, m->xa, m->efmt, lm_rows, H, H, TC_BOX_A);
+            if (lsplit) tc_make_map(&a_lm_lo, m->xa_lo, m->efmt, lm_rows, H, H, TC_BOX_A);
+            launch_rows_to_half(m->efmt, m->h + static_cast<size_t>(lm_first) * H, H, lm_rows, H, m->final_norm, eps,
+                                m->xa, lsplit ? m->xa_lo : nullptr, H, st);
+            launch_gemm_tc(m->efmt, a_lm, lsplit ? &a_lm_lo : nullptr, m->tm_lm, lm_rows, m->v_loc, H, m->logits,
+                           m->v_loc, LIN_STORE, false, nullptr, m->ctx->ws(), TC_WS_FLOATS, err, st);
+        } else {
+            launch_linear(m->efmt, m->lm_head, nullptr, m->v_loc, H, m->h + static_cast<size_t>(lm_first) * H, H,
+                          lm_rows, m->final_norm, eps, m->logits, m->v_loc, LIN_STORE, st);
+        }
+        if (m->tp_size == 1) {
+            launch_argmax(m->logits, m->v_loc, m->v_loc, lm_rows, m->d_next, st);
+        } else {
+            unsigned long long* mine = m->d_keys + static_cast<size_t>(m->tp_rank) * lm_rows;
+            launch_argmax_keys(m->logits, m->v_loc, m->v_loc, lm_rows, m->v_off, mine, st);
+            nccl_check(nccl().all_gather(mine, m->d_keys, lm_rows, ncclUint64, m->comm, st), "argmax all-gather");
+            launch_argmax_merge(m->d_keys, m->tp_size, lm_rows, m->d_next, st);
+        }
     }
 }
 
@@ -664,6 +735,25 @@ void check_ids(const soc_model* m, const int32_t* ids, int n) {
     for (int i = 0; i < n; ++i)
         if (ids[i] < 0 || static_cast<size_t>(ids[i]) >= m->cfg.vocab)
             throw Error(SOC_B200_ERR_RANGE, "embedding input token id out of range");
+}
+
+// Copies the logits of `rows` rows (full vocab) to host memory.  With tensor parallelism
+// the vocab shards are all-gathered first, so every rank must make the same call.
+void logits_to_host(soc_model* m, int rows, float* host, cudaStream_t st) {
+    const size_t V = m->cfg.vocab, vl = static_cast<size_t>(m->v_loc);
+    if (m->tp_size == 1) {
+        SOCB_CUDA(cudaMemcpyAsync(host, m->logits, sizeof(float) * V * rows, cudaMemcpyDeviceToHost, st));
+        return;
+    }
+    if (rows > m->logits_all_rows) {
+        m->dfree(m->logits_all);
+        m->logits_all = static_cast<float*>(m->dmalloc(sizeof(float) * rows * V));
+        m->logits_all_rows = rows;
+    }
+    nccl_check(nccl().all_gather(m->logits, m->logits_all, vl * rows, ncclFloat32, m->comm, st), "logits all-gather");
+    for (int r = 0; r < m->tp_size; ++r)
+        SOCB_CUDA(cudaMemcpy2DAsync(host + r * vl, V * sizeof(float), m->logits_all + r * vl * rows, vl * sizeof(float),
+                                    vl * sizeof(float), rows, cudaMemcpyDeviceToHost, st));
 }
 
 constexpr int kPrefillChunk = 4096;
@@ -811,6 +901,18 @@ void decode_loop(soc_model* m, soc_kv* kv, int seq, int start, int steps, int32_
     ensure_logits(m, 1);
     if (splits > 1) ensure_attn_scratch(m, static_cast<size_t>(m->cfg.hq) * splits * (m->cfg.hd + 2));
     if (!m->d_loop) m->d_loop = static_cast<soc_model::LoopState*>(m->dmalloc(sizeof(soc_model::LoopState)));
+    if (m->tp_size > 1) {
+        // Tensor-parallel steps are queued one by one (their collectives stay out of graphs).
+        const soc_model::LoopState init{d_out, seq, start, 0};
+        SOCB_CUDA(cudaMemcpyAsync(m->d_loop, &init, sizeof(init), cudaMemcpyHostToDevice, st));
+        for (int i = 0; i < steps; ++i) {
+            k_step_begin<<<1, 1, 0, st>>>(m->d_loop, m->d_tokens, m->d_seq, m->d_pos);
+            forward_rows(m, kv, 1, start + steps, 0, 1, splits);
+            k_step_end<<<1, 1, 0, st>>>(m->d_loop, m->d_next);
+            count_launches(2);
+        }
+        return;
+    }
     if (!m->step_graph || m->graph_kv != kv || m->graph_splits != splits) {
         if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
         m->step_graph = nullptr;
@@ -889,16 +991,37 @@ void* soc_b200_stream(soc_ctx* ctx) { return ctx ? static_cast<void*>(ctx->strea
 int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_format, int tp_rank, int tp_size,
                          void* nccl_comm, soc_model** out) {
     if (!ctx || !manifest_path || !out) return fail(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: null argument");
-    if (tp_size != 1 || tp_rank != 0 || nccl_comm != nullptr)
-        return fail(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: tensor parallelism is not enabled in this build");
+    if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size)
+        return fail(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: tp_rank must be in [0, tp_size)");
+    if (tp_size > 1 && nccl_comm == nullptr)
+        return fail(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: tensor parallelism needs an NCCL communicator");
     auto m = std::make_unique<soc_model>();
     const int rc = guarded([&] {
         SOCB_CUDA(cudaSetDevice(ctx->device));
         m->ctx = ctx;
         const Manifest man = load_manifest(manifest_path);
-        m->cfg = read_config(man.config);
+        m->cfg_full = read_config(man.config);
+        m->cfg = m->cfg_full;
+        m->tp_rank = tp_rank;
+        m->tp_size = tp_size;
+        m->comm = static_cast<ncclComm_t>(nccl_comm);
+        if (tp_size > 1) {
+            const Config& f = m->cfg_full;
+            if (f.hq % tp_size || f.hkv % tp_size || f.inter % tp_size || f.vocab % tp_size)
+                throw Error(SOC_B200_ERR_INVALID,
+                            "tensor parallelism needs heads, kv heads, intermediate size and vocab divisible by tp_size");
+            if ((f.inter / tp_size) % 64 || (f.hq / tp_size * f.hd) % 64)
+                throw Error(SOC_B200_ERR_INVALID, "tensor-parallel shards must keep multiples of 64 features");
+            m->cfg.hq /= tp_size;
+            m->cfg.hkv /= tp_size;
+            m->cfg.inter /= tp_size;
+        }
         const Config& c = m->cfg;
         const size_t H = c.hidden, I = c.inter, D = c.hd, QW = c.hq * D, KW = c.hkv * D;
+        const size_t QWf = m->cfg_full.hq * D, KWf = m->cfg_full.hkv * D, If = m->cfg_full.inter;
+        const size_t tr = static_cast<size_t>(tp_rank);
+        m->v_loc = static_cast<int>(c.vocab / tp_size);
+        m->v_off = static_cast<int>(tr * m->v_loc);
 
         // Linear weight format: the stored type of the block linears unless the caller asks
         // for another one (float -> float conversion, or group quantisation at load time).
@@ -990,15 +1113,18 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
                     SOCB_CUDA(cudaMemcpy(*sdst, sc.data(), sc.size() * 2, cudaMemcpyHostToDevice));
                 }
             };
-            upload_rows({prepare_matrix(man, p + "self_attn.q_proj.weight", QW, H, fmt),
-                         prepare_matrix(man, p + "self_attn.k_proj.weight", KW, H, fmt),
-                         prepare_matrix(man, p + "self_attn.v_proj.weight", KW, H, fmt)},
+            // this rank's shard: rows of q/k/v and gate/up, columns of o_proj and down_proj
+            upload_rows({prepare_matrix(man, p + "self_attn.q_proj.weight", QWf, H, fmt, Block{tr * QW, QW, 0, H}),
+                         prepare_matrix(man, p + "self_attn.k_proj.weight", KWf, H, fmt, Block{tr * KW, KW, 0, H}),
+                         prepare_matrix(man, p + "self_attn.v_proj.weight", KWf, H, fmt, Block{tr * KW, KW, 0, H})},
                         {QW, KW, KW}, H, false, &w.wqkv, &w.sqkv);
-            upload_rows({prepare_matrix(man, p + "self_attn.o_proj.weight", H, QW, fmt)}, {H}, QW, false, &w.wo, &w.so);
-            upload_rows({prepare_matrix(man, p + "mlp.gate_proj.weight", I, H, fmt),
-                         prepare_matrix(man, p + "mlp.up_proj.weight", I, H, fmt)},
+            upload_rows({prepare_matrix(man, p + "self_attn.o_proj.weight", H, QWf, fmt, Block{0, H, tr * QW, QW})}, {H},
+                        QW, false, &w.wo, &w.so);
+            upload_rows({prepare_matrix(man, p + "mlp.gate_proj.weight", If, H, fmt, Block{tr * I, I, 0, H}),
+                         prepare_matrix(man, p + "mlp.up_proj.weight", If, H, fmt, Block{tr * I, I, 0, H})},
                         {I, I}, H, true, &w.wgu, &w.sgu);
-            upload_rows({prepare_matrix(man, p + "mlp.down_proj.weight", H, I, fmt)}, {H}, I, false, &w.wd, &w.sd);
+            upload_rows({prepare_matrix(man, p + "mlp.down_proj.weight", H, If, fmt, Block{0, H, tr * I, I})}, {H}, I,
+                        false, &w.wd, &w.sd);
         }
         m->final_norm = upload_norm("model.norm.weight", H);
         // TMA descriptors of the block linears for the tensor-core GEMM (for quantised
@@ -1020,13 +1146,22 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
             tc_make_map(&m->tm_dq_gu, m->wdq, WF_F16, 2 * I, H, H, TC_BOX_W);
             tc_make_map(&m->tm_dq_d, m->wdq, WF_F16, H, I, I, TC_BOX_W);
         }
-        if (c.tied) {
+        // lm_head rows [v_off, v_off + v_loc) (all of them without tensor parallelism)
+        const size_t vl = static_cast<size_t>(m->v_loc), vo = static_cast<size_t>(m->v_off);
+        if (c.tied && tp_size == 1) {
             m->lm_head = m->embed;
         } else {
-            const TensorRecord& r = man.find("lm_head.weight");
-            m->lm_head = m->dmalloc(c.vocab * H * 2);
-            upload_matrix(r, load_record(r, {c.vocab, H}), m->lm_head, m->efmt);
+            const TensorRecord& r = man.find(c.tied ? "model.embed_tokens.weight" : "lm_head.weight");
+            std::vector<char> b = load_record(r, {c.vocab, H});
+            const size_t rb = H * dtype_width(r.dtype);
+            if (tp_size > 1) b = std::vector<char>(b.begin() + vo * rb, b.begin() + (vo + vl) * rb);
+            m->lm_head = m->dmalloc(vl * H * 2);
+            upload_matrix(r, b, m->lm_head, m->efmt);
         }
+        if (m->tc_ok && (m->efmt == WF_F16 || m->efmt == WF_BF16))
+            tc_make_map(&m->tm_lm, m->lm_head, m->efmt, static_cast<uint64_t>(m->v_loc), H, H, TC_BOX_W);
+        else
+            m->tc_ok = false;
         // RoPE table (cos, sin) [max_pos][D/2], computed as RoPE::ApplyInPlace does (rope.cpp:74-79).
         m->rope_len = static_cast<int>(c.max_pos);
         std::vector<float2> cs(static_cast<size_t>(m->rope_len) * (D / 2));
@@ -1047,7 +1182,7 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
         const char* path = std::getenv("SOC_B200_DECODE_PATH");
         const bool want_mk = !(path && std::string(path) == "graph");
         const int grid = mk_grid(ctx->device);
-        if (want_mk && mk_supported(static_cast<int>(H), static_cast<int>(I), static_cast<int>(c.hq),
+        if (want_mk && tp_size == 1 && mk_supported(static_cast<int>(H), static_cast<int>(I), static_cast<int>(c.hq),
                                     static_cast<int>(c.hkv), static_cast<int>(D), fmt, grid) &&
             m->efmt == fmt) {
             std::vector<MKLayer> ml(c.layers);
@@ -1077,7 +1212,7 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
 
 int soc_b200_model_info(const soc_model* m, soc_model_info* out) {
     if (!m || !out) return fail(SOC_B200_ERR_INVALID, "null argument");
-    const Config& c = m->cfg;
+    const Config& c = m->cfg_full;
     out->layers = static_cast<int>(c.layers);
     out->hidden = static_cast<int>(c.hidden);
     out->intermediate = static_cast<int>(c.inter);
@@ -1090,6 +1225,8 @@ int soc_b200_model_info(const soc_model* m, soc_model_info* out) {
     out->max_position = m->rope_len;
     out->rms_norm_eps = static_cast<float>(c.eps);
     out->rope_theta = c.theta;
+    out->tp_rank = m->tp_rank;
+    out->tp_size = m->tp_size;
     return SOC_B200_OK;
 }
 
@@ -1209,7 +1346,8 @@ int soc_b200_kv_fill_random(soc_kv* kv, int seq, int n_tokens, unsigned long lon
         kv->reset(seq);
         kv->reserve(seq, n_tokens, st);
         launch_kv_fill_random(kv->k, kv->v, kv->layer_stride(), kv->d_page_table + static_cast<size_t>(seq) * kv->max_pages,
-                              kv->page_tokens, static_cast<int>(m->cfg.hkv), static_cast<int>(m->cfg.hd),
+                              kv->page_tokens, static_cast<int>(m->cfg.hkv), static_cast<int>(m->cfg_full.hkv),
+                              m->tp_rank * static_cast<int>(m->cfg.hkv), static_cast<int>(m->cfg.hd),
                               static_cast<int>(m->cfg.layers), n_tokens, seq, seed, st);
         kv->lengths[seq] = n_tokens;
     });
@@ -1256,8 +1394,7 @@ int soc_b200_prefill(soc_model* m, soc_kv* kv, int seq, const int32_t* ids, int 
         SOCB_CUDA(cudaSetDevice(m->ctx->device));
         prefill_impl(m, kv, seq, ids, n, false);
         cudaStream_t st = m->ctx->stream;
-        if (logits_last)
-            SOCB_CUDA(cudaMemcpyAsync(logits_last, m->logits, sizeof(float) * m->cfg.vocab, cudaMemcpyDeviceToHost, st));
+        if (logits_last) logits_to_host(m, 1, logits_last, st);
         int nid = 0;
         SOCB_CUDA(cudaMemcpyAsync(&nid, m->d_next, sizeof(int), cudaMemcpyDeviceToHost, st));
         check_device_error(m);
@@ -1303,9 +1440,7 @@ int soc_b200_decode(soc_model* m, soc_kv* kv, int n_seqs, const int* seq_ids, co
         SOCB_CUDA(cudaMemcpyAsync(m->d_seq, seq_ids, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, st));
         SOCB_CUDA(cudaMemcpyAsync(m->d_pos, pos.data(), sizeof(int) * n_seqs, cudaMemcpyHostToDevice, st));
         forward_rows(m, kv, n_seqs, max_vis, 0, n_seqs, 0);
-        if (logits)
-            SOCB_CUDA(cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->cfg.vocab * n_seqs, cudaMemcpyDeviceToHost,
-                                      st));
+        if (logits) logits_to_host(m, n_seqs, logits, st);
         if (next_ids) SOCB_CUDA(cudaMemcpyAsync(next_ids, m->d_next, sizeof(int) * n_seqs, cudaMemcpyDeviceToHost, st));
         check_device_error(m);
         for (int i = 0; i < n_seqs; ++i) kv->lengths[seq_ids[i]] = pos[i] + 1;
@@ -1373,6 +1508,33 @@ int soc_b200_generate_device(soc_model* m, soc_kv* kv, int seq, const int32_t* d
         SOCB_CUDA(cudaSetDevice(m->ctx->device));
         generate_dev(m, kv, seq, d_prompt, n_prompt, max_new, d_out, true);
     });
+}
+
+int soc_b200_nccl_unique_id(void* id_out) {
+    if (!id_out) return fail(SOC_B200_ERR_INVALID, "null argument");
+    return guarded([&] {
+        ncclUniqueId id;
+        nccl_check(nccl().get_unique_id(&id), "ncclGetUniqueId");
+        std::memcpy(id_out, &id, sizeof(id));
+    });
+}
+
+int soc_b200_nccl_comm_create(soc_ctx* ctx, int nranks, int rank, const void* id, void** comm_out) {
+    if (!ctx || !id || !comm_out) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (nranks < 1 || rank < 0 || rank >= nranks) return fail(SOC_B200_ERR_INVALID, "rank must be in [0, nranks)");
+    return guarded([&] {
+        SOCB_CUDA(cudaSetDevice(ctx->device));
+        ncclUniqueId uid;
+        std::memcpy(&uid, id, sizeof(uid));
+        ncclComm_t comm = nullptr;
+        nccl_check(nccl().comm_init_rank(&comm, nranks, uid, rank), "ncclCommInitRank");
+        *comm_out = comm;
+    });
+}
+
+int soc_b200_nccl_comm_destroy(void* comm) {
+    if (!comm) return SOC_B200_OK;
+    return guarded([&] { nccl_check(nccl().comm_destroy(static_cast<ncclComm_t>(comm)), "ncclCommDestroy"); });
 }
 
 int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* scales, int out_features,
@@ -1476,6 +1638,8 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
     if (!m || !kv) return fail(SOC_B200_ERR_INVALID, "null argument");
     if (kv->m != m) return fail(SOC_B200_ERR_INVALID, "kv cache belongs to another model");
     return guarded([&] {
+        if (m->tp_size > 1)
+            throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: not available for a tensor-parallel shard");
         const Config& c = m->cfg;
         SOCB_CUDA(cudaSetDevice(m->ctx->device));
         cudaStream_t st = m->ctx->stream;

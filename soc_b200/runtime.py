@@ -42,7 +42,7 @@ class ModelInfo(C.Structure):
         ("layers", C.c_int), ("hidden", C.c_int), ("intermediate", C.c_int), ("q_heads", C.c_int),
         ("kv_heads", C.c_int), ("head_dim", C.c_int), ("vocab", C.c_int), ("tied_embeddings", C.c_int),
         ("weight_format", C.c_int), ("max_position", C.c_int), ("rms_norm_eps", C.c_float),
-        ("rope_theta", C.c_double),
+        ("rope_theta", C.c_double), ("tp_rank", C.c_int), ("tp_size", C.c_int),
     ]
 
 
@@ -68,6 +68,9 @@ _SIGNATURES = {
     "soc_b200_kv_read": (C.c_int, [_VP, C.c_int, C.c_int, C.c_int, C.c_int, _FP, _FP]),
     "soc_b200_kv_write": (C.c_int, [_VP, C.c_int, C.c_int, C.c_int, C.c_int, _FP, _FP]),
     "soc_b200_kv_fill_random": (C.c_int, [_VP, C.c_int, C.c_int, C.c_ulonglong]),
+    "soc_b200_nccl_unique_id": (C.c_int, [_VP]),
+    "soc_b200_nccl_comm_create": (C.c_int, [_VP, C.c_int, C.c_int, _VP, C.POINTER(_VP)]),
+    "soc_b200_nccl_comm_destroy": (C.c_int, [_VP]),
     "soc_b200_prefill": (C.c_int, [_VP, _VP, C.c_int, _I32P, C.c_int, _FP, _I32P]),
     "soc_b200_decode": (C.c_int, [_VP, _VP, C.c_int, _I32P, _I32P, _FP, _I32P]),
     "soc_b200_generate": (C.c_int, [_VP, _VP, C.c_int, _I32P, C.c_int, C.c_int, C.c_int, _I32P,
@@ -138,11 +141,41 @@ class Context:
         _check(lib().soc_b200_linear(self.h, weight_format, w_ptr, scales_ptr, out_features, in_features, x_ptr,
                                      rows, y_ptr, stream))
 
+    # ---- tensor parallelism (NCCL loaded at run time)
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        _check(lib().soc_b200_nccl_unique_id(buf))
+        return buf.raw
+
+    def nccl_comm_create(self, nranks: int, rank: int, uid: bytes):
+        """Communicator of `nranks` ranks on this context's device (every rank calls it)."""
+        buf = C.create_string_buffer(bytes(uid), 128)
+        h = _VP()
+        _check(lib().soc_b200_nccl_comm_create(self.h, nranks, rank, buf, C.byref(h)))
+        return h
+
+    @staticmethod
+    def nccl_comm_destroy(comm):
+        if comm:
+            _check(lib().soc_b200_nccl_comm_destroy(comm))
+
+
+def tensor_parallel_comm(ctx: "Context", group=None):
+    """NCCL communicator over the ranks of an initialised torch.distributed group: rank 0's
+    id reaches the others by broadcast_object_list."""
+    import torch.distributed as dist
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    obj = [Context.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    return ctx.nccl_comm_create(world, rank, obj[0])
+
 
 class Model:
-    def __init__(self, ctx: Context, manifest_path, weight_format: int = WEIGHTS_NATIVE):
+    def __init__(self, ctx: Context, manifest_path, weight_format: int = WEIGHTS_NATIVE, tp_rank: int = 0,
+                 tp_size: int = 1, comm=None):
         h = _VP()
-        _check(lib().soc_b200_load_bundle(ctx.h, str(manifest_path).encode(), weight_format, 0, 1, None,
+        _check(lib().soc_b200_load_bundle(ctx.h, str(manifest_path).encode(), weight_format, tp_rank, tp_size, comm,
                                           C.byref(h)))
         self.ctx = ctx
         self.h = h
@@ -216,8 +249,10 @@ class KVCache:
         return r
 
     def read(self, seq: int, layer: int, start: int, end: int):
+        """K and V [end - start, kv heads held here, head_dim] (a tensor-parallel rank holds
+        kv_heads / tp_size of them)."""
         i = self.model.info
-        k = np.empty((end - start, i.kv_heads, i.head_dim), dtype=np.float32)
+        k = np.empty((end - start, i.kv_heads // i.tp_size, i.head_dim), dtype=np.float32)
         v = np.empty_like(k)
         _check(lib().soc_b200_kv_read(self.h, seq, layer, start, end, _fp(k), _fp(v)))
         return k, v

@@ -519,6 +519,102 @@ def run_config3(args, rank, world, local):
         print(json.dumps(result), flush=True)
 
 
+# ------------------------------------------------------------------- config 4
+C4_BATCH, C4_CTX = 32, 2048
+
+
+def run_config4(args, rank, world, local):
+    """Config 4: Qwen3-8B architecture, random bf16 weights N(0, 0.02) seed 5 (drawn by
+    torch.randn on the GPU: 8.2 G values), tensor
+    parallel over the ranks (TP = --gpus: heads and FFN columns sharded, all-reduce of the
+    residual stream after o_proj and down_proj, vocab-parallel lm_head).  Batch 32 decode at
+    context 2048 of seeded ~N(0, 1) KV (soc_b200_kv_fill_random, seed 5000 + sequence), one
+    soc_b200_decode call per step.  Prints one JSON line (rank 0), max-over-ranks time."""
+    import torch
+    import torch.distributed as dist
+    from soc_b200 import runtime as R
+    from soc_b200.bundle import QWEN3_8B, cached_bundle
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    cfg = QWEN3_8B
+    if rank == 0:
+        p = cached_bundle("config4_qwen3_8b_bf16", cfg, seed=5, dtype="bfloat16", torch_device="cuda")
+    barrier()
+    if rank != 0:
+        p = cached_bundle("config4_qwen3_8b_bf16", cfg, seed=5, dtype="bfloat16", torch_device="cuda")
+    ctx = R.Context(local)
+    comm = R.tensor_parallel_comm(ctx) if world > 1 else None
+    model = R.Model(ctx, p, tp_rank=rank, tp_size=world, comm=comm)
+    steps, warmup = args.steps, max(args.warmup, 3)
+    kv = R.KVCache(model, C4_BATCH, C4_BATCH * (C4_CTX + steps + warmup + 16))
+    for s in range(C4_BATCH):
+        kv.fill_random(s, C4_CTX, 5000 + s)
+    ctx.synchronize()
+    toks = np.random.default_rng(6).integers(0, cfg["vocab_size"], C4_BATCH).astype(np.int32)
+    seqs = list(range(C4_BATCH))
+    for _ in range(warmup):
+        _, toks = model.decode(kv, seqs, toks, want_logits=False)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ctx.synchronize()
+    launches0 = R.kernel_launches()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            _, toks = model.decode(kv, seqs, toks, want_logits=False)
+        e1.record(stream)
+        ctx.synchronize()
+        wall = time.perf_counter() - t0
+    launches = R.kernel_launches() - launches0
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms, wall], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, wall = t.tolist()
+    H, I, L, D = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["head_dim"]
+    hq, hkv, V = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["vocab_size"]
+    params = L * (H * (hq + 2 * hkv) * D + H * hq * D + 3 * H * I) + V * H
+    mean_ctx = C4_CTX + warmup + (steps + 1) / 2
+    bytes_rank = (2 * params + C4_BATCH * mean_ctx * L * 2 * hkv * D * 2) / world
+    achieved = bytes_rank * steps / (ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": C4_BATCH * steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16w-f32a", "data": "synthetic", "impl": "soc_b200",
+            "config": {"workload": "config4: Qwen3-8B bf16 seed 5, batch 32 decode, context 2048 random N(0,1) KV",
+                       "global_batch": C4_BATCH, "seq_len": C4_CTX + steps + warmup, "parallelism": f"tp{world}",
+                       "l2": "weights 15.1 GB + KV 9.8 GB per step > 126 MB L2; no flush needed"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"], "traffic": None,
+                         "unit_of_work": "one batch-32 decode step, bytes held by one rank",
+                         "algorithmic_bytes_per_step_per_rank": bytes_rank},
+            "e2e": {"value": C4_BATCH * steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 8 * C4_BATCH,
+                    "d2h_bytes_per_step": 4 * C4_BATCH},
+            "gpu_launches": int(launches), "clocks": clk.summary(),
+        }
+    kv.free()
+    model.free()
+    R.Context.nccl_comm_destroy(comm)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
 # ------------------------------------------------------------- config 1 sweep
 SWEEP_SHAPES = {"q_proj": (2048, 1024), "k_proj": (1024, 1024), "o_proj": (1024, 2048), "gate_proj": (3072, 1024),
                 "down_proj": (1024, 3072), "lm_head": (151936, 1024)}
@@ -601,9 +697,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="soc", choices=["soc", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config0", choices=["config0", "linear-sweep", "config2", "config3"],
+    ap.add_argument("--workload", default="config0", choices=["config0", "linear-sweep", "config2", "config3", "config4"],
                     help="config0 (the headline line), linear-sweep (config 1, one line per case), config2, "
-                         "config3 (batched ragged decode, sequence-sharded over --gpus)")
+                         "config3 (batched ragged decode, sequence-sharded over --gpus), "
+                         "config4 (Qwen3-8B batch-32 decode, tensor-parallel over --gpus)")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.workload == "linear-sweep":
@@ -614,6 +711,9 @@ def main():
         return
     if args.workload == "config3":
         run_config3(args, rank, world, local)
+        return
+    if args.workload == "config4":
+        run_config4(args, rank, world, local)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

@@ -270,6 +270,7 @@ def write_synthetic_bundle(
     quant: str | None = None,
     std: float = 0.02,
     model_id: str = "synthetic/qwen3",
+    torch_device: str | None = None,
 ) -> Path:
     """Write a seeded random Qwen3 bundle in the reference format.
 
@@ -279,12 +280,19 @@ def write_synthetic_bundle(
     float type (``float16``/``bfloat16``/``float32``).  ``quant`` (``int8_g64``
     or ``int4_g32``) stores the block linears group-quantised instead, with
     embeddings, norms and the lm_head kept in ``dtype``.
+    ``torch_device`` (e.g. ``"cuda"``) draws the values with
+    ``torch.randn(shape, generator=torch.Generator(device).manual_seed(seed))`` on that
+    device instead (same order, same std), for multi-billion-parameter bundles.
     Returns the manifest path.
     """
     out = Path(out_dir)
     (out / "weights").mkdir(parents=True, exist_ok=True)
     (out / "tokenizer").mkdir(parents=True, exist_ok=True)
     rng = np.random.default_rng(seed)
+    tgen = None
+    if torch_device is not None:
+        import torch
+        tgen = torch.Generator(device=torch_device).manual_seed(seed)
     used: set[str] = set()
     records = []
 
@@ -301,6 +309,13 @@ def write_synthetic_bundle(
     for name, shape in tensor_shapes(cfg):
         if is_norm(name):
             w = np.ones(shape, dtype=np.float32)
+        elif tgen is not None:
+            import torch
+            t = torch.randn(tuple(shape), generator=tgen, device=torch_device, dtype=torch.float32) * std
+            if dtype == "bfloat16" and quant is None:
+                emit(name, t.to(torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16), "bfloat16")
+                continue
+            w = t.cpu().numpy()
         else:
             w = rng.standard_normal(shape, dtype=np.float32)
             w *= np.float32(std)
@@ -334,7 +349,8 @@ def write_synthetic_bundle(
         "tokenizer_runtime_file": "tokenizer/tokenizer_runtime.json",
         "tensors": records,
         "tokenizer": {"runtime_file": "tokenizer_runtime.json"},
-        "synthetic": {"seed": seed, "std": std, "dtype": dtype, "quant": quant},
+        "synthetic": {"seed": seed, "std": std, "dtype": dtype, "quant": quant,
+                      "generator": "numpy.default_rng" if torch_device is None else f"torch.randn({torch_device})"},
     }
     path = out / "manifest.json"
     path.write_text(json.dumps(manifest, indent=1))
@@ -410,7 +426,7 @@ def load_tensor(manifest: dict[str, Any], name: str) -> np.ndarray:
 
 
 def cached_bundle(name: str, cfg: dict[str, Any], seed: int, dtype: str = "float16",
-                  quant: str | None = None, root: str | None = None) -> Path:
+                  quant: str | None = None, root: str | None = None, torch_device: str | None = None) -> Path:
     """Write a synthetic bundle once under ``root`` (default: a temp dir) and reuse it."""
     root = root or os.environ.get("SOC_B200_BUNDLE_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "soc_b200_bundles"))
     out = Path(root) / name
@@ -419,7 +435,7 @@ def cached_bundle(name: str, cfg: dict[str, Any], seed: int, dtype: str = "float
     if manifest.exists() and stamp.exists():
         return manifest
     tmp = Path(root) / (name + f".tmp{os.getpid()}")
-    write_synthetic_bundle(tmp, cfg, seed=seed, dtype=dtype, quant=quant)
+    write_synthetic_bundle(tmp, cfg, seed=seed, dtype=dtype, quant=quant, torch_device=torch_device)
     (tmp / ".complete").write_text("ok")
     out.parent.mkdir(parents=True, exist_ok=True)
     if out.exists():

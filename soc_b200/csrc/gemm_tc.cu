@@ -144,6 +144,32 @@ __device__ __forceinline__ void store_half(T* hi, T* lo, size_t i, float f) {
     if (lo != nullptr) lo[i] = to_w<T>(f - static_cast<float>(h));
 }
 
+// 8 consecutive values -> 8 T in one 16-byte store (and their remainders when lo != null).
+template <typename T>
+__device__ __forceinline__ void store8_half(T* hi, T* lo, const float* f) {
+    uint4 ph, pl;
+    uint32_t* h = reinterpret_cast<uint32_t*>(&ph);
+    uint32_t* l = reinterpret_cast<uint32_t*>(&pl);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const T a = to_w<T>(f[2 * j]), b = to_w<T>(f[2 * j + 1]);
+        h[j] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&a)) |
+               (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&b)) << 16);
+        if (lo != nullptr) {
+            const T c = to_w<T>(f[2 * j] - static_cast<float>(a)), d = to_w<T>(f[2 * j + 1] - static_cast<float>(b));
+            l[j] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&c)) |
+                   (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&d)) << 16);
+        }
+    }
+    *reinterpret_cast<uint4*>(hi) = ph;
+    if (lo != nullptr) *reinterpret_cast<uint4*>(lo) = pl;
+}
+
+template <typename T>
+__device__ __forceinline__ bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
 template <typename T>
 __device__ __forceinline__ void epilogue(const float (&v)[32], int row, int col, int M, int N, void* y, void* y_lo,
                                          int ldy, int mode, int out_half) {
@@ -153,6 +179,14 @@ __device__ __forceinline__ void epilogue(const float (&v)[32], int row, int col,
         if (out_half) {
             T* yr = static_cast<T*>(y) + static_cast<size_t>(row) * ldy;
             T* yl = y_lo ? static_cast<T*>(y_lo) + static_cast<size_t>(row) * ldy : nullptr;
+            if (o + 16 <= no && aligned16<T>(yr + o) && (yl == nullptr || aligned16<T>(yl + o))) {
+                float g[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) g[j] = silu_f(v[2 * j]) * v[2 * j + 1];
+                store8_half<T>(yr + o, yl ? yl + o : nullptr, g);
+                store8_half<T>(yr + o + 8, yl ? yl + o + 8 : nullptr, g + 8);
+                return;
+            }
 #pragma unroll
             for (int j = 0; j < 16; ++j)
                 if (o + j < no) store_half<T>(yr, yl, o + j, silu_f(v[2 * j]) * v[2 * j + 1]);
@@ -167,6 +201,11 @@ __device__ __forceinline__ void epilogue(const float (&v)[32], int row, int col,
     if (out_half) {
         T* yr = static_cast<T*>(y) + static_cast<size_t>(row) * ldy;
         T* yl = y_lo ? static_cast<T*>(y_lo) + static_cast<size_t>(row) * ldy : nullptr;
+        if (col + 32 <= N && aligned16<T>(yr + col) && (yl == nullptr || aligned16<T>(yl + col))) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) store8_half<T>(yr + col + j, yl ? yl + col + j : nullptr, v + j);
+            return;
+        }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
             if (col + j < N) store_half<T>(yr, yl, col + j, v[j]);
@@ -321,34 +360,64 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 }
 
 // One CTA per row: optional RMSNorm (x * (1/sqrt(mean(x^2) + eps)) * w), cast to T; with
-// out_lo also the remainder x' - float(T(x')) cast to T.
+// out_lo also the remainder x' - float(T(x')) cast to T.  Each thread keeps up to RV float4
+// of the row in registers between the sum of squares and the scaled store.
+constexpr int R2H_RV = 4;
 template <typename T>
-__global__ void __launch_bounds__(256) k_rows_to_half(const float* __restrict__ x, int ldx, int cols,
-                                                      const float* __restrict__ w, float eps, T* __restrict__ out,
-                                                      T* __restrict__ out_lo, int ldo) {
-    __shared__ float red[8];
+__global__ void __launch_bounds__(1024) k_rows_to_half(const float* __restrict__ x, int ldx, int cols,
+                                                       const float* __restrict__ w, float eps, T* __restrict__ out,
+                                                       T* __restrict__ out_lo, int ldo) {
+    __shared__ float red[32];
     __shared__ float scale;
     const float* xr = x + static_cast<size_t>(blockIdx.x) * ldx;
     T* orow = out + static_cast<size_t>(blockIdx.x) * ldo;
     T* lrow = out_lo ? out_lo + static_cast<size_t>(blockIdx.x) * ldo : nullptr;
+    const int n4 = cols >> 2;
+    float4 v[R2H_RV];
+    float ss = 0.0f;
+#pragma unroll
+    for (int u = 0; u < R2H_RV; ++u) {
+        const int i = threadIdx.x + u * blockDim.x;
+        v[u] = i < n4 ? reinterpret_cast<const float4*>(xr)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+    }
     float s = 1.0f;
     if (w != nullptr) {
-        float ss = 0.0f;
-        for (int i = threadIdx.x; i < cols; i += blockDim.x) ss += xr[i] * xr[i];
         ss = warp_sum(ss);
         if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
         __syncthreads();
-        if (threadIdx.x == 0) {
-            float t = 0.0f;
-            for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) t += red[i];
-            scale = 1.0f / sqrtf(t / static_cast<float>(cols) + eps);
+        if (threadIdx.x < 32) {
+            float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+            t = warp_sum(t);
+            if (threadIdx.x == 0) scale = 1.0f / sqrtf(t / static_cast<float>(cols) + eps);
         }
         __syncthreads();
         s = scale;
     }
-    for (int i = threadIdx.x; i < cols; i += blockDim.x) {
-        const float v = w != nullptr ? xr[i] * s * w[i] : xr[i];
-        store_half<T>(orow, lrow, i, v);
+#pragma unroll
+    for (int u = 0; u < R2H_RV; ++u) {
+        const int i = threadIdx.x + u * blockDim.x;
+        if (i >= n4) break;
+        float f[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        if (w != nullptr) {
+            const float4 g = reinterpret_cast<const float4*>(w)[i];
+            f[0] = f[0] * s * g.x;
+            f[1] = f[1] * s * g.y;
+            f[2] = f[2] * s * g.z;
+            f[3] = f[3] * s * g.w;
+        }
+        uint2 ph, pl;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const T a = to_w<T>(f[2 * j]), b = to_w<T>(f[2 * j + 1]);
+            (&ph.x)[j] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&a)) |
+                         (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&b)) << 16);
+            const T c = to_w<T>(f[2 * j] - static_cast<float>(a)), d = to_w<T>(f[2 * j + 1] - static_cast<float>(b));
+            (&pl.x)[j] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&c)) |
+                         (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&d)) << 16);
+        }
+        reinterpret_cast<uint2*>(orow)[i] = ph;
+        if (lrow != nullptr) reinterpret_cast<uint2*>(lrow)[i] = pl;
     }
 }
 
@@ -535,13 +604,19 @@ void launch_gemm_tc(int wfmt, const CUtensorMap& a, const CUtensorMap* a_lo, con
 void launch_rows_to_half(int wfmt, const float* x, int ldx, int rows, int cols, const float* norm_w, float eps,
                          void* out, void* out_lo, int ldo, cudaStream_t st) {
     if (rows <= 0) return;
+    if (cols % 4 != 0 || ldx % 4 != 0 || ldo % 4 != 0) throw Error(-1, "row conversion needs multiples of 4 columns");
+    const int n4 = cols / 4;
+    int threads = (n4 + R2H_RV - 1) / R2H_RV;
+    threads = (threads + 31) / 32 * 32;
+    if (threads > 1024) throw Error(-1, "row conversion supports at most 16384 columns");
+    if (threads < 32) threads = 32;
     if (wfmt == WF_BF16)
-        k_rows_to_half<__nv_bfloat16><<<rows, 256, 0, st>>>(x, ldx, cols, norm_w, eps,
-                                                            static_cast<__nv_bfloat16*>(out),
-                                                            static_cast<__nv_bfloat16*>(out_lo), ldo);
+        k_rows_to_half<__nv_bfloat16><<<rows, threads, 0, st>>>(x, ldx, cols, norm_w, eps,
+                                                                static_cast<__nv_bfloat16*>(out),
+                                                                static_cast<__nv_bfloat16*>(out_lo), ldo);
     else
-        k_rows_to_half<__half><<<rows, 256, 0, st>>>(x, ldx, cols, norm_w, eps, static_cast<__half*>(out),
-                                                     static_cast<__half*>(out_lo), ldo);
+        k_rows_to_half<__half><<<rows, threads, 0, st>>>(x, ldx, cols, norm_w, eps, static_cast<__half*>(out),
+                                                         static_cast<__half*>(out_lo), ldo);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }

@@ -540,9 +540,9 @@ __global__ void k_attn_combine(const float* __restrict__ part, int hq, int n_spl
 }
 
 // Decode-shaped attention (few rows per sequence): CTA = (row, kv head, key split), 4
-// warps; a group of LPK lanes owns one key at a time (LPK = 8, or 16 for 8 query heads per
-// kv head), each lane DPL = D / LPK dims of it, so 32 / LPK keys are in flight per warp
-// step and the K/V rows are read as contiguous 16-byte vectors.  Every group keeps its own
+// warps; a group of LPK lanes owns one key at a time (LPK = 8, or 16 for 4 or more query
+// heads per kv head at head_dim 128), each lane DPL = D / LPK dims of it, so 32 / LPK keys
+// are in flight per warp step and the K/V rows are read as contiguous 16-byte vectors.  Every group keeps its own
 // online-softmax state for the G query heads of the kv head (base-2 exponent, log2(e)
 // folded into the query scale); the groups and warps are merged in shared memory at the
 // end.  The next key's K/V vectors are loaded before the current key is consumed.
@@ -550,7 +550,7 @@ template <int D, int G>
 __global__ void __launch_bounds__(128) k_attn_rows(const float* __restrict__ q, const int* __restrict__ row_seq,
                                                    const int* __restrict__ row_pos, int hq, int hkv, KVLayerView kv,
                                                    int n_splits, float* __restrict__ out, float* __restrict__ part) {
-    constexpr int LPK = (G >= 8 && D >= 128) ? 16 : 8, DPL = D / LPK, KPW = 32 / LPK, NW = 4, NS = NW * KPW;
+    constexpr int LPK = (G >= 4 && D >= 128) ? 16 : 8, DPL = D / LPK, KPW = 32 / LPK, NW = 4, NS = NW * KPW;
     constexpr int NV = DPL / 8;  // 16-byte vectors per lane per key row
     __shared__ float sm_m[NS][G], sm_l[NS][G];
     __shared__ float sm_o[NS][G][D];

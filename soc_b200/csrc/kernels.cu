@@ -12,6 +12,8 @@
 // The B200 layout differs from the reference: the KV cache is paged fp16, q/k/v are one
 // fused matrix, gate/up rows are interleaved so one warp owns a (gate, up) pair.
 #include <atomic>
+#include <cstdlib>
+#include <string>
 
 #include "kernels.h"
 
@@ -545,7 +547,7 @@ __global__ void k_attn_combine(const float* __restrict__ part, int hq, int n_spl
 // are in flight per warp step and the K/V rows are read as contiguous 16-byte vectors.  Every group keeps its own
 // online-softmax state for the G query heads of the kv head (base-2 exponent, log2(e)
 // folded into the query scale); the groups and warps are merged in shared memory at the
-// end.  The next key's K/V vectors are loaded before the current key is consumed.
+// end.  The K/V vectors of the next two keys of a group are in flight while it consumes one.
 template <int D, int G>
 __global__ void __launch_bounds__(128) k_attn_rows(const float* __restrict__ q, const int* __restrict__ row_seq,
                                                    const int* __restrict__ row_pos, int hq, int hkv, KVLayerView kv,
@@ -598,12 +600,14 @@ __global__ void __launch_bounds__(128) k_attn_rows(const float* __restrict__ q, 
             }
         }
     };
+    // keys p (consumed), p + NS and p + 2 NS (in flight)
     int p = kb + warp * KPW + grp;
-    uint4 kc[NV], vc[NV];
+    uint4 kc[NV], vc[NV], k1[NV], v1[NV];
     load(p, kc, vc);
+    load(p + NS, k1, v1);
     for (; p - grp < ke; p += NS) {
         uint4 kn[NV], vn[NV];
-        load(p + NS, kn, vn);
+        load(p + 2 * NS, kn, vn);
         if (p < ke) {
             float kf[DPL], vf[DPL];
 #pragma unroll
@@ -642,8 +646,10 @@ __global__ void __launch_bounds__(128) k_attn_rows(const float* __restrict__ q, 
         }
 #pragma unroll
         for (int c = 0; c < NV; ++c) {
-            kc[c] = kn[c];
-            vc[c] = vn[c];
+            kc[c] = k1[c];
+            vc[c] = v1[c];
+            k1[c] = kn[c];
+            v1[c] = vn[c];
         }
     }
     const int slot = warp * KPW + grp;
@@ -696,6 +702,12 @@ static bool attn_rows_d(int G, dim3 grid, const float* q, const Rows& rows, int 
     }
 }
 
+// SOC_B200_ATTENTION=rows selects the register-prefetch kernel instead of page streaming.
+int attention_path() {
+    const char* e = std::getenv("SOC_B200_ATTENTION");
+    return (e && std::string(e) == "rows") ? 1 : 0;
+}
+
 int attention_splits(int rows, int hkv, int max_visible) {
     // enough CTAs for two waves, and no split longer than 512 keys (long contexts of a
     // ragged batch would otherwise form the tail)
@@ -710,7 +722,8 @@ int attention_splits(int rows, int hkv, int max_visible) {
 }
 
 void launch_attention(const float* q, const Rows& rows, int splits, int hq, int hkv, int head_dim,
-                      const KVLayerView& kv, float* out, float* scratch, size_t scratch_floats, cudaStream_t st) {
+                      const KVLayerView& kv, float* out, float* scratch, size_t scratch_floats, int* err,
+                      cudaStream_t st) {
     if (rows.n <= 0) return;
     if (hq % hkv != 0 || hq / hkv > ATT_MAXG) throw Error(-1, "attention: unsupported head grouping");
     if (splits < 1) splits = 1;
@@ -718,9 +731,10 @@ void launch_attention(const float* q, const Rows& rows, int splits, int hq, int 
     if (splits > 1 && (scratch == nullptr || need > scratch_floats)) throw Error(-5, "attention: split-K scratch too small");
     dim3 grid(rows.n, hkv, splits);
     const int G = hq / hkv;
-    bool done = false;
-    if (head_dim == 128) done = attn_rows_d<128>(G, grid, q, rows, hq, hkv, kv, splits, out, scratch, st);
-    else if (head_dim == 64) done = attn_rows_d<64>(G, grid, q, rows, hq, hkv, kv, splits, out, scratch, st);
+    bool done = attention_path() == 0 &&
+                launch_attention_pages(q, rows, splits, hq, hkv, head_dim, kv, out, scratch, err, st);
+    if (!done && head_dim == 128) done = attn_rows_d<128>(G, grid, q, rows, hq, hkv, kv, splits, out, scratch, st);
+    else if (!done && head_dim == 64) done = attn_rows_d<64>(G, grid, q, rows, hq, hkv, kv, splits, out, scratch, st);
     if (done) {
         if (splits > 1) {
             if (head_dim == 128) k_attn_combine<128><<<dim3(rows.n, hq), 128, 0, st>>>(scratch, hq, splits, out);

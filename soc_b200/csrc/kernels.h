@@ -41,7 +41,12 @@ void launch_qk_norm_rope_kv(const float* qkv, const Rows& rows, int hq, int hkv,
 // (computed per row on the device).  `scratch` (may be null when splits == 1) holds the split-K
 // partials: rows*hq*splits*(head_dim + 2) floats.
 void launch_attention(const float* q, const Rows& rows, int splits, int hq, int hkv, int head_dim,
-                      const KVLayerView& kv, float* out, float* scratch, size_t scratch_floats, cudaStream_t st);
+                      const KVLayerView& kv, float* out, float* scratch, size_t scratch_floats, int* err,
+                      cudaStream_t st);
+// Page-streaming variant (attn_decode.cu) used by launch_attention; false when the shape is
+// outside its instances (16-token pages, head_dim 64/128, 1/2/4/8 query heads per kv head).
+bool launch_attention_pages(const float* q, const Rows& rows, int splits, int hq, int hkv, int head_dim,
+                            const KVLayerView& kv, float* out, float* scratch, int* err, cudaStream_t st);
 int attention_splits(int rows, int hkv, int max_visible);
 
 // Causal attention of the n rows of one prefill chunk (row r = position start + r of

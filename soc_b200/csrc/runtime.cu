@@ -683,7 +683,7 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
         else
             launch_attention(m->q, rows, splits, static_cast<int>(c.hq), static_cast<int>(c.hkv),
                              static_cast<int>(c.hd), kv->view(static_cast<int>(l)), m->att, m->attn_scratch,
-                             m->attn_scratch_floats, st);
+                             m->attn_scratch_floats, m->ctx->d_err, st);
         if (tc) {
             launch_rows_to_half(gf, m->att, QW, n, QW, nullptr, eps, m->xa, xlo, QW, st);
             launch_gemm_tc(gf, a_att, split ? &a_att_lo : nullptr, wmap(w.tm_o, w.wo, w.so, H, QW, m->tm_dq_o), n, H,

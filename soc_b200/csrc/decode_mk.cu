@@ -673,34 +673,67 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                     }
                 }
             }
+            // KB keys at a time: their dot products reduce in one interleaved shuffle tree and
+            // the running softmax is rescaled once per batch (KB + 1 exponentials, not 2 KB).
+            constexpr int KB = 4;
 #pragma unroll
-            for (int i = 0; i < KPF; ++i) {
-                const int key = base + NC * i;
-                if (key >= ke) break;
-                float kf[DL], vf[DL];
-                if (key == pos) {
+            for (int i0 = 0; i0 < KPF; i0 += KB) {
+                if (base + NC * i0 >= ke) break;
+                float kf[KB][DL], vf[KB][DL];
+                bool ok[KB];
 #pragma unroll
-                    for (int q = 0; q < DL; ++q) {
-                        kf[q] = ks[lane * DL + q];
-                        vf[q] = vs[lane * DL + q];
+                for (int b = 0; b < KB; ++b) {
+                    const int key = base + NC * (i0 + b);
+                    ok[b] = key < ke;
+                    if (!ok[b]) {  // past the split: the prefetch registers hold nothing (0 * NaN)
+#pragma unroll
+                        for (int q = 0; q < DL; ++q) kf[b][q] = vf[b][q] = 0.0f;
+                    } else if (key == pos) {
+#pragma unroll
+                        for (int q = 0; q < DL; ++q) {
+                            kf[b][q] = ks[lane * DL + q];
+                            vf[b][q] = vs[lane * DL + q];
+                        }
+                    } else {
+                        unpack_kv(kraw[i0 + b], kf[b]);
+                        unpack_kv(vraw[i0 + b], vf[b]);
                     }
-                } else {
-                    unpack_kv(kraw[i], kf);
-                    unpack_kv(vraw[i], vf);
                 }
 #pragma unroll
                 for (int g = 0; g < MAXG; ++g) {
                     if (g >= G) break;
-                    float d = 0.0f;
+                    float d[KB];
 #pragma unroll
-                    for (int q = 0; q < DL; ++q) d += qr[g][q] * kf[q];
-                    d = warp_sum(d) * scale;
-                    const float mn = fmaxf(m[g], d);
+                    for (int b = 0; b < KB; ++b) {
+                        d[b] = 0.0f;
+#pragma unroll
+                        for (int q = 0; q < DL; ++q) d[b] += qr[g][q] * kf[b][q];
+                    }
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                        for (int b = 0; b < KB; ++b) d[b] += __shfl_xor_sync(0xffffffffu, d[b], off);
+                    float mn = m[g];
+#pragma unroll
+                    for (int b = 0; b < KB; ++b) {
+                        d[b] = ok[b] ? d[b] * scale : -INFINITY;
+                        mn = fmaxf(mn, d[b]);
+                    }
                     const float corr = expf(m[g] - mn);
-                    const float pe = expf(d - mn);
-                    lsum[g] = lsum[g] * corr + pe;
+                    float ps = 0.0f, pe[KB];
 #pragma unroll
-                    for (int q = 0; q < DL; ++q) o[g][q] = o[g][q] * corr + pe * vf[q];
+                    for (int b = 0; b < KB; ++b) {
+                        pe[b] = ok[b] ? expf(d[b] - mn) : 0.0f;
+                        ps += pe[b];
+                    }
+                    lsum[g] = lsum[g] * corr + ps;
+#pragma unroll
+                    for (int q = 0; q < DL; ++q) {
+                        float acc = o[g][q] * corr;
+#pragma unroll
+                        for (int b = 0; b < KB; ++b) acc += pe[b] * vf[b][q];
+                        o[g][q] = acc;
+                    }
                     m[g] = mn;
                 }
             }

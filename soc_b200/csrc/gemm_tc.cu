@@ -511,7 +511,7 @@ bool tc_available() { return encode_fn() != nullptr; }
 
 int tc_min_rows() {
     const char* e = std::getenv("SOC_B200_TC_MIN_ROWS");
-    return e && *e ? std::atoi(e) : 4;
+    return e && *e ? std::atoi(e) : 16;
 }
 
 int tc_split_max_rows() {

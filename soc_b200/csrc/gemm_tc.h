@@ -10,9 +10,9 @@ namespace socb {
 
 // Whether this process can build TMA descriptors (driver entry point present).
 bool tc_available();
-// Rows from which the fp16/bf16 linears of a forward run on the tensor-core GEMM (default 4;
+// Rows from which the fp16/bf16 linears of a forward run on the tensor-core GEMM (default 16;
 // SOC_B200_TC_MIN_ROWS overrides it, 0 disables the path); group-quantised linears use it
-// from 4 * that many rows (their weights are expanded to fp16 first).
+// from 2 * that many rows (their weights are expanded to fp16 first).
 int tc_min_rows();
 // Up to this many rows (default 512, SOC_B200_TC_SPLIT_MAX_ROWS) the GEMM input rows are
 // carried as hi + lo halves (two MMAs per K step, about 22 significand bits); above it as

@@ -102,8 +102,8 @@ void launch_rmsnorm(const float* x, int rows, int n, const float* w, float eps, 
 }
 
 // ------------------------------------------------------------------------ linear
-// One CTA = 8 warps = 16 output rows (a warp owns a row pair) x RB input rows staged in
-// shared memory.  Every lane streams 16-byte weight vectors (Codec<F>::EPV elements) with
+// One CTA = 8 warps x NWR output rows (a warp owns NWR consecutive rows, whole SwiGLU pairs)
+// x RB input rows staged in shared memory.  Every lane streams 16-byte weight vectors (Codec<F>::EPV elements) with
 // the loads of UNR iterations issued before their FMAs, fp32 accumulation, warp-shuffle
 // reduction.  Group-quantised formats multiply the lane's partial sum over one group
 // slice by that group's fp16 scale.  The RMSNorm of the input rows (when norm_w !=
@@ -126,7 +126,7 @@ __device__ __forceinline__ int lin_slot(int k) {
     return blk * (32 * EPV) + ((e >> 3) * 32 + ln) * 8 + (e & 7);
 }
 
-template <int F, int RB>
+template <int F, int RB, int NWR>
 __global__ void __launch_bounds__(LIN_THREADS) k_linear(const uint8_t* __restrict__ W, const __half* __restrict__ S,
                                                         int out_f, int in_f, const float* __restrict__ x, int ldx,
                                                         int rows, const float* __restrict__ norm_w, float eps,
@@ -174,97 +174,107 @@ __global__ void __launch_bounds__(LIN_THREADS) k_linear(const uint8_t* __restric
     }
     __syncthreads();
 
-    const int pair = blockIdx.x * LIN_WARPS + warp;
-    const int o0 = 2 * pair;
+    // This warp's NWR consecutive output rows (NWR even: SwiGLU pairs stay together).
+    const int o0 = NWR * (blockIdx.x * LIN_WARPS + warp);
     if (o0 >= out_f) return;
-    const bool has1 = (o0 + 1) < out_f;
     const size_t row_bytes = static_cast<size_t>(in_f) / EPV * 16;
-    const uint8_t* w0 = W + static_cast<size_t>(o0) * row_bytes;
-    const uint8_t* w1 = has1 ? w0 + row_bytes : w0;
     const int ng = G ? in_f / G : 0;
-    const __half* s0 = G ? S + static_cast<size_t>(o0) * ng : nullptr;
-    const __half* s1 = (G && has1) ? s0 + ng : s0;
-
-    float acc0[RB], acc1[RB];
+    const uint8_t* wr[NWR];
+    const __half* sr[NWR];
 #pragma unroll
-    for (int r = 0; r < RB; ++r) acc0[r] = acc1[r] = 0.0f;
+    for (int i = 0; i < NWR; ++i) {
+        const int o = o0 + i < out_f ? o0 + i : o0;
+        wr[i] = W + static_cast<size_t>(o) * row_bytes;
+        sr[i] = G ? S + static_cast<size_t>(o) * ng : nullptr;
+    }
 
-    // One 16-byte vector of each of the two rows: vector index vv (lane = vv % 32).
-    auto consume = [&](const uint4& ua, const uint4& ub, float sa, float sb, int vv) {
+    float acc[NWR][RB];
+#pragma unroll
+    for (int i = 0; i < NWR; ++i)
+#pragma unroll
+        for (int r = 0; r < RB; ++r) acc[i][r] = 0.0f;
+
+    // One 16-byte vector of each row: vector index vv (lane = vv % 32).  Every x float4 read
+    // from shared memory feeds NWR rows.
+    auto consume = [&](const uint4 (&u)[NWR], const float (&sc)[NWR], int vv) {
         const int base = (vv >> 5) * (32 * EPV) + lane * 8;
-        float t0[RB], t1[RB];
+        float t[NWR][RB];
 #pragma unroll
-        for (int r = 0; r < RB; ++r) t0[r] = t1[r] = 0.0f;
+        for (int i = 0; i < NWR; ++i)
+#pragma unroll
+            for (int r = 0; r < RB; ++r) t[i][r] = 0.0f;
 #pragma unroll
         for (int p = 0; p < NP; ++p) {
-            float wa[8], wb[8];
-            C::part(ua, p, wa);
-            C::part(ub, p, wb);
+            float w[NWR][8];
+#pragma unroll
+            for (int i = 0; i < NWR; ++i) C::part(u[i], p, w[i]);
             const int off = base + p * 256;
 #pragma unroll
             for (int r = 0; r < RB; ++r) {
                 const float4 xa = xs4[(r * pin + off) >> 2];
                 const float4 xb = xs4[(r * pin + off + 4) >> 2];
-                t0[r] += wa[0] * xa.x + wa[1] * xa.y + wa[2] * xa.z + wa[3] * xa.w + wa[4] * xb.x + wa[5] * xb.y +
-                         wa[6] * xb.z + wa[7] * xb.w;
-                t1[r] += wb[0] * xa.x + wb[1] * xa.y + wb[2] * xa.z + wb[3] * xa.w + wb[4] * xb.x + wb[5] * xb.y +
-                         wb[6] * xb.z + wb[7] * xb.w;
+#pragma unroll
+                for (int i = 0; i < NWR; ++i)
+                    t[i][r] += w[i][0] * xa.x + w[i][1] * xa.y + w[i][2] * xa.z + w[i][3] * xa.w + w[i][4] * xb.x +
+                               w[i][5] * xb.y + w[i][6] * xb.z + w[i][7] * xb.w;
             }
         }
 #pragma unroll
-        for (int r = 0; r < RB; ++r) {
-            if (G) {
-                acc0[r] = fmaf(sa, t0[r], acc0[r]);
-                acc1[r] = fmaf(sb, t1[r], acc1[r]);
-            } else {
-                acc0[r] += t0[r];
-                acc1[r] += t1[r];
-            }
-        }
+        for (int i = 0; i < NWR; ++i)
+#pragma unroll
+            for (int r = 0; r < RB; ++r) acc[i][r] = G ? fmaf(sc[i], t[i][r], acc[i][r]) : acc[i][r] + t[i][r];
     };
 
-    constexpr int UNR = EPV == 8 ? 4 : 2;
+    constexpr int UNR = (EPV == 8 ? 8 : 4) / NWR;
     const int nv = in_f / EPV;
     int v = lane;
     for (; v + 32 * (UNR - 1) < nv; v += 32 * UNR) {
-        uint4 ua[UNR], ub[UNR];
-        float sa[UNR], sb[UNR];
+        uint4 u[UNR][NWR];
+        float sc[UNR][NWR];
 #pragma unroll
-        for (int u = 0; u < UNR; ++u) {
-            ua[u] = ld_nc16(w0 + static_cast<size_t>(v + 32 * u) * 16);
-            ub[u] = ld_nc16(w1 + static_cast<size_t>(v + 32 * u) * 16);
-            sa[u] = G ? __half2float(s0[(v + 32 * u) * EPV / (G ? G : 1)]) : 1.0f;
-            sb[u] = G ? __half2float(s1[(v + 32 * u) * EPV / (G ? G : 1)]) : 1.0f;
-        }
+        for (int k = 0; k < UNR; ++k)
 #pragma unroll
-        for (int u = 0; u < UNR; ++u) consume(ua[u], ub[u], sa[u], sb[u], v + 32 * u);
+            for (int i = 0; i < NWR; ++i) {
+                u[k][i] = ld_nc16(wr[i] + static_cast<size_t>(v + 32 * k) * 16);
+                sc[k][i] = G ? __half2float(sr[i][(v + 32 * k) * EPV / (G ? G : 1)]) : 1.0f;
+            }
+#pragma unroll
+        for (int k = 0; k < UNR; ++k) consume(u[k], sc[k], v + 32 * k);
     }
     for (; v < nv; v += 32) {
-        const uint4 ua = ld_nc16(w0 + static_cast<size_t>(v) * 16);
-        const uint4 ub = ld_nc16(w1 + static_cast<size_t>(v) * 16);
-        const float sa = G ? __half2float(s0[v * EPV / (G ? G : 1)]) : 1.0f;
-        const float sb = G ? __half2float(s1[v * EPV / (G ? G : 1)]) : 1.0f;
-        consume(ua, ub, sa, sb, v);
+        uint4 u[NWR];
+        float sc[NWR];
+#pragma unroll
+        for (int i = 0; i < NWR; ++i) {
+            u[i] = ld_nc16(wr[i] + static_cast<size_t>(v) * 16);
+            sc[i] = G ? __half2float(sr[i][v * EPV / (G ? G : 1)]) : 1.0f;
+        }
+        consume(u, sc, v);
     }
 #pragma unroll
-    for (int r = 0; r < RB; ++r) {
-        acc0[r] = warp_sum(acc0[r]);
-        acc1[r] = warp_sum(acc1[r]);
-    }
+    for (int i = 0; i < NWR; ++i)
+#pragma unroll
+        for (int r = 0; r < RB; ++r) acc[i][r] = warp_sum(acc[i][r]);
     if (lane < nr) {
         // lane r writes input row r (register arrays indexed by a compile-time loop).
 #pragma unroll
         for (int r = 0; r < RB; ++r) {
             if (r != lane) continue;
             float* yr = y + static_cast<size_t>(r0 + r) * ldy;
-            if (mode == LIN_SWIGLU) {
-                yr[pair] = silu_f(acc0[r]) * acc1[r];
-            } else if (mode == LIN_RESIDUAL) {
-                yr[o0] += acc0[r];
-                if (has1) yr[o0 + 1] += acc1[r];
-            } else {
-                yr[o0] = acc0[r];
-                if (has1) yr[o0 + 1] = acc1[r];
+#pragma unroll
+            for (int i = 0; i < NWR; i += 2) {
+                if (mode == LIN_SWIGLU) {
+                    if (o0 + i + 1 < out_f) yr[(o0 + i) / 2] = silu_f(acc[i][r]) * acc[i + 1][r];
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        if (o0 + i + k >= out_f) continue;
+                        if (mode == LIN_RESIDUAL)
+                            yr[o0 + i + k] += acc[i + k][r];
+                        else
+                            yr[o0 + i + k] = acc[i + k][r];
+                    }
+                }
             }
         }
     }
@@ -275,16 +285,21 @@ constexpr size_t LIN_SMEM_CAP = 96 * 1024;  // fp32 staging budget that picks th
 template <int F, int RB>
 static void linear_rb(const void* W, const void* S, int out_f, int in_f, const float* x, int ldx, int rows,
                       const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    // One weight row pair per warp for a single input row; from two input rows on, four
+    // weight rows per warp halve the shared-memory reads of x per weight.
+    constexpr int NWR = RB >= 2 ? 4 : 2;
     const size_t smem = static_cast<size_t>(RB) * lin_padded<Codec<F>::EPV>(in_f) * sizeof(float);
     static bool attr_set = false;  // one attribute set per template instance
     if (!attr_set) {
-        SOCB_CUDA(cudaFuncSetAttribute(k_linear<F, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        SOCB_CUDA(cudaFuncSetAttribute(k_linear<F, RB, NWR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       200 * 1024));
         attr_set = true;
     }
-    const int pairs = (out_f + 1) / 2;
-    dim3 grid((pairs + LIN_WARPS - 1) / LIN_WARPS, (rows + RB - 1) / RB);
-    k_linear<F, RB><<<grid, LIN_THREADS, smem, st>>>(static_cast<const uint8_t*>(W), static_cast<const __half*>(S),
-                                                     out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode);
+    const int groups = (out_f + NWR - 1) / NWR;
+    dim3 grid((groups + LIN_WARPS - 1) / LIN_WARPS, (rows + RB - 1) / RB);
+    k_linear<F, RB, NWR><<<grid, LIN_THREADS, smem, st>>>(static_cast<const uint8_t*>(W),
+                                                          static_cast<const __half*>(S), out_f, in_f, x, ldx, rows,
+                                                          norm_w, eps, y, ldy, mode);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }

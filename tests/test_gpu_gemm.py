@@ -1,7 +1,8 @@
 """Tensor-core (tcgen05) GEMM of the prefill / batched-row linears.
 
-soc_b200_linear and the forward switch to the tcgen05 kernel from 4 rows (fp16/bf16
-weights; 16 rows for int8/int4, expanded to fp16 first).  Up to 512 rows the input rows are
+soc_b200_linear and the forward switch to the tcgen05 kernel from 16 rows (fp16/bf16
+weights; 32 rows for int8/int4, expanded to fp16 first); fewer rows run on the CUDA-core
+GEMV (the 4-row cases below).  Up to 512 rows the input rows are
 carried as hi + lo halves (fp32-level products); above that they are rounded once to the
 weight type (fp16: 11-bit, bf16: 8-bit significand) and accumulated in fp32, so the kernel
 cases compare against an fp64 product with tolerances scaled by that rounding; the model cases compare prefill logits with the

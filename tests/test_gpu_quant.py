@@ -128,7 +128,7 @@ def test_load_time_quantisation_equals_exported_bundle(gpu_ctx, make_bundle, tmp
 
 @pytest.mark.parametrize("quant", sorted(FORMATS))
 def test_quantized_prefill_tensor_core_path(qmodels, quant):
-    """40 prompt rows (>= 16): the quantised linears run as an fp16 expansion of each
+    """40 prompt rows (>= 32): the quantised linears run as an fp16 expansion of each
     matrix feeding the tensor-core GEMM.  Logits vs the oracle, then greedy decode."""
     p, m = qmodels("qwen06_shape_2layer", quant)
     prompt = np.random.default_rng(31).integers(0, QWEN3_0_6B["vocab_size"], 40).astype(np.int32)

@@ -18,6 +18,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "gemm_tc.h"
 #include "kernels.h"
@@ -38,7 +39,13 @@ struct TcCfg {
 static_assert(TcCfg<true>::STAGES * TcCfg<true>::STAGE_BYTES <= MAX_STAGES * (A_BYTES + W_BYTES), "ring size");
 constexpr int TC_THREADS = 192;
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s
-constexpr size_t TC_SMEM = MAX_STAGES * (A_BYTES + W_BYTES) + 1024 /* barriers */ + 1024 /* alignment */;
+constexpr int RING_BYTES = MAX_STAGES * (A_BYTES + W_BYTES);
+// fp32 outputs leave through shared memory: per epilogue warp two 32 x 32 fp32 staging
+// tiles (128-byte swizzle) that TMA stores (or reduce-adds, for the residual) to global.
+constexpr int STG_BYTES = 32 * 32 * 4;
+constexpr int STG_TOTAL = 4 * 2 * STG_BYTES;
+constexpr size_t TC_SMEM = RING_BYTES + STG_TOTAL + 1024 /* barriers */ + 1024 /* alignment */;
+static_assert(TC_SMEM <= 232448, "shared memory per CTA");
 
 struct TcBars {
     unsigned long long full[MAX_STAGES], empty[MAX_STAGES], acc_full[2], acc_empty[2];
@@ -235,12 +242,14 @@ template <typename T, bool SPLIT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap ta_lo,
               const __grid_constant__ CUtensorMap tw, int M, int N, int K, void* __restrict__ y,
-              void* __restrict__ y_lo, int ldy, int mode, int out_half, int ksplit, int* err) {
+              void* __restrict__ y_lo, int ldy, int mode, int out_half, int ksplit,
+              const __grid_constant__ CUtensorMap ty, int out_tma, int* err) {
     using Cfg = TcCfg<SPLIT>;
     constexpr int STAGES = Cfg::STAGES, STAGE_BYTES = Cfg::STAGE_BYTES, W_OFF = Cfg::A_TILES * A_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    TcBars* bars = reinterpret_cast<TcBars*>(smem + STAGES * STAGE_BYTES);
+    static_assert(STAGES * STAGE_BYTES <= RING_BYTES, "ring");
+    TcBars* bars = reinterpret_cast<TcBars*>(smem + RING_BYTES + STG_TOTAL);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN, tiles = mt * nt, kbn = (K + BK - 1) / BK;
     // Work unit u = (tile u % tiles, K slice u / tiles); with ksplit > 1 every slice writes
@@ -327,6 +336,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q = warp & 3;
         unsigned local = 0;
         const bool partial = ksplit > 1;
+        uint8_t* stg = smem + RING_BYTES + q * 2 * STG_BYTES;
+        unsigned sbuf = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
             const int t = u % tiles;
             const unsigned b = local & 1u;
@@ -341,15 +352,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (n0 + c >= N) break;
                 float v[32];
                 tmem_ld32(base + c, v);
-                if (partial)
+                if (out_tma) {
+                    // row `lane` of the warp's 32 x 32 fp32 block -> swizzled staging tile -> TMA
+                    uint8_t* buf = stg + (sbuf & 1) * STG_BYTES;
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    __syncwarp();
+                    float4* rowp = reinterpret_cast<float4*>(buf + lane * 128);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        rowp[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        const int x = n0 + c, yr = m0 + q * 32;
+                        if (partial)
+                            asm volatile(
+                                "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                                    &ty),
+                                "r"(su32(buf)), "r"(x), "r"(yr), "r"(u / tiles)
+                                : "memory");
+                        else if (mode == LIN_RESIDUAL)
+                            asm volatile(
+                                "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                                    &ty),
+                                "r"(su32(buf)), "r"(x), "r"(yr)
+                                : "memory");
+                        else
+                            asm volatile(
+                                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(&ty),
+                                "r"(su32(buf)), "r"(x), "r"(yr)
+                                : "memory");
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    }
+                    ++sbuf;
+                } else if (partial) {
                     epilogue<T>(v, row, n0 + c, M, N, yy, nullptr, N, LIN_STORE, 0);
-                else
+                } else {
                     epilogue<T>(v, row, n0 + c, M, N, y, y_lo, ldy, mode, out_half);
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->acc_empty[b]);
         }
+        // every TMA store of this warp has written global memory before the CTA exits
+        if (out_tma && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
@@ -514,6 +561,12 @@ int tc_min_rows() {
     return e && *e ? std::atoi(e) : 16;
 }
 
+// SOC_B200_TC_OUT=registers keeps the fp32 GEMM outputs on the register-store epilogue.
+int tc_out_tma() {
+    const char* e = std::getenv("SOC_B200_TC_OUT");
+    return (e && std::string(e) == "registers") ? 0 : 1;
+}
+
 int tc_split_max_rows() {
     const char* e = std::getenv("SOC_B200_TC_SPLIT_MAX_ROWS");
     return e && *e ? std::atoi(e) : 512;
@@ -536,6 +589,31 @@ void tc_make_map(CUtensorMap* map, const void* base, int wfmt, uint64_t rows, ui
     if (r != CUDA_SUCCESS) throw Error(-2, "cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r)));
 }
 
+// fp32 output descriptor for the TMA epilogue: [M, N] (ld `ld`), or [slices][M][N] for the
+// split-K partials; 32 x 32 boxes with 128-byte swizzle.  False when the operand breaks the
+// TMA alignment rules (the epilogue then stores from registers).
+bool make_out_map(CUtensorMap* map, void* base, int M, int N, int ld, int slices) {
+    auto fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) != 0 || ld % 4 != 0 || N % 4 != 0) return false;
+    const cuuint32_t es[3] = {1, 1, 1};
+    CUresult r;
+    if (slices <= 1) {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+        const cuuint32_t box[2] = {32, 32};
+        r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M),
+                                    static_cast<cuuint64_t>(slices)};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(N) * 4, static_cast<cuuint64_t>(M) * N * 4};
+        const cuuint32_t box[3] = {32, 32, 1};
+        r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    return r == CUDA_SUCCESS;
+}
+
 template <typename T, bool SPLIT>
 static void gemm_t(const CUtensorMap& a, const CUtensorMap& a_lo, const CUtensorMap& w, int M, int N, int K, void* y,
                    void* y_lo, int ldy, int mode, bool out_half, int ksplit, float* ws, int* err, int grid,
@@ -546,13 +624,16 @@ static void gemm_t(const CUtensorMap& a, const CUtensorMap& a_lo, const CUtensor
                                        static_cast<int>(TC_SMEM)));
         set = true;
     }
+    CUtensorMap ty{};
     if (ksplit <= 1) {
+        const bool tma = !out_half && mode != LIN_SWIGLU && tc_out_tma() && make_out_map(&ty, y, M, N, ldy, 1);
         k_gemm_tc<T, SPLIT><<<grid, TC_THREADS, TC_SMEM, st>>>(a, a_lo, w, M, N, K, y, y_lo, ldy, mode,
-                                                               out_half ? 1 : 0, 1, err);
+                                                               out_half ? 1 : 0, 1, ty, tma ? 1 : 0, err);
         return;
     }
+    const bool tma = tc_out_tma() && make_out_map(&ty, ws, M, N, N, ksplit);
     k_gemm_tc<T, SPLIT><<<grid, TC_THREADS, TC_SMEM, st>>>(a, a_lo, w, M, N, K, ws, nullptr, N, LIN_STORE, 0, ksplit,
-                                                           err);
+                                                           ty, tma ? 1 : 0, err);
     const size_t pairs = static_cast<size_t>(M) * (N / 2);
     const int rgrid = static_cast<int>(std::min<size_t>((pairs + 255) / 256, 148 * 16));
     k_splitk_reduce<T><<<rgrid, 256, 0, st>>>(ws, ksplit, M, N, y, y_lo, ldy, mode, out_half ? 1 : 0);

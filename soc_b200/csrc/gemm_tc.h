@@ -18,6 +18,9 @@ int tc_min_rows();
 // carried as hi + lo halves (two MMAs per K step, about 22 significand bits); above it as
 // one half (prefill-sized GEMMs, tensor-throughput bound).
 int tc_split_max_rows();
+// 1 (default): fp32 GEMM outputs leave through shared memory and TMA stores / reduce-adds;
+// SOC_B200_TC_OUT=registers: stores from the epilogue threads' registers.
+int tc_out_tma();
 // 2-D TMA descriptor of a row-major [rows, cols] fp16/bf16 matrix with leading dimension
 // `ld` elements, box = 64 columns x box_rows rows, 128-byte swizzle.
 void tc_make_map(CUtensorMap* map, const void* base, int wfmt, uint64_t rows, uint64_t cols, uint64_t ld,

@@ -136,13 +136,16 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* b, unsigned parity
 // output waits (one thread, acquire) until the counter reaches (step + 1) * contributors.
 // A device-wide hand-off of this kind measured about 1 us on B200 with 148 CTAs; polling
 // one flag per CTA instead was about 4 us (148 writers and pollers on the same lines).
-//   [l * 6 + e]        e in {E_QKV, E_ATT, E_HO, E_ACT, E_HD}; E_ATT counts kv heads
-//   [L * 6]            lm_head done (per CTA)
-//   [L * 6 + 1 + l * hkv + j]  split-K arrivals of kv head j
-__device__ __forceinline__ unsigned* ctr(const MKParams& p, int l, int e) { return p.flags + l * 6 + e; }
-__device__ __forceinline__ unsigned* ctr_lm(const MKParams& p) { return p.flags + p.L * 6; }
+// Every counter sits on its own 128-byte line (FLAG_STRIDE words): counters that shared a
+// line made the pollers of one phase queue behind the adds of another.
+//   slot l * 6 + e     e in {E_QKV, E_ATT, E_HO, E_ACT, E_HD}; E_ATT counts kv heads
+//   slot L * 6         lm_head done (per CTA)
+//   slot L * 6 + 1 + l * hkv + j  split-K arrivals of kv head j
+constexpr int FLAG_STRIDE = 32;
+__device__ __forceinline__ unsigned* ctr(const MKParams& p, int l, int e) { return p.flags + (l * 6 + e) * FLAG_STRIDE; }
+__device__ __forceinline__ unsigned* ctr_lm(const MKParams& p) { return p.flags + p.L * 6 * FLAG_STRIDE; }
 __device__ __forceinline__ unsigned* split_ctr(const MKParams& p, int l, int j) {
-    return p.flags + p.L * 6 + 1 + l * p.hkv + j;
+    return p.flags + (p.L * 6 + 1 + l * p.hkv + j) * FLAG_STRIDE;
 }
 
 __device__ __forceinline__ void red_release_add(unsigned* c) {
@@ -945,7 +948,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_mk(MKParams p) {
 
 }  // namespace
 
-int mk_flag_count(int L, int hkv, int grid) { return L * 6 + 1 + L * hkv + 0 * grid; }
+int mk_flag_count(int L, int hkv, int grid) { return (L * 6 + 1 + L * hkv) * FLAG_STRIDE + 0 * grid; }
 
 size_t mk_vec_floats(int H, int I, int hq, int hkv, int D) {
     return static_cast<size_t>(H) + static_cast<size_t>(hq + 2 * hkv) * D + static_cast<size_t>(hq) * D + I;

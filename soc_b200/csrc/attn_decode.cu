@@ -14,6 +14,9 @@
 // per CTA without registers.  Groups and warps are merged in shared memory at the end; a
 // split writes unnormalised partials (natural-log max, sum) for k_attn_combine.  Every
 // mbarrier wait is bounded (2 s of %globaltimer): on expiry DERR_WAIT_TIMEOUT is recorded.
+#include <cstdlib>
+#include <string>
+
 #include "kernels.h"
 
 namespace socb {
@@ -227,11 +230,286 @@ __global__ void __launch_bounds__(AP_THREADS) k_attn_pages(const float* __restri
     }
 }
 
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+// Tensor-core variant: one consumer warp owns a whole page (16 keys) at a time and runs
+// the page as two m16n8k16 products with the G query heads padded to n = 8:
+//   S^T [16 keys x 8 heads] = K [16 x D] . Q^T        (A = K rows, ldmatrix)
+//   O^T [D x 8 heads]      += V^T [D x 16 keys] . P^T (A = V rows, ldmatrix.trans)
+// Q and P enter the MMAs as hi + lo fp16 halves (two MMAs each), which keeps the scores and
+// weights at about 22 significand bits; K and V are fp16 in the cache, so the products are
+// exact.  P goes through per-warp shared tiles to become the second product's B operand.  Each
+// warp keeps its own online softmax (one max and one rescale per page and head); the four
+// warps' states are merged at the end.
+template <int D, int G>
+__global__ void __launch_bounds__(AP_THREADS) k_attn_pages_mma(const float* __restrict__ q,
+                                                              const int* __restrict__ row_seq,
+                                                              const int* __restrict__ row_pos, int hq, int hkv,
+                                                              KVLayerView kv, int n_splits, float* __restrict__ out,
+                                                              float* __restrict__ part, int* err) {
+    constexpr int PT = 16, PAGE_B = PT * D * 2, KS = D / 16;
+    static_assert(G <= 8, "at most 8 query heads per kv head");
+    extern __shared__ __align__(128) uint8_t sm[];
+    uint8_t* ring = sm;                                                   // [NSLOT][K | V][PAGE_B]
+    unsigned long long* full = reinterpret_cast<unsigned long long*>(sm + NSLOT * 2 * PAGE_B);
+    unsigned long long* empty = full + NSLOT;
+    __half* ptile = reinterpret_cast<__half*>(sm + NSLOT * 2 * PAGE_B + 2 * NSLOT * 8);  // [CW][hi|lo][8][16]
+    float* mstate = reinterpret_cast<float*>(sm);  // after the loop: [CW][8][D + 2]
+
+    const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int seq = row_seq[row];
+    const int nvis = row_pos[row] + 1;
+    const int chunk = ((nvis + n_splits - 1) / n_splits + PT - 1) / PT * PT;
+    const int kb = split * chunk, ke = min(nvis, kb + chunk);
+    const int pg0 = kb / PT, npages = ke > kb ? (ke - kb + PT - 1) / PT : 0;
+    const int* pt = kv.page_table + static_cast<size_t>(seq) * kv.max_pages;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSLOT; ++s) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(full + s)) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(empty + s)) : "memory");
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncthreads();
+
+    // per thread: heads h0 = (lane % 4) * 2, h0 + 1 of the S / O fragments
+    const int h0 = (lane & 3) * 2;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+    float o[KS][4];
+#pragma unroll
+    for (int t = 0; t < KS; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+
+    if (warp == CW) {
+        if (lane == 0) {  // page producer
+            int i = 0;
+            for (; i < npages; ++i) {
+                const int s = i % NSLOT;
+                if (!mb_wait(empty + s, ((i / NSLOT) & 1u) ^ 1u, err)) break;
+                const int page = pt[pg0 + i];
+                const size_t off = (static_cast<size_t>(page) * hkv + kvh) * PT * D;
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(full + s)),
+                             "r"(2 * PAGE_B)
+                             : "memory");
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        su32(ring + s * 2 * PAGE_B)),
+                    "l"(kv.k + off), "r"(PAGE_B), "r"(su32(full + s))
+                    : "memory");
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        su32(ring + s * 2 * PAGE_B + PAGE_B)),
+                    "l"(kv.v + off), "r"(PAGE_B), "r"(su32(full + s))
+                    : "memory");
+            }
+            for (int j = i > NSLOT ? i - NSLOT : 0; j < i; ++j) mb_wait(full + j % NSLOT, (j / NSLOT) & 1u, err);
+        }
+    } else {
+        // Q^T as the B operand: b0 = (dims kk*16 + (lane%4)*2, +1; head lane/4), b1 = dims + 8.
+        const float qs = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+        const int hb = lane >> 2;
+        // hi + lo fp16 halves of the scaled query (x = hi + lo): the score keeps ~22 bits
+        uint32_t qb[KS][2], ql[KS][2];
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            float2 a = make_float2(0.f, 0.f), b = a;
+            if (hb < G) {
+                const float* qp = q + (static_cast<size_t>(row) * hq + kvh * G + hb) * D + kk * 16 + (lane & 3) * 2;
+                a = *reinterpret_cast<const float2*>(qp);
+                b = *reinterpret_cast<const float2*>(qp + 8);
+            }
+            const float f[4] = {a.x * qs, a.y * qs, b.x * qs, b.y * qs};
+            __half hi[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) hi[e] = __float2half_rn(f[e]);
+            qb[kk][0] = pack_h2(__half2float(hi[0]), __half2float(hi[1]));
+            qb[kk][1] = pack_h2(__half2float(hi[2]), __half2float(hi[3]));
+            ql[kk][0] = pack_h2(f[0] - __half2float(hi[0]), f[1] - __half2float(hi[1]));
+            ql[kk][1] = pack_h2(f[2] - __half2float(hi[2]), f[3] - __half2float(hi[3]));
+        }
+        __half* pw = ptile + warp * 2 * 8 * PT;  // hi tile, then lo tile
+        for (int i = warp; i < npages; i += CW) {
+            const int s = i % NSLOT;
+            if (!mb_wait(full + s, (i / NSLOT) & 1u, err)) break;
+            const uint32_t kpage = su32(ring + s * 2 * PAGE_B), vpage = kpage + PAGE_B;
+            // Positions past the split's last key hold whatever the pool held (possibly NaN
+            // patterns): their V rows are zeroed, since P = 0 times NaN is NaN in the MMA.
+            const int kvalid = ke - (pg0 + i) * PT;
+            if (kvalid < PT) {
+                uint4* vz = reinterpret_cast<uint4*>(ring + s * 2 * PAGE_B + PAGE_B + kvalid * D * 2);
+                for (int z = lane; z < (PT - kvalid) * D * 2 / 16; z += 32) vz[z] = make_uint4(0u, 0u, 0u, 0u);
+                __syncwarp();
+            }
+            // S^T = K . Q^T
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+            const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+                uint32_t a[4];
+                ldsm_x4(kpage + static_cast<uint32_t>((arow * D + kk * 16 + acol) * 2), a);
+                mma16816(sc, a, qb[kk][0], qb[kk][1]);
+                mma16816(sc, a, ql[kk][0], ql[kk][1]);
+            }
+            // sc[0], sc[1]: key lane/4, heads h0, h0+1; sc[2], sc[3]: key lane/4 + 8
+            const int key0 = (pg0 + i) * PT + (lane >> 2);
+            if (key0 >= ke) sc[0] = sc[1] = -INFINITY;
+            if (key0 + 8 >= ke) sc[2] = sc[3] = -INFINITY;
+            float pmax0 = fmaxf(sc[0], sc[2]), pmax1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                pmax0 = fmaxf(pmax0, __shfl_xor_sync(0xffffffffu, pmax0, off));
+                pmax1 = fmaxf(pmax1, __shfl_xor_sync(0xffffffffu, pmax1, off));
+            }
+            // the page's first key is always visible, so pmax is finite
+            const float mn0 = fmaxf(m[0], pmax0), mn1 = fmaxf(m[1], pmax1);
+            const float c0 = exp2f(m[0] - mn0), c1 = exp2f(m[1] - mn1);
+            m[0] = mn0;
+            m[1] = mn1;
+            const float p00 = exp2f(sc[0] - mn0), p01 = exp2f(sc[1] - mn1);
+            const float p10 = exp2f(sc[2] - mn0), p11 = exp2f(sc[3] - mn1);
+            l[0] = l[0] * c0 + p00 + p10;
+            l[1] = l[1] * c1 + p01 + p11;
+#pragma unroll
+            for (int t = 0; t < KS; ++t) {
+                o[t][0] *= c0;
+                o[t][1] *= c1;
+                o[t][2] *= c0;
+                o[t][3] *= c1;
+            }
+            // P [8 heads][16 keys] through the warp's tiles as hi + lo fp16 halves
+            const int kr = lane >> 2;
+            auto put = [&](int idx, float v) {
+                const __half h = __float2half_rn(v);
+                pw[idx] = h;
+                pw[8 * PT + idx] = __float2half_rn(v - __half2float(h));
+            };
+            put(h0 * PT + kr, p00);
+            put((h0 + 1) * PT + kr, p01);
+            put(h0 * PT + kr + 8, p10);
+            put((h0 + 1) * PT + kr + 8, p11);
+            __syncwarp();
+            const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(pw + hb * PT + (lane & 3) * 2);
+            const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(pw + hb * PT + 8 + (lane & 3) * 2);
+            const uint32_t pl0 = *reinterpret_cast<const uint32_t*>(pw + 8 * PT + hb * PT + (lane & 3) * 2);
+            const uint32_t pl1 = *reinterpret_cast<const uint32_t*>(pw + 8 * PT + hb * PT + 8 + (lane & 3) * 2);
+            // O^T += V^T . P^T ; A tile t = dims t*16.. from the V page, transposed
+            const int vkey = (lane & 7) + (lane >> 4) * 8, vdim = ((lane >> 3) & 1) * 8;
+#pragma unroll
+            for (int t = 0; t < KS; ++t) {
+                uint32_t a[4];
+                ldsm_x4_t(vpage + static_cast<uint32_t>((vkey * D + t * 16 + vdim) * 2), a);
+                mma16816(o[t], a, pb0, pb1);
+                mma16816(o[t], a, pl0, pl1);
+            }
+            // order this warp's generic writes to the slot before the next bulk copy into it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(empty + s)) : "memory");
+        }
+        // sum of p over the 16 keys of each head: lanes sharing lane % 4
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            l[0] += __shfl_xor_sync(0xffffffffu, l[0], off);
+            l[1] += __shfl_xor_sync(0xffffffffu, l[1], off);
+        }
+    }
+    __syncthreads();
+    // merge the CW warp states (the ring is free now): o[t][0..1] = dims t*16 + lane/4, heads
+    // h0, h0 + 1; o[t][2..3] = dims + 8
+    if (warp < CW) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int h = h0 + hh;
+            float* st = mstate + (static_cast<size_t>(warp) * 8 + h) * (D + 2);
+            if ((lane >> 2) == 0) {
+                st[D] = m[hh];
+                st[D + 1] = l[hh];
+            }
+#pragma unroll
+            for (int t = 0; t < KS; ++t) {
+                st[t * 16 + (lane >> 2)] = o[t][hh];
+                st[t * 16 + (lane >> 2) + 8] = o[t][2 + hh];
+            }
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * D; idx += AP_THREADS) {
+        const int g = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (int w = 0; w < CW; ++w) M = fmaxf(M, mstate[(static_cast<size_t>(w) * 8 + g) * (D + 2) + D]);
+        float Lt = 0.0f, acc = 0.0f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < CW; ++w) {
+                const float* st = mstate + (static_cast<size_t>(w) * 8 + g) * (D + 2);
+                const float f = st[D] == -INFINITY ? 0.0f : exp2f(st[D] - M);
+                Lt += st[D + 1] * f;
+                acc += st[d] * f;
+            }
+        }
+        const int h = kvh * G + g;
+        if (n_splits == 1) {
+            out[(static_cast<size_t>(row) * hq + h) * D + d] = Lt > 0.0f ? acc / Lt : 0.0f;
+        } else {
+            float* pp = part + ((static_cast<size_t>(row) * hq + h) * n_splits + split) * (D + 2);
+            pp[d] = acc;
+            if (d == 0) {
+                pp[D] = M == -INFINITY ? -INFINITY : M * 0.6931471805599453f;
+                pp[D + 1] = Lt;
+            }
+        }
+    }
+}
+
+// Kernel choice per query heads per kv head: the tensor-core page kernel from 4 (its MMAs
+// amortise over the heads; at 1-2 heads its 256-byte page rows conflict in shared memory
+// more than the lane groups pay for their shuffles).  SOC_B200_ATTENTION=lanes / =mma
+// forces one of them.
+bool use_lane_groups(int G) {
+    const char* e = std::getenv("SOC_B200_ATTENTION");
+    if (e && std::string(e) == "lanes") return true;
+    if (e && std::string(e) == "mma") return false;
+    return G < 4;
+}
+
 template <int D, int G>
 void pages_dg(dim3 grid, const float* q, const Rows& rows, int hq, int hkv, const KVLayerView& kv, int splits,
               float* out, float* scratch, int* err, cudaStream_t st) {
     constexpr int PAGE_B = 16 * D * 2;
     constexpr int ring = NSLOT * 2 * PAGE_B + 2 * NSLOT * 8;
+    if (!use_lane_groups(G)) {
+        constexpr int smem_m = ring + CW * 2 * 8 * 16 * 2;
+        constexpr int merge_m = CW * 8 * (D + 2) * 4;
+        static_assert(merge_m <= NSLOT * 2 * PAGE_B, "merge area fits in the ring");
+        static bool set_m = false;
+        if (!set_m) {
+            SOCB_CUDA(cudaFuncSetAttribute(k_attn_pages_mma<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_m));
+            set_m = true;
+        }
+        k_attn_pages_mma<D, G><<<grid, AP_THREADS, smem_m, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out,
+                                                                 scratch, err);
+        return;
+    }
     constexpr int LPK = (G >= 4 && D >= 128) ? 16 : 8;
     constexpr int merge = CW * (32 / LPK) * G * (D + 2) * 4;
     constexpr int smem = ring > merge ? ring : merge;

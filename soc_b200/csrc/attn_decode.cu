@@ -22,8 +22,9 @@
 namespace socb {
 namespace {
 
-constexpr int NSLOT = 6;
+constexpr int NSLOT = 6;                 // ring slots of the lane-group kernel (every warp reads every page)
 constexpr int CW = 4;                    // consumer warps
+constexpr int NSLOT_MMA = 8;             // ring slots of the tensor-core kernel (a page per warp)
 constexpr int AP_THREADS = (CW + 1) * 32;
 constexpr unsigned long long AP_WAIT_NS = 2000000000ull;
 
@@ -251,7 +252,9 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
                  : "r"(addr));
 }
 
-// Tensor-core variant: one consumer warp owns a whole page (16 keys) at a time and runs
+// Tensor-core variant: pages arrive by 2-D TMA (64-dim x 16-key boxes, 128-byte swizzle, so
+// the ldmatrix reads below are free of bank conflicts); one consumer warp owns a whole page
+// (16 keys) at a time and runs
 // the page as two m16n8k16 products with the G query heads padded to n = 8:
 //   S^T [16 keys x 8 heads] = K [16 x D] . Q^T        (A = K rows, ldmatrix)
 //   O^T [D x 8 heads]      += V^T [D x 16 keys] . P^T (A = V rows, ldmatrix.trans)
@@ -260,16 +263,30 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
 // exact.  P goes through per-warp shared tiles to become the second product's B operand.  Each
 // warp keeps its own online softmax (one max and one rescale per page and head); the four
 // warps' states are merged at the end.
+// Byte offset of (key k, dim d) in a page landed by the 64 x 16 TMA boxes with 128-byte
+// swizzle: box d / 64 (2 KB each), row k (128 B), 16-byte chunk ((d % 64) / 8) ^ (k % 8).
+__device__ __forceinline__ uint32_t sw_off(int k, int d) {
+    return static_cast<uint32_t>((d >> 6) * 2048 + k * 128 + ((((d & 63) >> 3) ^ (k & 7)) << 4) + (d & 7) * 2);
+}
+
 template <int D, int G>
 __global__ void __launch_bounds__(AP_THREADS) k_attn_pages_mma(const float* __restrict__ q,
                                                               const int* __restrict__ row_seq,
                                                               const int* __restrict__ row_pos, int hq, int hkv,
                                                               KVLayerView kv, int n_splits, float* __restrict__ out,
-                                                              float* __restrict__ part, int* err) {
+                                                              float* __restrict__ part,
+                                                              const __grid_constant__ CUtensorMap tk,
+                                                              const __grid_constant__ CUtensorMap tv, int* err) {
     constexpr int PT = 16, PAGE_B = PT * D * 2, KS = D / 16;
+    // Page i goes to slot i % NSLOT and warp i % CW; NSLOT a multiple of CW keeps every slot
+    // with one warp, so no warp can wait on a slot's phase parity two phases ahead.
+    constexpr int NSLOT = NSLOT_MMA;
+    static_assert(NSLOT % CW == 0, "each ring slot must belong to one consumer warp");
     static_assert(G <= 8, "at most 8 query heads per kv head");
-    extern __shared__ __align__(128) uint8_t sm[];
-    uint8_t* ring = sm;                                                   // [NSLOT][K | V][PAGE_B]
+    static_assert(D % 64 == 0, "pages arrive as 64-dim boxes");
+    extern __shared__ __align__(1024) uint8_t sm_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = sm;                                                   // [NSLOT][K | V][PAGE_B], swizzled
     unsigned long long* full = reinterpret_cast<unsigned long long*>(sm + NSLOT * 2 * PAGE_B);
     unsigned long long* empty = full + NSLOT;
     __half* ptile = reinterpret_cast<__half*>(sm + NSLOT * 2 * PAGE_B + 2 * NSLOT * 8);  // [CW][hi|lo][8][16]
@@ -308,20 +325,23 @@ __global__ void __launch_bounds__(AP_THREADS) k_attn_pages_mma(const float* __re
                 const int s = i % NSLOT;
                 if (!mb_wait(empty + s, ((i / NSLOT) & 1u) ^ 1u, err)) break;
                 const int page = pt[pg0 + i];
-                const size_t off = (static_cast<size_t>(page) * hkv + kvh) * PT * D;
+                const int y = kv.row0 + (page * hkv + kvh) * PT;
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(full + s)),
                              "r"(2 * PAGE_B)
                              : "memory");
-                asm volatile(
-                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                        su32(ring + s * 2 * PAGE_B)),
-                    "l"(kv.k + off), "r"(PAGE_B), "r"(su32(full + s))
-                    : "memory");
-                asm volatile(
-                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                        su32(ring + s * 2 * PAGE_B + PAGE_B)),
-                    "l"(kv.v + off), "r"(PAGE_B), "r"(su32(full + s))
-                    : "memory");
+#pragma unroll
+                for (int bx = 0; bx < D / 64; ++bx) {
+                    asm volatile(
+                        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+                            su32(ring + s * 2 * PAGE_B + bx * 2048)),
+                        "l"(&tk), "r"(su32(full + s)), "r"(bx * 64), "r"(y)
+                        : "memory");
+                    asm volatile(
+                        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+                            su32(ring + s * 2 * PAGE_B + PAGE_B + bx * 2048)),
+                        "l"(&tv), "r"(su32(full + s)), "r"(bx * 64), "r"(y)
+                        : "memory");
+                }
             }
             for (int j = i > NSLOT ? i - NSLOT : 0; j < i; ++j) mb_wait(full + j % NSLOT, (j / NSLOT) & 1u, err);
         }
@@ -357,8 +377,13 @@ __global__ void __launch_bounds__(AP_THREADS) k_attn_pages_mma(const float* __re
             // patterns): their V rows are zeroed, since P = 0 times NaN is NaN in the MMA.
             const int kvalid = ke - (pg0 + i) * PT;
             if (kvalid < PT) {
-                uint4* vz = reinterpret_cast<uint4*>(ring + s * 2 * PAGE_B + PAGE_B + kvalid * D * 2);
-                for (int z = lane; z < (PT - kvalid) * D * 2 / 16; z += 32) vz[z] = make_uint4(0u, 0u, 0u, 0u);
+                // rows kvalid..15 of every 64-dim box (each row 128 B, 8 chunks)
+                uint8_t* vbase = ring + s * 2 * PAGE_B + PAGE_B;
+                for (int z = lane; z < (PT - kvalid) * 8 * (D / 64); z += 32) {
+                    const int bx = z / ((PT - kvalid) * 8), rem = z % ((PT - kvalid) * 8);
+                    *reinterpret_cast<uint4*>(vbase + bx * 2048 + (kvalid + rem / 8) * 128 + (rem % 8) * 16) =
+                        make_uint4(0u, 0u, 0u, 0u);
+                }
                 __syncwarp();
             }
             // S^T = K . Q^T
@@ -367,7 +392,7 @@ __global__ void __launch_bounds__(AP_THREADS) k_attn_pages_mma(const float* __re
 #pragma unroll
             for (int kk = 0; kk < KS; ++kk) {
                 uint32_t a[4];
-                ldsm_x4(kpage + static_cast<uint32_t>((arow * D + kk * 16 + acol) * 2), a);
+                ldsm_x4(kpage + sw_off(arow, kk * 16 + acol), a);
                 mma16816(sc, a, qb[kk][0], qb[kk][1]);
                 mma16816(sc, a, ql[kk][0], ql[kk][1]);
             }
@@ -418,7 +443,7 @@ __global__ void __launch_bounds__(AP_THREADS) k_attn_pages_mma(const float* __re
 #pragma unroll
             for (int t = 0; t < KS; ++t) {
                 uint32_t a[4];
-                ldsm_x4_t(vpage + static_cast<uint32_t>((vkey * D + t * 16 + vdim) * 2), a);
+                ldsm_x4_t(vpage + sw_off(vkey, t * 16 + vdim), a);
                 mma16816(o[t], a, pb0, pb1);
                 mma16816(o[t], a, pl0, pl1);
             }
@@ -481,15 +506,11 @@ __global__ void __launch_bounds__(AP_THREADS) k_attn_pages_mma(const float* __re
     }
 }
 
-// Kernel choice per query heads per kv head: the tensor-core page kernel from 4 (its MMAs
-// amortise over the heads; at 1-2 heads its 256-byte page rows conflict in shared memory
-// more than the lane groups pay for their shuffles).  SOC_B200_ATTENTION=lanes / =mma
-// forces one of them.
-bool use_lane_groups(int G) {
+// The tensor-core page kernel runs whenever the cache has its TMA views;
+// SOC_B200_ATTENTION=lanes selects the CUDA-core lane-group kernel instead.
+bool use_lane_groups(int) {
     const char* e = std::getenv("SOC_B200_ATTENTION");
-    if (e && std::string(e) == "lanes") return true;
-    if (e && std::string(e) == "mma") return false;
-    return G < 4;
+    return e && std::string(e) == "lanes";
 }
 
 template <int D, int G>
@@ -497,17 +518,18 @@ void pages_dg(dim3 grid, const float* q, const Rows& rows, int hq, int hkv, cons
               float* out, float* scratch, int* err, cudaStream_t st) {
     constexpr int PAGE_B = 16 * D * 2;
     constexpr int ring = NSLOT * 2 * PAGE_B + 2 * NSLOT * 8;
-    if (!use_lane_groups(G)) {
-        constexpr int smem_m = ring + CW * 2 * 8 * 16 * 2;
+    if (!use_lane_groups(G) && kv.tmk != nullptr && kv.tmv != nullptr) {
+        constexpr int ring_m = NSLOT_MMA * 2 * PAGE_B + 2 * NSLOT_MMA * 8;
+        constexpr int smem_m = ring_m + CW * 2 * 8 * 16 * 2 + 1024;  // + alignment of the swizzled ring
         constexpr int merge_m = CW * 8 * (D + 2) * 4;
-        static_assert(merge_m <= NSLOT * 2 * PAGE_B, "merge area fits in the ring");
+        static_assert(merge_m <= NSLOT_MMA * 2 * PAGE_B, "merge area fits in the ring");
         static bool set_m = false;
         if (!set_m) {
             SOCB_CUDA(cudaFuncSetAttribute(k_attn_pages_mma<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_m));
             set_m = true;
         }
         k_attn_pages_mma<D, G><<<grid, AP_THREADS, smem_m, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out,
-                                                                 scratch, err);
+                                                                 scratch, *kv.tmk, *kv.tmv, err);
         return;
     }
     constexpr int LPK = (G >= 4 && D >= 128) ? 16 : 8;

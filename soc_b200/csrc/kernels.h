@@ -1,6 +1,8 @@
 // Host launchers of the modular Qwen3 kernels (kernels.cu).
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace socb {
@@ -16,6 +18,11 @@ struct KVLayerView {
     const int* page_table;  // [max_seqs][max_pages]
     int max_pages;
     int page_tokens;
+    // optional 2-D TMA views of the whole K / V pools ([rows = L * pages * hkv * 16, head_dim],
+    // 64 x 16 boxes, 128-byte swizzle) and this layer's first row; null when not built
+    const CUtensorMap* tmk = nullptr;
+    const CUtensorMap* tmv = nullptr;
+    int row0 = 0;
 };
 
 // Per-forward row descriptors (one row = one token of some sequence), all device pointers.

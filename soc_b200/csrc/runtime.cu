@@ -514,9 +514,16 @@ struct soc_kv {
     std::vector<std::vector<int>> pages;
     std::vector<int> free_pages;
     size_t layer_stride() const { return static_cast<size_t>(num_pages) * m->cfg.hkv * page_tokens * m->cfg.hd; }
+    CUtensorMap tmk{}, tmv{};  // TMA views of the pools for the page-streaming attention
+    bool tm_ok = false;
     KVLayerView view(int layer) const {
-        return KVLayerView{k + layer * layer_stride(), v + layer * layer_stride(), d_page_table, max_pages,
-                           page_tokens};
+        KVLayerView v_{k + layer * layer_stride(), v + layer * layer_stride(), d_page_table, max_pages, page_tokens};
+        if (tm_ok) {
+            v_.tmk = &tmk;
+            v_.tmv = &tmv;
+            v_.row0 = static_cast<int>(static_cast<size_t>(layer) * num_pages * m->cfg.hkv * page_tokens);
+        }
+        return v_;
     }
     void check_seq(int seq) const {
         if (seq < 0 || seq >= max_seqs) throw Error(SOC_B200_ERR_INVALID, "kv cache sequence index out of range");
@@ -1256,6 +1263,14 @@ int soc_b200_kv_create(soc_model* m, int max_seqs, int max_tokens, int page_toke
         SOCB_CUDA(cudaMalloc(&kv->k, elems * sizeof(__half)));
         SOCB_CUDA(cudaMalloc(&kv->v, elems * sizeof(__half)));
         SOCB_CUDA(cudaMalloc(&kv->d_page_table, sizeof(int) * static_cast<size_t>(max_seqs) * kv->max_pages));
+        {  // 2-D TMA views [L * pages * hkv * 16, head_dim] of the pools (row index must fit int32)
+            const size_t rows = m->cfg.layers * static_cast<size_t>(kv->num_pages) * m->cfg.hkv * page_tokens;
+            if (tc_available() && rows < (size_t(1) << 31) && m->cfg.hd % 64 == 0) {
+                tc_make_map(&kv->tmk, kv->k, WF_F16, rows, m->cfg.hd, m->cfg.hd, static_cast<uint32_t>(page_tokens));
+                tc_make_map(&kv->tmv, kv->v, WF_F16, rows, m->cfg.hd, m->cfg.hd, static_cast<uint32_t>(page_tokens));
+                kv->tm_ok = true;
+            }
+        }
         SOCB_CUDA(cudaMemset(kv->d_page_table, 0, sizeof(int) * static_cast<size_t>(max_seqs) * kv->max_pages));
         kv->lengths.assign(max_seqs, 0);
         kv->pages.assign(max_seqs, {});

@@ -76,3 +76,41 @@ def test_batched_ragged_decode_over_random_contexts(gpu_ctx, make_bundle, case):
         assert kv.length(s) == int(ctx[s]) + 3
     kv.free()
     m.free()
+
+
+@pytest.mark.parametrize("kernel", ["lanes", "mma"])
+def test_batched_decode_long_contexts_cycle_the_page_ring(gpu_ctx, make_bundle, kernel):
+    """40 sequences at contexts 700-1100: one attention split streams 20-35 pages through the
+    shared-memory ring (several times around it), for both page-attention kernels."""
+    import os
+    cfg = dict(QWEN3_0_6B, num_hidden_layers=2)
+    p = make_bundle("batched_qwen06_2layer_f16", cfg, seed=43, dtype="float16")
+    old = os.environ.get("SOC_B200_ATTENTION")
+    os.environ["SOC_B200_ATTENTION"] = kernel
+    try:
+        m = R.Model(gpu_ctx, p)
+        L, hkv, hd = cfg["num_hidden_layers"], cfg["num_key_value_heads"], cfg["head_dim"]
+        n = 40
+        rng = np.random.default_rng(46)
+        ctx = rng.integers(700, 1100, n)
+        kv = R.KVCache(m, n, int(ctx.sum()) + 32 * n)
+        for s in range(n):
+            kv.fill_random(s, int(ctx[s]), 2000 + s)
+        toks = rng.integers(0, cfg["vocab_size"], n).astype(np.int32)
+        lg, nxt = m.decode(kv, list(range(n)), toks)
+        for s in (0, 19, 39):
+            om = O.OracleModel(p, 1200)
+            for layer in range(L):
+                om.set_cache(layer, O.kv_random(2000 + s, s, layer, 0, int(ctx[s]), hkv, hd, L),
+                             O.kv_random(2000 + s, s, layer, 1, int(ctx[s]), hkv, hd, L))
+            om.set_length(int(ctx[s]))
+            ref = om.forward([int(toks[s])], int(ctx[s]), last_only=True)[0]
+            assert np.abs(lg[s] - ref).max() <= LOGIT_TOL, (s, np.abs(lg[s] - ref).max())
+            assert int(nxt[s]) == O.argmax(ref)
+        kv.free()
+        m.free()
+    finally:
+        if old is None:
+            os.environ.pop("SOC_B200_ATTENTION", None)
+        else:
+            os.environ["SOC_B200_ATTENTION"] = old

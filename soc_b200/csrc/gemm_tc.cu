@@ -561,6 +561,18 @@ int tc_min_rows() {
     return e && *e ? std::atoi(e) : 16;
 }
 
+bool tc_rows_ok(int rows, long long out_f, long long in_f, bool quant) {
+    const char* e = std::getenv("SOC_B200_TC_MIN_ROWS");
+    if (e && *e) {
+        const int t = std::atoi(e);
+        return t > 0 && rows >= (quant ? 2 * t : t);
+    }
+    // measured crossovers against the CUDA-core GEMV: at 4-15 rows a matrix of 32 M weights
+    // or more already streams faster through the tensor-core GEMM, smaller ones do not
+    const bool big = out_f * in_f >= (32ll << 20);
+    return quant ? (rows >= 32 || (rows >= 16 && big)) : (rows >= 16 || (rows >= 4 && big));
+}
+
 // SOC_B200_TC_OUT=registers keeps the fp32 GEMM outputs on the register-store epilogue.
 int tc_out_tma() {
     const char* e = std::getenv("SOC_B200_TC_OUT");

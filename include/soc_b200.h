@@ -149,6 +149,29 @@ SOC_B200_API int soc_b200_generate(soc_model* model, soc_kv* kv, int seq, const 
 SOC_B200_API int soc_b200_generate_device(soc_model* model, soc_kv* kv, int seq, const int32_t* d_prompt, int n_prompt,
                              int max_new, int32_t* d_out);
 
+/* ---- string pipeline (host only, no GPU) ----------------------------------
+ * The bundle's tokenizer (tokenizer/tokenizer_runtime.json) and the Qwen3 chat
+ * template.  Replaces TokenizerRuntimeLoader::LoadFromFile + StartupValidator::
+ * ValidateTokenizerRuntime (Mac/cpu/src/runtime_assets.cpp:170-216,
+ * startup_validator.cpp:25-73), TokenizerRuntime::Encode / Decode
+ * (Mac/cpu/header/tokenizer_runtime.h:17-18) and Qwen3TemplateBuilder::BuildPrompt
+ * (Mac/cpu/src/runtime_assets.cpp:221-258); same results and error texts. */
+typedef struct soc_tokenizer soc_tokenizer;
+SOC_B200_API int soc_b200_tokenizer_load(const char* tokenizer_runtime_path, soc_tokenizer** out);
+SOC_B200_API void soc_b200_tokenizer_free(soc_tokenizer* tokenizer);
+/* *n_ids = number of ids; SOC_B200_ERR_CAPACITY (first `capacity` ids written) when larger. */
+SOC_B200_API int soc_b200_tokenizer_encode(const soc_tokenizer* tokenizer, const char* text, size_t len, int32_t* ids,
+                                           int capacity, int* n_ids);
+/* *len = bytes of text (not NUL-terminated); SOC_B200_ERR_CAPACITY when larger than capacity. */
+SOC_B200_API int soc_b200_tokenizer_decode(const soc_tokenizer* tokenizer, const int32_t* ids, int n, char* text,
+                                           size_t capacity, size_t* len);
+/* Messages (role, content) -> prompt text; without a "system" message the override (or the
+ * template's default system prompt) is prepended. */
+SOC_B200_API int soc_b200_chat_prompt(const soc_tokenizer* tokenizer, const char* const* roles,
+                                      const char* const* contents, int n_messages, int add_generation_prompt,
+                                      int enable_thinking, const char* system_prompt_override, char* out,
+                                      size_t capacity, size_t* len);
+
 /* Tensor parallelism plumbing (the reference is single-device; these have no counterpart
  * in it).  NCCL is loaded at run time from libnccl.so.2.  Rank 0 creates the id, every rank
  * receives its 128 bytes out of band and creates the communicator on its own context's

@@ -376,3 +376,55 @@ def kv_random(seed: int, seq: int, layer: int, kind: int, n_tokens: int, hkv: in
                 total += (z >> np.uint64(sh)) & np.uint64(0xFFFF)
     val = total.astype(np.float32) * np.float32(1.0 / 65536.0) - np.float32(6.0)
     return val.astype(np.float16).reshape(n_tokens, hkv, hd)
+
+
+class RefTokenizer:
+    """The reference's TokenizerRuntime + Qwen3TemplateBuilder (oracle/_ref), for parity tests."""
+
+    def __init__(self, path):
+        lib = ref_lib()
+        if not hasattr(lib, "_tok_bound"):
+            lib.socref_tokenizer_load.argtypes = [C.c_char_p]
+            lib.socref_tokenizer_load.restype = C.c_void_p
+            lib.socref_tokenizer_free.argtypes = [C.c_void_p]
+            lib.socref_tokenizer_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.POINTER(C.c_int32), C.c_int]
+            lib.socref_tokenizer_decode.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_char_p, C.c_int]
+            lib.socref_chat_prompt.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, C.c_char_p, C.c_char_p,
+                                               C.c_int]
+            lib._tok_bound = True
+        self.lib = lib
+        self.h = lib.socref_tokenizer_load(str(path).encode())
+        if not self.h:
+            raise ValueError(lib.socref_last_error().decode())
+
+    def free(self):
+        if self.h:
+            self.lib.socref_tokenizer_free(self.h)
+            self.h = None
+
+    def encode(self, text):
+        data = text.encode("utf-8") if isinstance(text, str) else bytes(text)
+        cap = len(data) + 16
+        ids = (C.c_int32 * cap)()
+        n = self.lib.socref_tokenizer_encode(self.h, data, len(data), ids, cap)
+        if n < 0:
+            raise ValueError(self.lib.socref_last_error().decode())
+        return list(ids[:n])
+
+    def decode_bytes(self, ids):
+        arr = (C.c_int32 * max(1, len(ids)))(*ids)
+        cap = 64 + 64 * len(ids)
+        buf = C.create_string_buffer(cap)
+        n = self.lib.socref_tokenizer_decode(self.h, arr, len(ids), buf, cap)
+        if n < 0:
+            raise ValueError(self.lib.socref_last_error().decode())
+        return buf.raw[:n]
+
+    def chat_prompt(self, user, add_generation_prompt=True, enable_thinking=True, system_prompt=""):
+        cap = 1024 + 4 * len(user.encode()) + len(system_prompt.encode())
+        buf = C.create_string_buffer(cap)
+        n = self.lib.socref_chat_prompt(self.h, user.encode(), int(add_generation_prompt), int(enable_thinking),
+                                        system_prompt.encode(), buf, cap)
+        if n < 0:
+            raise ValueError(self.lib.socref_last_error().decode())
+        return buf.raw[:n].decode("utf-8")

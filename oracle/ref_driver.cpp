@@ -8,6 +8,7 @@
 // QwenCausalLM::ForwardLogitsCached (Mac/cpu/src/qwen_causal_lm.cpp:74-80),
 // never GenerationSession::Generate (which runs the prompt twice,
 // Mac/cpu/src/generation_session.cpp:55-56).
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -25,6 +26,7 @@
 #include "header/runtime_assets.h"
 #include "header/sampler.h"
 #include "header/startup_validator.h"
+#include "header/tokenizer_runtime.h"
 
 namespace {
 thread_local std::string g_err;
@@ -169,6 +171,56 @@ int socref_attention(const float* q, int T, int Hq, const float* k, const float*
                                                FloatTensor(v, {1, sz(S), sz(Hkv), sz(D)}), sz(prefix));
         std::memcpy(out, r.data<const float>(), sizeof(float) * r.numel());
         return 0;
+    } catch (const std::exception& e) {
+        return Fail(e);
+    }
+}
+
+
+// ---- tokenizer / chat template (TokenizerRuntimeLoader::LoadFromFile, runtime_assets.cpp:170-216;
+// TokenizerRuntime::{Encode, Decode}, tokenizer_runtime.cpp; Qwen3TemplateBuilder::BuildPrompt,
+// runtime_assets.cpp:221-258)
+void* socref_tokenizer_load(const char* path) {
+    try {
+        TokenizerRuntimeData data = TokenizerRuntimeLoader::LoadFromFile(path);
+        StartupValidator::ValidateTokenizerRuntime(data);
+        return new TokenizerRuntime(std::move(data));
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return nullptr;
+    }
+}
+
+void socref_tokenizer_free(void* t) { delete static_cast<TokenizerRuntime*>(t); }
+
+int socref_tokenizer_encode(void* t, const char* text, int len, int32_t* ids, int cap) {
+    try {
+        const std::vector<int> out = static_cast<TokenizerRuntime*>(t)->Encode(std::string(text, len));
+        for (int i = 0; i < static_cast<int>(out.size()) && i < cap; ++i) ids[i] = out[i];
+        return static_cast<int>(out.size());
+    } catch (const std::exception& e) {
+        return Fail(e);
+    }
+}
+
+int socref_tokenizer_decode(void* t, const int32_t* ids, int n, char* out, int cap) {
+    try {
+        const std::string s = static_cast<TokenizerRuntime*>(t)->Decode(std::vector<int>(ids, ids + n));
+        std::memcpy(out, s.data(), std::min<std::size_t>(s.size(), static_cast<std::size_t>(cap)));
+        return static_cast<int>(s.size());
+    } catch (const std::exception& e) {
+        return Fail(e);
+    }
+}
+
+int socref_chat_prompt(void* t, const char* user, int add_generation_prompt, int enable_thinking,
+                       const char* system_override, char* out, int cap) {
+    try {
+        const Qwen3TemplateBuilder builder(static_cast<TokenizerRuntime*>(t)->runtime_data().template_runtime);
+        const std::string s = builder.BuildPrompt(std::vector<ChatMessage>{{"user", user}}, add_generation_prompt != 0,
+                                                  enable_thinking != 0, system_override ? system_override : "");
+        std::memcpy(out, s.data(), std::min<std::size_t>(s.size(), static_cast<std::size_t>(cap)));
+        return static_cast<int>(s.size());
     } catch (const std::exception& e) {
         return Fail(e);
     }

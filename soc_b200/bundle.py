@@ -222,6 +222,110 @@ def dequantize_groupwise(q: np.ndarray, scale: np.ndarray, fmt: str) -> np.ndarr
     return (qi.reshape(out_f, in_f // g, g) * s).reshape(out_f, in_f)
 
 
+# Text the synthetic BPE tokenizer learns its merges from (own words; any text works).
+BPE_TRAINING_TEXT = (
+    "The quick brown fox jumps over the lazy dog. A tokenizer splits text into pieces, and the model "
+    "reads those pieces as numbers. Byte pairs that appear together often are merged first: th, he, in, "
+    "er, an, the, and, ing, tion. Numbers like 2048, 151936 and 3.14159 stay as digit runs; punctuation "
+    "such as !?;:,.() stays apart from words. Hello world! Hello again, world. Decoding joins the pieces "
+    "back into the same bytes, including UTF-8 text like café, naïve, 東京 and emoji 🙂.\n\tTabs and "
+    "  double  spaces are kept. Qwen3 models chat with im_start and im_end markers around each turn."
+)
+
+
+def bytes_to_unicode() -> list[str]:
+    """The byte-level BPE alphabet (GPT-2's published mapping): printable Latin-1 bytes stand
+    for themselves, the other bytes for code points 256, 257, ... in byte order."""
+    keep = list(range(ord("!"), ord("~") + 1)) + list(range(ord("\u00a1"), ord("\u00ac") + 1)) + \
+        list(range(ord("\u00ae"), ord("\u00ff") + 1))
+    table, extra = {}, 0
+    for b in range(256):
+        if b in keep:
+            table[b] = chr(b)
+        else:
+            table[b] = chr(256 + extra)
+            extra += 1
+    return [table[b] for b in range(256)]
+
+
+def _pretokenize(text: str) -> list[bytes]:
+    """Whitespace run + one run of letters, digits or other non-space bytes (the reference's
+    byte-level pre-tokenizer rule, ``tokenizer_runtime.cpp`` PreTokenizeText), on bytes."""
+    data, out, i = text.encode("utf-8"), [], 0
+    isspace = lambda c: c in b" \t\n\r\x0b\x0c"
+    isalpha = lambda c: (65 <= c <= 90) or (97 <= c <= 122)
+    isdigit = lambda c: 48 <= c <= 57
+    while i < len(data):
+        start = i
+        while i < len(data) and isspace(data[i]):
+            i += 1
+        if i == len(data):
+            out.append(data[start:])
+            break
+        if isalpha(data[i]):
+            while i < len(data) and isalpha(data[i]):
+                i += 1
+        elif isdigit(data[i]):
+            while i < len(data) and isdigit(data[i]):
+                i += 1
+        else:
+            while i < len(data) and not isspace(data[i]) and not isalpha(data[i]) and not isdigit(data[i]):
+                i += 1
+        out.append(data[start:i])
+    return out
+
+
+def synthetic_bpe_tokenizer(vocab_size: int, n_merges: int = 300, text: str = BPE_TRAINING_TEXT) -> dict[str, Any]:
+    """A ``soc.cpp.tokenizer_runtime`` v1 byte-level BPE document: 256 byte symbols (ids 0-255),
+    up to ``n_merges`` merges learned greedily from ``text`` (most frequent adjacent pair, ties
+    to the smaller pair), merged symbols as ids 256.., and the chat / control tokens as added
+    tokens at the top of the id range."""
+    b2u = bytes_to_unicode()
+    words: dict[tuple[str, ...], int] = {}
+    for piece in _pretokenize(text):
+        key = tuple(b2u[b] for b in piece)
+        words[key] = words.get(key, 0) + 1
+    merges: list[tuple[str, str]] = []
+    vocab = list(b2u)
+    specials = ["<|endoftext|>", "<|im_start|>", "<|im_end|>", "<think>", "</think>"]
+    limit = vocab_size - len(specials) - 256
+    while len(merges) < min(n_merges, limit):
+        pairs: dict[tuple[str, str], int] = {}
+        for w, c in words.items():
+            for a, b in zip(w, w[1:]):
+                pairs[(a, b)] = pairs.get((a, b), 0) + c
+        if not pairs:
+            break
+        best = min(pairs, key=lambda pr: (-pairs[pr], pr))
+        if pairs[best] < 2:
+            break
+        merges.append(best)
+        vocab.append(best[0] + best[1])
+        new_words: dict[tuple[str, ...], int] = {}
+        for w, c in words.items():
+            out, i = [], 0
+            while i < len(w):
+                if i + 1 < len(w) and (w[i], w[i + 1]) == best:
+                    out.append(w[i] + w[i + 1])
+                    i += 2
+                else:
+                    out.append(w[i])
+                    i += 1
+            new_words[tuple(out)] = new_words.get(tuple(out), 0) + c
+        words = new_words
+    doc = _tokenizer_runtime(vocab_size)
+    doc["tokenizer_class"] = "SyntheticByteLevelBPE"
+    doc["vocab"] = [{"id": i, "token": t} for i, t in enumerate(vocab)]
+    doc["bpe_model"] = {"type": "bpe", "unk_token": None, "continuing_subword_prefix": None,
+                        "end_of_word_suffix": None, "merges": [{"left": a, "right": b} for a, b in merges]}
+    doc["pre_tokenizer"] = {"type": "ByteLevel", "byte_level": {"enabled": True, "add_prefix_space": False,
+                                                                 "use_regex": True}}
+    doc["decoder"] = {"type": "ByteLevel", "byte_level": {"enabled": True, "add_prefix_space": False,
+                                                           "trim_offsets": False, "use_regex": True,
+                                                           "byte_to_unicode": b2u}}
+    return doc
+
+
 def _tokenizer_runtime(vocab_size: int) -> dict[str, Any]:
     """A minimal ``soc.cpp.tokenizer_runtime`` v1 document that passes the
     reference validator (``Mac/cpu/src/startup_validator.cpp:25-75``).

@@ -17,6 +17,9 @@ struct Error : std::runtime_error {
     Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
 };
 
+// Message returned by soc_b200_last_error() on this thread (runtime.cu).
+void set_last_error(const std::string& message);
+
 #define SOCB_CUDA(expr)                                                                            \
     do {                                                                                           \
         cudaError_t e_ = (expr);                                                                   \

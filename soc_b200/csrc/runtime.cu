@@ -37,6 +37,11 @@ int fail(int code, const std::string& msg) {
     g_last_error = msg;
     return code;
 }
+}  // namespace
+
+void socb::set_last_error(const std::string& message) { g_last_error = message; }
+
+namespace {
 
 template <typename F>
 int guarded(F&& f) {

@@ -78,6 +78,12 @@ _SIGNATURES = {
     "soc_b200_generate_device": (C.c_int, [_VP, _VP, C.c_int, _VP, C.c_int, C.c_int, _VP]),
     "soc_b200_linear": (C.c_int, [_VP, C.c_int, _VP, _VP, C.c_int, C.c_int, _VP, C.c_int, _VP, _VP]),
     "soc_b200_decode_noalloc": (C.c_int, [_VP, _VP, C.c_int, C.c_int32, _FP, _I32P]),
+    "soc_b200_tokenizer_load": (C.c_int, [C.c_char_p, C.POINTER(_VP)]),
+    "soc_b200_tokenizer_free": (None, [_VP]),
+    "soc_b200_tokenizer_encode": (C.c_int, [_VP, C.c_char_p, C.c_size_t, _I32P, C.c_int, C.POINTER(C.c_int)]),
+    "soc_b200_tokenizer_decode": (C.c_int, [_VP, _I32P, C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "soc_b200_chat_prompt": (C.c_int, [_VP, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p), C.c_int, C.c_int, C.c_int,
+                                       C.c_char_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
 }
 
 
@@ -336,3 +342,62 @@ def header_functions() -> list[str]:
     import re
     text = HEADER.read_text()
     return re.findall(r"SOC_B200_API\s+[\w\s\*]+?\b(soc_b200_\w+)\s*\(", text)
+
+
+class Tokenizer:
+    """The bundle's tokenizer and Qwen3 chat template (host only; ``soc_b200_tokenizer_*``)."""
+
+    def __init__(self, path):
+        """`path`: a tokenizer_runtime.json, or a bundle's manifest.json (its tokenizer file is used)."""
+        import json as _json
+        from pathlib import Path as _P
+        p = _P(path)
+        if p.name == "manifest.json":
+            p = p.parent / _json.loads(p.read_text())["tokenizer_runtime_file"]
+        h = _VP()
+        _check(lib().soc_b200_tokenizer_load(str(p).encode(), C.byref(h)))
+        self.h = h
+
+    def free(self):
+        if self.h:
+            lib().soc_b200_tokenizer_free(self.h)
+            self.h = None
+
+    def encode(self, text: str | bytes) -> list[int]:
+        data = text.encode("utf-8") if isinstance(text, str) else bytes(text)
+        n = C.c_int(0)
+        cap = max(16, len(data) + 16)
+        ids = np.zeros(cap, dtype=np.int32)
+        rc = lib().soc_b200_tokenizer_encode(self.h, data, len(data), _ip(ids), cap, C.byref(n))
+        if rc == ERR_CAPACITY:
+            ids = np.zeros(n.value, dtype=np.int32)
+            rc = lib().soc_b200_tokenizer_encode(self.h, data, len(data), _ip(ids), n.value, C.byref(n))
+        _check(rc)
+        return ids[: n.value].tolist()
+
+    def decode_bytes(self, ids) -> bytes:
+        ids = _i32(ids)
+        n = C.c_size_t(0)
+        cap = max(64, 16 * ids.size)
+        buf = C.create_string_buffer(cap)
+        rc = lib().soc_b200_tokenizer_decode(self.h, _ip(ids), ids.size, buf, cap, C.byref(n))
+        if rc == ERR_CAPACITY:
+            buf = C.create_string_buffer(n.value)
+            rc = lib().soc_b200_tokenizer_decode(self.h, _ip(ids), ids.size, buf, n.value, C.byref(n))
+        _check(rc)
+        return buf.raw[: n.value]
+
+    def decode(self, ids) -> str:
+        return self.decode_bytes(ids).decode("utf-8", errors="replace")
+
+    def chat_prompt(self, messages, add_generation_prompt=True, enable_thinking=True, system_prompt="") -> str:
+        """messages: [(role, content), ...] -> the Qwen3 template text."""
+        n = len(messages)
+        roles = (C.c_char_p * max(n, 1))(*[r.encode() for r, _ in messages])
+        contents = (C.c_char_p * max(n, 1))(*[c.encode() for _, c in messages])
+        ln = C.c_size_t(0)
+        cap = 256 + sum(len(c.encode()) + len(r) + 32 for r, c in messages) + len(system_prompt.encode())
+        buf = C.create_string_buffer(cap)
+        _check(lib().soc_b200_chat_prompt(self.h, roles, contents, n, int(add_generation_prompt), int(enable_thinking),
+                                          system_prompt.encode(), buf, cap, C.byref(ln)))
+        return buf.raw[: ln.value].decode("utf-8")

@@ -1,0 +1,112 @@
+"""String pipeline (host only): the library's tokenizer and chat template against the
+reference's TokenizerRuntime / Qwen3TemplateBuilder compiled from its own sources
+(oracle/_ref).  Token ids, decoded bytes and prompt text must be identical."""
+import json
+
+import pytest
+
+from oracle import oracle as O
+from soc_b200 import runtime as R
+from soc_b200.bundle import synthetic_bpe_tokenizer, tiny_config, write_synthetic_bundle
+
+TEXTS = [
+    "",
+    "Hello world!",
+    "Hello again, world. The quick brown fox jumps over the lazy dog.",
+    "  leading spaces and\ttabs\nnewlines\r\n  trailing  ",
+    "numbers 2048 151936 3.14159 and x2y3z",
+    "punctuation !?;:,.() [] {} <> -- == ++",
+    "UTF-8: café naïve 東京 🙂 ñ",
+    "<|im_start|>user\nHi there<|im_end|>\n<|im_start|>assistant\n<think>\n",
+    "special tokens inside<|im_end|>text<|endoftext|>and<think>more</think>",
+    "thinking andand the then there these",
+    "a",
+    " ",
+    "\x00\x01 control bytes \x7f",
+]
+
+
+@pytest.fixture(scope="module")
+def bpe_path(tmp_path_factory):
+    p = tmp_path_factory.mktemp("tok") / "tokenizer_runtime.json"
+    p.write_text(json.dumps(synthetic_bpe_tokenizer(1000)))
+    return p
+
+
+@pytest.fixture(scope="module")
+def byte_bundle(tmp_path_factory):
+    return write_synthetic_bundle(tmp_path_factory.mktemp("tb") / "b", tiny_config(), seed=1)
+
+
+def _pair(path):
+    if not O.ref_available():
+        pytest.skip("reference library not built (oracle/_ref)")
+    return R.Tokenizer(path), O.RefTokenizer(path)
+
+
+@pytest.mark.parametrize("text", TEXTS, ids=range(len(TEXTS)))
+def test_bpe_encode_decode_matches_reference(bpe_path, text):
+    ours, ref = _pair(bpe_path)
+    ids = ours.encode(text)
+    assert ids == ref.encode(text)
+    assert ours.decode_bytes(ids) == ref.decode_bytes(ids) == text.encode("utf-8")
+    ours.free()
+    ref.free()
+
+
+def test_bpe_merges_are_used(bpe_path):
+    ours, _ = _pair(bpe_path)
+    text = "the then there and"
+    assert len(ours.encode(text)) < len(text.encode())
+    ours.free()
+
+
+@pytest.mark.parametrize("text", ["<|im_start|>", "plain <|im_end|>", "x"], ids=range(3))
+def test_placeholder_tokenizer_matches_reference(byte_bundle, text):
+    """The placeholder tokenizer of the synthetic bundles (no BPE model): longest-match over
+    its tokens, and the reference's error text where nothing matches."""
+    import json as _j
+    path = byte_bundle.parent / _j.loads(byte_bundle.read_text())["tokenizer_runtime_file"]
+    ours, ref = _pair(path)
+    try:
+        expect = ref.encode(text)
+    except ValueError as e:
+        with pytest.raises(R.SocError) as got:
+            ours.encode(text)
+        assert str(e) in str(got.value)
+    else:
+        assert ours.encode(text) == expect
+    ours.free()
+    ref.free()
+
+
+@pytest.mark.parametrize("gen,think,system", [(True, True, ""), (True, False, ""), (False, False, "Be terse."),
+                                              (True, True, "Du bist hilfreich.")])
+def test_chat_prompt_matches_reference(bpe_path, gen, think, system):
+    ours, ref = _pair(bpe_path)
+    for user in ("Hello!", "Explain 2+2.\nThen stop.", ""):
+        assert ours.chat_prompt([("user", user)], gen, think, system) == ref.chat_prompt(user, gen, think, system)
+    ours.free()
+    ref.free()
+
+
+def test_chat_prompt_keeps_a_given_system_message(bpe_path):
+    ours, _ = _pair(bpe_path)
+    p = ours.chat_prompt([("system", "S"), ("user", "U")], True, False)
+    assert p == "<|im_start|>system\nS<|im_end|>\n<|im_start|>user\nU<|im_end|>\n<|im_start|>assistant\n"
+    ours.free()
+
+
+def test_tokenizer_errors(tmp_path, bpe_path):
+    doc = json.loads(bpe_path.read_text())
+    doc["format_version"] = 2
+    bad = tmp_path / "bad.json"
+    bad.write_text(json.dumps(doc))
+    with pytest.raises(R.SocError, match="format_version must be 1"):
+        R.Tokenizer(bad)
+    with pytest.raises(R.SocError, match="failed to open file"):
+        R.Tokenizer(tmp_path / "missing.json")
+    ours = R.Tokenizer(bpe_path)
+    with pytest.raises(R.SocError, match="unknown token id"):
+        ours.decode([10 ** 6])
+    ours.free()

@@ -172,6 +172,30 @@ SOC_B200_API int soc_b200_chat_prompt(const soc_tokenizer* tokenizer, const char
                                       int enable_thinking, const char* system_prompt_override, char* out,
                                       size_t capacity, size_t* len);
 
+/* StartupValidator::ValidateManifestAndTokenizer's cross checks of a tokenizer against the
+ * model's vocab_size (Mac/cpu/src/startup_validator.cpp:77-101). */
+SOC_B200_API int soc_b200_tokenizer_check_model(const soc_tokenizer* tokenizer, long long model_vocab_size);
+
+/* RuntimeGenerationOptions (Mac/cpu/header/runtime_pipeline.h:12-17): the defaults, overridden
+ * by the manifest's generation_config as RuntimePipeline::GenerationOptionsFromManifest does
+ * (Mac/cpu/src/runtime_pipeline.cpp:43-55; "max_length" feeds max_sequence_length). */
+typedef struct soc_generation_options {
+    size_t max_new_tokens;      /* 32 */
+    float temperature;          /* 1.0 */
+    size_t top_k;               /* 1 */
+    int eos_token_id;           /* -1: disabled */
+    size_t max_sequence_length; /* 256: the KV capacity of a generation */
+} soc_generation_options;
+SOC_B200_API int soc_b200_manifest_generation_options(const char* manifest_path, soc_generation_options* out);
+/* The manifest's tokenizer_runtime_file resolved against the manifest's directory
+ * (ManifestLoader::LoadFromFile, Mac/cpu/src/runtime_assets.cpp:138-168); NUL-terminated,
+ * *len excludes the NUL. */
+SOC_B200_API int soc_b200_manifest_tokenizer_path(const char* manifest_path, char* out, size_t capacity, size_t* len);
+/* Sampler's argument checks (Mac/cpu/src/sampler.cpp:17-20).  The reference sampler returns
+ * the best of the top_k largest logit/temperature scores, which is the greedy argmax the
+ * decode kernels compute for every temperature > 0. */
+SOC_B200_API int soc_b200_sampler_check(float temperature, size_t top_k);
+
 /* Tensor parallelism plumbing (the reference is single-device; these have no counterpart
  * in it).  NCCL is loaded at run time from libnccl.so.2.  Rank 0 creates the id, every rank
  * receives its 128 bytes out of band and creates the communicator on its own context's

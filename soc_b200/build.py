@@ -1,4 +1,5 @@
-"""Build libsoc_b200.so in-tree with nvcc for sm_100a (no GPU needed to build).
+"""Build libsoc_b200.so in-tree with nvcc for sm_100a (no GPU needed to build), and the
+soc_b200_cli runner beside it.
 
     python -m soc_b200.build            # incremental
     python -m soc_b200.build --force    # rebuild
@@ -13,6 +14,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libsoc_b200.so"
+CLI = PKG / "soc_b200_cli"
 OBJ = PKG / "_build"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -46,6 +48,12 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             subprocess.run(cmd, check=True)
     if force or _stale(LIB, objs):
         cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda", "-ldl"]
+        subprocess.run(cmd, check=True)
+    # The command-line runner (host C++ over the C ABI; finds the library next to itself).
+    cli_src = CSRC / "cli.cpp"
+    if force or _stale(CLI, [cli_src, LIB, PKG.parent / "include" / "soc_b200.h"]):
+        cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-I", str(PKG.parent / "include"), str(cli_src),
+               "-o", str(CLI), "-L", str(PKG), "-lsoc_b200", "-Wl,-rpath,$ORIGIN"]
         subprocess.run(cmd, check=True)
     return LIB
 

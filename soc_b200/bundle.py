@@ -375,6 +375,7 @@ def write_synthetic_bundle(
     std: float = 0.02,
     model_id: str = "synthetic/qwen3",
     torch_device: str | None = None,
+    tokenizer: str = "placeholder",
 ) -> Path:
     """Write a seeded random Qwen3 bundle in the reference format.
 
@@ -387,6 +388,8 @@ def write_synthetic_bundle(
     ``torch_device`` (e.g. ``"cuda"``) draws the values with
     ``torch.randn(shape, generator=torch.Generator(device).manual_seed(seed))`` on that
     device instead (same order, same std), for multi-billion-parameter bundles.
+    ``tokenizer``: ``"placeholder"`` (chat and control tokens only) or ``"bpe"``
+    (``synthetic_bpe_tokenizer``, a byte-level BPE over the config's vocab_size).
     Returns the manifest path.
     """
     out = Path(out_dir)
@@ -437,7 +440,12 @@ def write_synthetic_bundle(
             raise ValueError(f"unsupported bundle dtype {dtype}")
         del w
 
-    tok = _tokenizer_runtime(cfg["vocab_size"])
+    if tokenizer == "bpe":
+        tok = synthetic_bpe_tokenizer(cfg["vocab_size"])
+    elif tokenizer == "placeholder":
+        tok = _tokenizer_runtime(cfg["vocab_size"])
+    else:
+        raise ValueError(f"unknown synthetic tokenizer {tokenizer}")
     (out / "tokenizer" / "tokenizer_runtime.json").write_text(json.dumps(tok, indent=1))
     manifest = {
         "format": FORMAT,

@@ -45,6 +45,8 @@ struct soc_tokenizer {
     std::string dec_suffix;
     std::vector<std::string> byte_sym;                     // byte -> symbol
     std::unordered_map<std::string, unsigned char> sym_byte;  // symbol -> byte
+    long long vocab_size = 0;  // the file's vocab_size
+    int max_id = -1;           // largest id over added tokens and vocab
 };
 
 namespace {
@@ -259,7 +261,8 @@ void load(soc_tokenizer& t, const std::string& path) {
         if (root.at("format_version").as_int64() != 1) bad("tokenizer runtime format_version must be 1");
         root.at("tokenizer_class").as_string();
         root.at("model_max_length").as_int64();
-        if (root.at("vocab_size").as_int64() <= 0) bad("tokenizer runtime vocab_size must be positive");
+        t.vocab_size = root.at("vocab_size").as_int64();
+        if (t.vocab_size <= 0) bad("tokenizer runtime vocab_size must be positive");
         const Json& tr = root.at("template_runtime");
         if (tr.at("type").as_string() != "qwen3") bad("tokenizer template runtime type must be qwen3");
         t.im_start = tr.at("im_start").as_string();
@@ -273,6 +276,7 @@ void load(soc_tokenizer& t, const std::string& path) {
             t.id_of.emplace(c, id);
             t.token_of.emplace(id, c);
             t.added_ids.insert(id);
+            t.max_id = std::max(t.max_id, id);
             t.added_longest_first.push_back(c);
             t.all_longest_first.push_back(c);
         }
@@ -281,6 +285,7 @@ void load(soc_tokenizer& t, const std::string& path) {
             const std::string& c = v.at("token").as_string();
             t.id_of.emplace(c, id);
             t.token_of.emplace(id, c);
+            t.max_id = std::max(t.max_id, id);
             t.all_longest_first.push_back(c);
         }
         sort_unique(t.added_longest_first);
@@ -346,9 +351,99 @@ int copy_out(const std::string& s, char* out, size_t cap, size_t* len) {
     return SOC_B200_OK;
 }
 
+// ResolveRelativePath (Mac/cpu/src/runtime_assets.cpp): absolute paths stay, relative ones
+// hang off the manifest's directory.
+std::string manifest_relative(const std::string& manifest, const std::string& p) {
+    if (!p.empty() && p[0] == '/') return p;
+    const auto cut = manifest.find_last_of('/');
+    return (cut == std::string::npos ? std::string() : manifest.substr(0, cut + 1)) + p;
+}
+
+// ReadOptionalInt / ReadOptionalSize / ReadOptionalFloat (Mac/cpu/src/runtime_pipeline.cpp:6-33):
+// a missing key keeps the default; an integer given as an array takes its first element.
+long long opt_int(const Json& o, const char* key, long long fallback, bool array_ok) {
+    if (!o.is_object() || !o.contains(key)) return fallback;
+    const Json& v = o.at(key);
+    if (array_ok && v.is_array()) return v.as_array().empty() ? fallback : v.as_array().front().as_int64();
+    return v.as_int64();
+}
+
 }  // namespace
 
 extern "C" {
+
+int soc_b200_manifest_generation_options(const char* manifest_path, soc_generation_options* out) {
+    if (!manifest_path || !out) return tok_fail(SOC_B200_ERR_INVALID, "null argument");
+    return tok_guard([&] {
+        Json root;
+        try {
+            root = JsonReader(read_text(manifest_path)).parse();
+        } catch (const Error&) {
+            throw;
+        } catch (const std::exception& e) {
+            bad(e.what());
+        }
+        soc_generation_options o;
+        o.max_new_tokens = 32;
+        o.temperature = 1.0f;
+        o.top_k = 1;
+        o.eos_token_id = -1;
+        o.max_sequence_length = 256;
+        try {
+            if (root.contains("generation_config")) {
+                const Json& g = root.at("generation_config");
+                o.max_new_tokens = static_cast<size_t>(opt_int(g, "max_new_tokens", 32, false));
+                if (g.is_object() && g.contains("temperature"))
+                    o.temperature = static_cast<float>(g.at("temperature").as_number());
+                o.top_k = static_cast<size_t>(opt_int(g, "top_k", 1, false));
+                o.eos_token_id = static_cast<int>(opt_int(g, "eos_token_id", -1, true));
+                o.max_sequence_length = static_cast<size_t>(opt_int(g, "max_length", 256, false));
+            }
+        } catch (const Error&) {
+            throw;
+        } catch (const std::exception& e) {
+            bad(e.what());
+        }
+        *out = o;
+    });
+}
+
+int soc_b200_manifest_tokenizer_path(const char* manifest_path, char* out, size_t capacity, size_t* len) {
+    if (!manifest_path) return tok_fail(SOC_B200_ERR_INVALID, "null argument");
+    int rc = SOC_B200_OK;
+    const int g = tok_guard([&] {
+        Json root;
+        try {
+            root = JsonReader(read_text(manifest_path)).parse();
+            if (!root.contains("tokenizer_runtime_file") || root.at("tokenizer_runtime_file").as_string().empty())
+                bad("manifest must reference tokenizer_runtime_file");
+        } catch (const Error&) {
+            throw;
+        } catch (const std::exception& e) {
+            bad(e.what());
+        }
+        const std::string p = manifest_relative(manifest_path, root.at("tokenizer_runtime_file").as_string());
+        rc = copy_out(p + std::string(1, '\0'), out, capacity, len);
+        if (len) *len -= 1;
+    });
+    return g != SOC_B200_OK ? g : rc;
+}
+
+int soc_b200_tokenizer_check_model(const soc_tokenizer* t, long long model_vocab_size) {
+    if (!t) return tok_fail(SOC_B200_ERR_INVALID, "null argument");
+    if (t->vocab_size <= 0) return tok_fail(SOC_B200_ERR_FORMAT, "tokenizer vocab_size must be positive");
+    if (t->vocab_size > model_vocab_size)
+        return tok_fail(SOC_B200_ERR_FORMAT, "tokenizer vocab_size must not exceed qwen3 config vocab_size");
+    if (t->max_id < 0 || t->max_id >= model_vocab_size)
+        return tok_fail(SOC_B200_ERR_FORMAT, "tokenizer token ids must fit within qwen3 config vocab_size");
+    return SOC_B200_OK;
+}
+
+int soc_b200_sampler_check(float temperature, size_t top_k) {
+    if (!(temperature > 0.0f)) return tok_fail(SOC_B200_ERR_INVALID, "sampler temperature must be positive");
+    if (top_k == 0) return tok_fail(SOC_B200_ERR_INVALID, "sampler top_k must be positive");
+    return SOC_B200_OK;
+}
 
 int soc_b200_tokenizer_load(const char* path, soc_tokenizer** out) {
     if (!path || !out) return tok_fail(SOC_B200_ERR_INVALID, "null argument");

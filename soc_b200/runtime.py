@@ -84,6 +84,10 @@ _SIGNATURES = {
     "soc_b200_tokenizer_decode": (C.c_int, [_VP, _I32P, C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
     "soc_b200_chat_prompt": (C.c_int, [_VP, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p), C.c_int, C.c_int, C.c_int,
                                        C.c_char_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "soc_b200_tokenizer_check_model": (C.c_int, [_VP, C.c_longlong]),
+    "soc_b200_manifest_generation_options": (C.c_int, [C.c_char_p, C.c_void_p]),
+    "soc_b200_manifest_tokenizer_path": (C.c_int, [C.c_char_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "soc_b200_sampler_check": (C.c_int, [C.c_float, C.c_size_t]),
 }
 
 
@@ -344,19 +348,50 @@ def header_functions() -> list[str]:
     return re.findall(r"SOC_B200_API\s+[\w\s\*]+?\b(soc_b200_\w+)\s*\(", text)
 
 
+class GenerationOptions(C.Structure):
+    """``soc_generation_options``: RuntimeGenerationOptions (Mac/cpu/header/runtime_pipeline.h:12-17)."""
+    _fields_ = [("max_new_tokens", C.c_size_t), ("temperature", C.c_float), ("top_k", C.c_size_t),
+                ("eos_token_id", C.c_int), ("max_sequence_length", C.c_size_t)]
+
+    @classmethod
+    def from_manifest(cls, manifest_path) -> "GenerationOptions":
+        """Defaults overridden by the manifest's generation_config
+        (RuntimePipeline::GenerationOptionsFromManifest, Mac/cpu/src/runtime_pipeline.cpp:43-55)."""
+        o = cls()
+        _check(lib().soc_b200_manifest_generation_options(str(manifest_path).encode(), C.byref(o)))
+        return o
+
+    def check(self) -> None:
+        """The sampler's argument checks (Mac/cpu/src/sampler.cpp:17-20)."""
+        _check(lib().soc_b200_sampler_check(self.temperature, self.top_k))
+
+
+def manifest_tokenizer_path(manifest_path) -> str:
+    """The manifest's tokenizer_runtime_file, resolved against the manifest's directory."""
+    n = C.c_size_t(0)
+    lib().soc_b200_manifest_tokenizer_path(str(manifest_path).encode(), None, 0, C.byref(n))
+    buf = C.create_string_buffer(n.value + 1)
+    _check(lib().soc_b200_manifest_tokenizer_path(str(manifest_path).encode(), buf, n.value + 1, C.byref(n)))
+    return buf.value.decode()
+
+
 class Tokenizer:
     """The bundle's tokenizer and Qwen3 chat template (host only; ``soc_b200_tokenizer_*``)."""
 
     def __init__(self, path):
         """`path`: a tokenizer_runtime.json, or a bundle's manifest.json (its tokenizer file is used)."""
-        import json as _json
         from pathlib import Path as _P
         p = _P(path)
         if p.name == "manifest.json":
-            p = p.parent / _json.loads(p.read_text())["tokenizer_runtime_file"]
+            p = manifest_tokenizer_path(p)
         h = _VP()
         _check(lib().soc_b200_tokenizer_load(str(p).encode(), C.byref(h)))
         self.h = h
+
+    def check_model(self, model_vocab_size: int) -> None:
+        """StartupValidator::ValidateManifestAndTokenizer's vocab checks
+        (Mac/cpu/src/startup_validator.cpp:77-101)."""
+        _check(lib().soc_b200_tokenizer_check_model(self.h, int(model_vocab_size)))
 
     def free(self):
         if self.h:

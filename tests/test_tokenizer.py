@@ -110,3 +110,38 @@ def test_tokenizer_errors(tmp_path, bpe_path):
     with pytest.raises(R.SocError, match="unknown token id"):
         ours.decode([10 ** 6])
     ours.free()
+
+
+def test_generation_options_from_manifest(tmp_path, byte_bundle):
+    o = R.GenerationOptions.from_manifest(byte_bundle)
+    doc = json.loads(byte_bundle.read_text())
+    g = doc["generation_config"]
+    assert (o.max_new_tokens, o.temperature, o.top_k, o.eos_token_id, o.max_sequence_length) == \
+        (g["max_new_tokens"], g["temperature"], g["top_k"], g["eos_token_id"], g["max_length"])
+    # defaults when absent; an eos list takes its first id (runtime_pipeline.cpp ReadOptionalInt)
+    doc["generation_config"] = {"eos_token_id": [151645, 151643], "temperature": 0.7}
+    p = tmp_path / "manifest.json"
+    p.write_text(json.dumps(doc))
+    o = R.GenerationOptions.from_manifest(p)
+    assert (o.max_new_tokens, o.top_k, o.eos_token_id, o.max_sequence_length) == (32, 1, 151645, 256)
+    assert abs(o.temperature - 0.7) < 1e-7
+    del doc["generation_config"]
+    p.write_text(json.dumps(doc))
+    o = R.GenerationOptions.from_manifest(p)
+    assert (o.max_new_tokens, o.temperature, o.top_k, o.eos_token_id, o.max_sequence_length) == (32, 1.0, 1, -1, 256)
+    o.temperature = 0.0
+    with pytest.raises(R.SocError, match="sampler temperature must be positive"):
+        o.check()
+    o.temperature, o.top_k = 1.0, 0
+    with pytest.raises(R.SocError, match="sampler top_k must be positive"):
+        o.check()
+    assert R.manifest_tokenizer_path(byte_bundle) == str(byte_bundle.parent / doc["tokenizer_runtime_file"])
+
+
+def test_tokenizer_vocab_checked_against_model(bpe_path):
+    t = R.Tokenizer(bpe_path)
+    t.check_model(1000)
+    t.check_model(4096)
+    with pytest.raises(R.SocError, match="must not exceed qwen3 config vocab_size"):
+        t.check_model(999)
+    t.free()

@@ -278,8 +278,8 @@ def _pretokenize(text: str) -> list[bytes]:
 def synthetic_bpe_tokenizer(vocab_size: int, n_merges: int = 300, text: str = BPE_TRAINING_TEXT) -> dict[str, Any]:
     """A ``soc.cpp.tokenizer_runtime`` v1 byte-level BPE document: 256 byte symbols (ids 0-255),
     up to ``n_merges`` merges learned greedily from ``text`` (most frequent adjacent pair, ties
-    to the smaller pair), merged symbols as ids 256.., and the chat / control tokens as added
-    tokens at the top of the id range."""
+    to the smaller pair), merged symbols as ids 256.., filler symbols of printable bytes up to the added
+    tokens, and the chat / control tokens as added tokens at the top of the id range."""
     b2u = bytes_to_unicode()
     words: dict[tuple[str, ...], int] = {}
     for piece in _pretokenize(text):
@@ -313,6 +313,20 @@ def synthetic_bpe_tokenizer(vocab_size: int, n_merges: int = 300, text: str = BP
                     i += 1
             new_words[tuple(out)] = new_words.get(tuple(out), 0) + c
         words = new_words
+    # Fill the rest of the id range below the added tokens with multi-byte symbols no merge
+    # produces, so that every id a model of this vocab_size can emit decodes to bytes.
+    have = set(vocab)
+    k = 94
+    while len(vocab) < vocab_size - len(specials):
+        digits, n = [], k  # k in base 94 over the printable bytes '!'..'~' (two or more symbols)
+        while n:
+            digits.append(b2u[0x21 + n % 94])
+            n //= 94
+        tok = "".join(reversed(digits))
+        k += 1
+        if tok not in have:
+            have.add(tok)
+            vocab.append(tok)
     doc = _tokenizer_runtime(vocab_size)
     doc["tokenizer_class"] = "SyntheticByteLevelBPE"
     doc["vocab"] = [{"id": i, "token": t} for i, t in enumerate(vocab)]

@@ -94,6 +94,13 @@ SOC_B200_API void* soc_b200_stream(soc_ctx* ctx);
 SOC_B200_API int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_format, int tp_rank, int tp_size,
                          void* nccl_comm, soc_model** out);
 SOC_B200_API int soc_b200_model_info(const soc_model* model, soc_model_info* out);
+/* Sampler(SamplerConfig) (Mac/cpu/src/sampler.cpp:17-57) for every later next-token pick
+ * of this model (prefill, decode, generate, decode_noalloc): the id maximising
+ * logit / temperature, the division IEEE single precision as in the reference, lowest id on
+ * ties.  The reference returns the best of the top_k largest such scores, which is that
+ * maximum for every top_k >= 1, so top_k is only validated.  Defaults: 1.0 and 1; the
+ * argument checks and their messages are the reference's. */
+SOC_B200_API int soc_b200_set_sampler(soc_model* model, float temperature, size_t top_k);
 SOC_B200_API void soc_b200_free_model(soc_model* model);
 
 
@@ -139,7 +146,9 @@ SOC_B200_API int soc_b200_decode(soc_model* model, soc_kv* kv, int n_seqs, const
 /* Reset `seq`, prefill the prompt and decode greedily up to max_new tokens,
  * stopping after eos_token_id when it is >= 0 (GenerationContext::Generate,
  * generation_context.cpp:118-172).  out_ids must hold max_new ids; *n_out
- * receives the count.  The decode steps run back to back on the device. */
+ * receives the count.  The decode steps run back to back on the device; with the
+ * persistent batch-1 decode kernel the eos stop happens on the device (no step after
+ * it runs), elsewhere the steps after it are computed and dropped. */
 SOC_B200_API int soc_b200_generate(soc_model* model, soc_kv* kv, int seq, const int32_t* prompt, int n_prompt, int max_new,
                       int eos_token_id, int32_t* out_ids, int* n_out);
 

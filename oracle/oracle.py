@@ -85,6 +85,7 @@ def ref_lib() -> C.CDLL:
         lib.socref_cache_length.argtypes = [C.c_void_p]
         lib.socref_forward_cached.argtypes = [C.c_void_p, C.c_void_p, _I, C.c_int, C.c_int, _F]
         lib.socref_sample_greedy.argtypes = [_F, C.c_int]
+        lib.socref_sample.argtypes = [_F, C.c_int, C.c_float, C.c_int]
         lib.socref_kv_read.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _F, _F]
         lib.socref_linear.argtypes = [_F, C.c_int, C.c_int, _F, C.c_int, _F]
         lib.socref_rmsnorm.argtypes = [_F, C.c_int, C.c_int, _F, C.c_float, _F]
@@ -428,3 +429,19 @@ class RefTokenizer:
         if n < 0:
             raise ValueError(self.lib.socref_last_error().decode())
         return buf.raw[:n].decode("utf-8")
+
+
+def ref_sample(logits_row, temperature=1.0, top_k=1) -> int:
+    """The reference Sampler::SampleFromLogits (Mac/cpu/src/sampler.cpp:22-57) on one row."""
+    x = _f32(logits_row)
+    r = int(ref_lib().socref_sample(_fp(x), x.size, float(temperature), int(top_k)))
+    if r < 0:
+        raise ValueError(ref_lib().socref_last_error().decode())
+    return r
+
+
+def sample_rule(logits_row, temperature=1.0) -> int:
+    """The pick the device kernels make: first index of the maximum of logit / temperature
+    (float32 IEEE division, as the reference's comparator computes it)."""
+    x = _f32(logits_row)
+    return int(np.argmax(x / np.float32(temperature)))

@@ -109,6 +109,17 @@ int socref_sample_greedy(const float* logits_row, int vocab) {
     return sampler.SampleFromLogits(FloatTensor(logits_row, {1, 1, static_cast<std::size_t>(vocab)}), 0, 0);
 }
 
+// The reference Sampler with an explicit config; -1 (message in socref_last_error) when the
+// config is rejected.
+int socref_sample(const float* logits_row, int vocab, float temperature, int top_k) {
+    try {
+        const Sampler sampler(SamplerConfig{temperature, static_cast<std::size_t>(top_k)});
+        return sampler.SampleFromLogits(FloatTensor(logits_row, {1, 1, static_cast<std::size_t>(vocab)}), 0, 0);
+    } catch (const std::exception& e) {
+        return Fail(e);
+    }
+}
+
 // KV rows [start, end) of one layer, as TensorKVCache::Read returns them ([S, Hkv, D] fp32).
 int socref_kv_read(void* c, int layer, int start, int end, float* k, float* v) {
     try {

@@ -167,7 +167,7 @@ int run(const Options& cli) {
     if (cli.set_top_k) g.top_k = cli.gen.top_k;
     if (cli.set_eos) g.eos_token_id = cli.gen.eos_token_id;
     if (cli.set_max_seq) g.max_sequence_length = cli.gen.max_sequence_length;
-    check(soc_b200_sampler_check(g.temperature, g.top_k));
+    check(soc_b200_set_sampler(h.model, g.temperature, g.top_k));
     if (g.max_sequence_length == 0) throw std::runtime_error("kv cache requires positive max_sequence_length");
 
     const std::string prepared = cli.chat ? chat_prompt(h.tok, cli) : cli.prompt;

@@ -170,6 +170,21 @@ __device__ __forceinline__ void wait_ctr(const unsigned* c, unsigned target, int
     nbar();
 }
 
+// One thread's bounded wait for c >= target (the producer's); false when it gave up.
+__device__ __forceinline__ bool wait_ctr_thread(const unsigned* c, unsigned target, int* err) {
+    for (unsigned i = 0;; ++i) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+        if (v >= target) return true;
+        if (i > SPIN_LIMIT) {
+            atomicOr(err, DERR_WAIT_TIMEOUT);
+            return false;
+        }
+        if ((i & 63u) == 63u && aborted(err)) return false;
+        if (i > 4) __nanosleep(32);
+    }
+}
+
 // After this CTA's part of a phase is stored: the CTA barrier, then one release add.
 __device__ __forceinline__ void signal(unsigned* c, int ctid) {
     nbar();
@@ -318,7 +333,27 @@ __device__ __forceinline__ void producer(const MKParams& p, Smem& sm) {
     }
     long long k = 0;
     bool ok = true;
+    int checked = -1;  // last step whose input id was compared with p.eos
     while (!ld.done && ok) {
+        if (p.eos >= 0 && ld.t != checked) {
+            // The first chunk of step ld.t: load it only if that step runs, i.e. its input id
+            // (step 0: ids[0]; later: the merged argmax of the step before) is not eos.  The
+            // consumers take the same decision from the same keys at the top of the step.
+            checked = ld.t;
+            int tok;
+            if (ld.t == 0) {
+                tok = __ldcg(p.ids);
+            } else {
+                if (!wait_ctr_thread(ctr_lm(p), static_cast<unsigned>(gridDim.x * ld.t), p.err)) break;
+                unsigned long long b = 0ull;
+                for (int c = 0; c < static_cast<int>(gridDim.x); ++c) {
+                    const unsigned long long kk = __ldcg(p.best + static_cast<size_t>(ld.t - 1) * gridDim.x + c);
+                    b = kk > b ? kk : b;
+                }
+                tok = b == 0ull ? 0 : argmax_key_index(b);
+            }
+            if (tok == p.eos) break;
+        }
         const int slot = static_cast<int>(k % SLOTS);
         const long long round = k / SLOTS;
         if (round > 0 && !mbar_wait(&sm.empty[slot], static_cast<unsigned>((round - 1) & 1), p.err)) {
@@ -502,8 +537,9 @@ __device__ __forceinline__ void consume(const MKParams& p, Smem& sm, const Phase
                             default: {
                                 const float yy = y[q] * s;
                                 if (p.logits) p.logits[static_cast<size_t>(sc.t) * p.V + unit] = yy;
-                                if (yy == yy) {
-                                    const unsigned long long key = argmax_key(yy, unit);
+                                const float sv = p.temperature == 1.0f ? yy : __fdiv_rn(yy, p.temperature);
+                                if (sv == sv) {
+                                    const unsigned long long key = argmax_key(sv, unit);
                                     wbest = key > wbest ? key : wbest;
                                 }
                             }
@@ -820,6 +856,7 @@ __device__ void consumers(const MKParams& p, Smem& sm, int cw, int lane) {
     const int GRID = gridDim.x;
     const int me = blockIdx.x;
     long long k = 0;
+    bool stopped = false;
     for (int t = 0; t < p.steps; ++t) {
         StepCtx sc;
         sc.t = t;
@@ -842,6 +879,11 @@ __device__ void consumers(const MKParams& p, Smem& sm, int cw, int lane) {
             }
             sc.tok = b == 0ull ? 0 : argmax_key_index(b);
             if (me == 0 && ctid == 0) p.ids[t] = sc.tok;
+        }
+        if (sc.tok == p.eos) {
+            // every CTA reads the same id, so all of them (and their producers) stop here
+            stopped = true;
+            break;
         }
         unsigned long long wbest = 0ull;
         for (int l = 0; l < p.L; ++l) {
@@ -906,7 +948,7 @@ __device__ void consumers(const MKParams& p, Smem& sm, int cw, int lane) {
         }
         MK_TR(p.L, 4);
     }
-    if (me == 0) {
+    if (me == 0 && !stopped) {
         const int t = p.steps - 1;
         wait_ctr(ctr_lm(p), static_cast<unsigned>(GRID * p.steps), p.err, ctid);
         if (cw == 0) {

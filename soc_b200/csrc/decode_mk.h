@@ -36,6 +36,8 @@ struct MKParams {
     int start;
     int steps;
     float* logits;  // nullable: [steps, V]
+    float temperature;  // the pick maximises logit / temperature (1: the logits)
+    int eos;            // >= 0: stop at the top of the first step whose input id is eos
     // activation vectors shared between CTAs
     float* h;                 // [H] residual stream
     float* qkv;               // [(hq + 2 hkv) D]

@@ -835,17 +835,21 @@ void launch_kv_fill_random(__half* kpool, __half* vpool, size_t layer_stride, co
 }
 
 // ------------------------------------------------------------------------ argmax
-// Greedy pick per row: maximum logit, lowest index on ties (the reference's
-// partial_sort with top_k = 1 keeps the first strict maximum).  NaNs never win.
+// Greedy pick per row: maximum logit / temperature, lowest index on ties (the reference's
+// Sampler::SampleFromLogits, Mac/cpu/src/sampler.cpp:22-57, ranks logit / temperature and
+// returns the best of its top_k, which is the maximum).  The division is the IEEE
+// round-to-nearest one the reference's float division performs, so ties it creates between
+// neighbouring logits are ties here too; temperature 1 compares the logits themselves.
+// NaNs never win.
 // keys != nullptr: write the row's best (value, global index) key instead of the id, for a
 // vocab shard whose first global index is v_off (merged across shards by k_argmax_merge).
-__global__ void k_argmax(const float* __restrict__ logits, int V, int ld, int v_off, int* __restrict__ next_ids,
-                         unsigned long long* __restrict__ keys) {
+__global__ void k_argmax(const float* __restrict__ logits, int V, int ld, int v_off, float temp,
+                         int* __restrict__ next_ids, unsigned long long* __restrict__ keys) {
     __shared__ unsigned long long red[32];
     const float* row = logits + static_cast<size_t>(blockIdx.x) * ld;
     unsigned long long best = 0ull;
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = row[i];
+        const float v = temp == 1.0f ? row[i] : __fdiv_rn(row[i], temp);
         if (v != v) continue;
         const unsigned long long k = argmax_key(v, v_off + i);
         best = k > best ? k : best;
@@ -886,17 +890,17 @@ __global__ void k_argmax_merge(const unsigned long long* __restrict__ keys_all, 
     next_ids[r] = b == 0ull ? 0 : argmax_key_index(b);
 }
 
-void launch_argmax(const float* logits, int vocab, int ld, int rows, int* next_ids, cudaStream_t st) {
+void launch_argmax(const float* logits, int vocab, int ld, int rows, float temperature, int* next_ids, cudaStream_t st) {
     if (rows <= 0) return;
-    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, 0, next_ids, nullptr);
+    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, 0, temperature, next_ids, nullptr);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }
 
-void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_off, unsigned long long* keys,
-                        cudaStream_t st) {
+void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_off, float temperature,
+                        unsigned long long* keys, cudaStream_t st) {
     if (rows <= 0) return;
-    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, v_off, nullptr, keys);
+    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, v_off, temperature, nullptr, keys);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }

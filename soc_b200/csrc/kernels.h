@@ -68,10 +68,11 @@ void launch_kv_fill_random(__half* kpool, __half* vpool, size_t layer_stride, co
                            int hkv, int hkv_total, int head_off, int D, int L, int n_tokens, int seq,
                            unsigned long long seed, cudaStream_t st);
 
-void launch_argmax(const float* logits, int vocab, int ld, int rows, int* next_ids, cudaStream_t st);
+// temperature: the pick maximises logit / temperature (IEEE single division; 1 = the logits).
+void launch_argmax(const float* logits, int vocab, int ld, int rows, float temperature, int* next_ids, cudaStream_t st);
 // Vocab-parallel greedy pick: per-row (value, global index) keys of one shard, and the merge
 // of all shards' keys [shards][rows] (lowest global index wins ties, as above).
-void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_off, unsigned long long* keys,
+void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_off, float temperature, unsigned long long* keys,
                         cudaStream_t st);
 void launch_argmax_merge(const unsigned long long* keys_all, int shards, int rows, int* next_ids, cudaStream_t st);
 

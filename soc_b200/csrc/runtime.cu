@@ -482,6 +482,10 @@ struct soc_model {
     long long graph_kernels = 0;
     // persistent batch-1 decode kernel (decode_mk.cu)
     bool mk_ok = false;
+    // Sampler(SamplerConfig) of the reference (Mac/cpu/header/sampler.h:9-12): picks maximise
+    // logit / temperature; top_k only validated (the best of the top k is the maximum).
+    float temperature = 1.0f;
+    size_t top_k = 1;
     int mk_grid = 0;
     MKLayer* d_mk_layers = nullptr;
     unsigned* mk_bars = nullptr;
@@ -732,10 +736,10 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
                           lm_rows, m->final_norm, eps, m->logits, m->v_loc, LIN_STORE, st);
         }
         if (m->tp_size == 1) {
-            launch_argmax(m->logits, m->v_loc, m->v_loc, lm_rows, m->d_next, st);
+            launch_argmax(m->logits, m->v_loc, m->v_loc, lm_rows, m->temperature, m->d_next, st);
         } else {
             unsigned long long* mine = m->d_keys + static_cast<size_t>(m->tp_rank) * lm_rows;
-            launch_argmax_keys(m->logits, m->v_loc, m->v_loc, lm_rows, m->v_off, mine, st);
+            launch_argmax_keys(m->logits, m->v_loc, m->v_loc, lm_rows, m->v_off, m->temperature, mine, st);
             nccl_check(nccl().all_gather(mine, m->d_keys, lm_rows, ncclUint64, m->comm, st), "argmax all-gather");
             launch_argmax_merge(m->d_keys, m->tp_size, lm_rows, m->d_next, st);
         }
@@ -807,7 +811,7 @@ __global__ void k_step_end(soc_model::LoopState* st, const int* next) {
 }
 
 // Persistent-kernel decode of `steps` tokens of one sequence (see decode_mk.cu).
-void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids, float* logits) {
+void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids, float* logits, int eos = -1) {
     const Config& c = m->cfg;
     cudaStream_t st = m->ctx->stream;
     if (start + steps > m->rope_len) throw Error(SOC_B200_ERR_CAPACITY, "decode position beyond the RoPE table");
@@ -864,6 +868,8 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
     p.start = start;
     p.steps = steps;
     p.logits = logits;
+    p.temperature = m->temperature;
+    p.eos = eos;
     p.h = m->mk_vec;
     p.qkv = p.h + c.hidden;
     p.attn = p.qkv + (c.hq + 2 * c.hkv) * c.hd;
@@ -900,10 +906,12 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
 
 // `steps` decode steps of sequence `seq`, whose cache holds `start` tokens and whose
 // next input id is d_out[0]; writes ids 1..steps of d_out.  One step is captured as a
-// CUDA graph (bound to this cache and split count) and replayed per token.
-void decode_loop(soc_model* m, soc_kv* kv, int seq, int start, int steps, int32_t* d_out) {
+// CUDA graph (bound to this cache and split count) and replayed per token.  eos >= 0: the
+// persistent kernel stops at the first step whose input id is eos (ids after it are not
+// written); the graph and tensor-parallel paths run every step.
+void decode_loop(soc_model* m, soc_kv* kv, int seq, int start, int steps, int32_t* d_out, int eos = -1) {
     if (m->mk_ok) {
-        run_mk(m, kv, seq, start, steps, d_out, nullptr);
+        run_mk(m, kv, seq, start, steps, d_out, nullptr, eos);
         return;
     }
     cudaStream_t st = m->ctx->stream;
@@ -1241,6 +1249,24 @@ int soc_b200_model_info(const soc_model* m, soc_model_info* out) {
     return SOC_B200_OK;
 }
 
+int soc_b200_set_sampler(soc_model* m, float temperature, size_t top_k) {
+    if (!m) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (!(temperature > 0.0f)) return fail(SOC_B200_ERR_INVALID, "sampler temperature must be positive");
+    if (top_k == 0) return fail(SOC_B200_ERR_INVALID, "sampler top_k must be positive");
+    return guarded([&] {
+        if (temperature != m->temperature) {
+            // the captured decode step holds the old temperature as a kernel argument
+            SOCB_CUDA(cudaSetDevice(m->ctx->device));
+            SOCB_CUDA(cudaStreamSynchronize(m->ctx->stream));
+            if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
+            m->step_graph = nullptr;
+            m->graph_kv = nullptr;
+        }
+        m->temperature = temperature;
+        m->top_k = top_k;
+    });
+}
+
 void soc_b200_free_model(soc_model* m) {
     if (!m) return;
     cudaSetDevice(m->ctx->device);
@@ -1469,7 +1495,7 @@ int soc_b200_decode(soc_model* m, soc_kv* kv, int n_seqs, const int* seq_ids, co
 // Device-side generation: prefill, then max_new - 1 decode steps that feed each greedy id
 // back on the device (no host round trip per token).
 static void generate_dev(soc_model* m, soc_kv* kv, int seq, const int32_t* prompt, int n_prompt, int max_new,
-                         int32_t* d_out, bool prompt_on_device) {
+                         int32_t* d_out, bool prompt_on_device, int eos = -1) {
     kv->check_seq(seq);
     if (max_new <= 0) throw Error(SOC_B200_ERR_INVALID, "generate requires max_new >= 1");
     kv->reset(seq);
@@ -1477,7 +1503,7 @@ static void generate_dev(soc_model* m, soc_kv* kv, int seq, const int32_t* promp
     kv->reserve(seq, n_prompt + max_new - 1, st);
     prefill_impl(m, kv, seq, prompt, n_prompt, prompt_on_device);
     SOCB_CUDA(cudaMemcpyAsync(d_out, m->d_next, sizeof(int), cudaMemcpyDeviceToDevice, st));
-    if (max_new > 1) decode_loop(m, kv, seq, n_prompt, max_new - 1, d_out);
+    if (max_new > 1) decode_loop(m, kv, seq, n_prompt, max_new - 1, d_out, eos);
     kv->lengths[seq] = n_prompt + max_new - 1;
 }
 
@@ -1497,7 +1523,9 @@ int soc_b200_generate(soc_model* m, soc_kv* kv, int seq, const int32_t* prompt, 
         }
         int32_t* d_out = static_cast<int32_t*>(m->dmalloc(sizeof(int32_t) * max_new));
         try {
-            generate_dev(m, kv, seq, prompt, n_prompt, max_new, d_out, false);
+            // ids after an eos stop are never written: clear them so the scan below is defined
+            if (eos_token_id >= 0) SOCB_CUDA(cudaMemsetAsync(d_out, 0xff, sizeof(int32_t) * max_new, m->ctx->stream));
+            generate_dev(m, kv, seq, prompt, n_prompt, max_new, d_out, false, eos_token_id);
             SOCB_CUDA(cudaMemcpyAsync(out_ids, d_out, sizeof(int32_t) * max_new, cudaMemcpyDeviceToHost,
                                       m->ctx->stream));
             check_device_error(m);
@@ -1726,6 +1754,8 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         p.start = pos;
         p.steps = 1;
         p.logits = lg;
+        p.temperature = m->temperature;
+        p.eos = -1;
         p.h = vec;
         p.qkv = vec + H;
         p.attn = p.qkv + (hq + 2 * hkv) * D;

@@ -88,6 +88,7 @@ _SIGNATURES = {
     "soc_b200_manifest_generation_options": (C.c_int, [C.c_char_p, C.c_void_p]),
     "soc_b200_manifest_tokenizer_path": (C.c_int, [C.c_char_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
     "soc_b200_sampler_check": (C.c_int, [C.c_float, C.c_size_t]),
+    "soc_b200_set_sampler": (C.c_int, [_VP, C.c_float, C.c_size_t]),
 }
 
 
@@ -215,6 +216,10 @@ class Model:
         _check(lib().soc_b200_decode(self.h, kv.h, n, _ip(seq_ids), _ip(last_ids),
                                      _fp(logits) if logits is not None else None, _ip(nxt)))
         return logits, nxt
+
+    def set_sampler(self, temperature: float = 1.0, top_k: int = 1) -> None:
+        """Sampler(SamplerConfig) for later picks: argmax of logit / temperature (``soc_b200_set_sampler``)."""
+        _check(lib().soc_b200_set_sampler(self.h, float(temperature), int(top_k)))
 
     def decode_noalloc(self, kv: "KVCache", seq: int, last_id: int, want_logits=True):
         """One decode step that allocates no device memory (``soc_b200_decode_noalloc``):

@@ -105,17 +105,63 @@ def test_generate_long_context_split_k(models, path):
     kv.free()
 
 
-def test_generate_eos_stops_and_truncates_cache(models):
-    p, m = models("tied_f16_gqa2_d64")
+@pytest.mark.parametrize("path", ["mk", "graph"])
+@pytest.mark.parametrize("at", [0, 3, 7])
+def test_generate_eos_stops_and_truncates_cache(models, path, at):
+    """EOS at the prefill's pick (0), mid-way (3) and at the last step (7).  On the persistent
+    kernel the stop happens on the device; the cache must then hold exactly the prompt and
+    the ids before the EOS, so decoding the EOS next continues the oracle's sequence."""
+    p, m = models("tied_f16_gqa2_d64", path)
     prompt = _prompt(CASES["tied_f16_gqa2_d64"][0], 5, 3)
-    toks, _ = O.OracleModel(p, 64).generate(prompt, 8)
+    toks, _ = O.OracleModel(p, 64).generate(prompt, 10)
     kv = R.KVCache(m, 1, 64)
-    eos = toks[3]
-    out = m.generate(kv, 0, prompt, 8, eos=eos)
+    eos = toks[at]
     first = toks.index(eos)
+    out = m.generate(kv, 0, prompt, 8, eos=eos)
     assert out == toks[: first + 1]
     assert kv.length(0) == len(prompt) + first
+    _, nxt = m.decode(kv, [0], [eos])
+    assert int(nxt[0]) == toks[first + 1]
+    assert kv.length(0) == len(prompt) + first + 1
+    # the next generation on the same model runs every step again
+    assert m.generate(kv, 0, prompt, 8) == toks[:8]
     kv.free()
+
+
+@pytest.mark.parametrize("path", ["mk", "graph"])
+@pytest.mark.parametrize("temperature", [0.7, 3.0])
+def test_sampler_temperature_on_every_pick_path(models, path, temperature):
+    """With Sampler(temperature, top_k) set, every pick (prefill, batch-1 decode, batched
+    decode, the on-device generate loop, decode_noalloc) is the reference rule applied to the
+    logits the device returns: bit-exact, since both divide the same floats."""
+    p, m = models("tied_f16_gqa2_d64", path)
+    cfg = CASES["tied_f16_gqa2_d64"][0]
+    with pytest.raises(R.SocError, match="sampler temperature must be positive"):
+        m.set_sampler(-1.0, 1)
+    with pytest.raises(R.SocError, match="sampler top_k must be positive"):
+        m.set_sampler(1.0, 0)
+    m.set_sampler(temperature, 4)
+    try:
+        kv = R.KVCache(m, 2, 256)
+        prompt = _prompt(cfg, 7, 11)
+        logits, nid = m.forward_logits_cached(kv, 0, prompt)
+        assert nid == O.sample_rule(logits, temperature)
+        picks, last = [nid], nid
+        for _ in range(6):
+            lg, nxt = m.decode(kv, [0], [last])
+            assert int(nxt[0]) == O.sample_rule(lg[0], temperature)
+            last = int(nxt[0])
+            picks.append(last)
+        assert m.generate(kv, 1, prompt, 7) == picks
+        lg, nxt = m.decode(kv, [0, 1], [last, last])
+        for r in range(2):
+            assert int(nxt[r]) == O.sample_rule(lg[r], temperature)
+        if path == "mk":
+            lg, nid2 = m.decode_noalloc(kv, 0, int(nxt[0]))
+            assert nid2 == O.sample_rule(lg, temperature)
+        kv.free()
+    finally:
+        m.set_sampler(1.0, 1)
 
 
 def test_batched_ragged_decode(models):

@@ -426,14 +426,16 @@ def run_config3(args, rank, world, local):
     """Config 3: batched ragged decode, Qwen3-0.6B with int8 group-64 linears (the config-0
     fp16 weights quantised at load time; embeddings, norms and the tied lm_head stay fp16).
     256 sequences with contexts U[128, 4096] (seed 4) of seeded ~N(0, 1) fp16 KV written on
-    the device (soc_b200_kv_fill_random, seed 4000 + sequence index), sequences split evenly
-    over the ranks, `steps` greedy decode steps of every local sequence per timed run (one
-    soc_b200_decode call per step: host ids in, host ids out).  Prints one JSON line (rank 0)
-    with the max-over-ranks time."""
+    the device (soc_b200_kv_fill_random, seed 4000 + sequence index), sequences placed on the
+    ranks by soc_b200.sharding.balanced_shards (equal counts, balanced total context),
+    `steps` greedy decode steps of every local sequence per timed run (one soc_b200_decode
+    call per step: host ids in, host ids out).  Prints one JSON line (rank 0) with the
+    max-over-ranks time."""
     import torch
     import torch.distributed as dist
     from soc_b200 import runtime as R
     from soc_b200.bundle import QWEN3_0_6B
+    from soc_b200.sharding import balanced_shards
 
     torch.cuda.set_device(local)
     if world > 1:
@@ -450,8 +452,8 @@ def run_config3(args, rank, world, local):
     model = R.Model(ctx, p, weight_format=R.WEIGHTS_INT8_G64)
     ctxs = config3_contexts()
     total = min(C3_SEQS, args.c3_seqs)  # a smaller case of the same kernels (profiling)
-    per = total // world
-    mine = list(range(rank * per, (rank + 1) * per if rank < world - 1 else total))
+    # equal counts per rank and balanced total context (the KV read bounds each step)
+    mine = balanced_shards(ctxs[:total], world)[rank]
     n = len(mine)
     steps, warmup = args.steps, max(args.warmup, 3)
     cap = int(sum(-(-(int(ctxs[g]) + steps + warmup + 1) // 16) * 16 for g in mine))

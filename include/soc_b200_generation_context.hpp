@@ -6,14 +6,21 @@
 // Generate with a nullable std::string* error_message, Reset(), and the prompt
 // / running token id accessors.  The Metal-specific arguments (MetalContext,
 // PipelineCache*, BufferArena*) have no B200 counterpart: device, stream and
-// buffers live in the soc_ctx / soc_model / soc_kv handles.  Sampling is greedy
-// on the device (top_k 1, the reference's default SamplerConfig), so only the
+// buffers live in the soc_ctx / soc_model / soc_kv handles.  The next-token pick
+// happens on the device (the model's Sampler, soc_b200_set_sampler), so only the
 // token id -- and the logits row when asked for -- crosses PCIe.
+//
+// Also here: Tokenizer (TokenizerRuntime + Qwen3TemplateBuilder, Mac/cpu/header/
+// tokenizer_runtime.h:12-46, runtime_assets.cpp:221-258) and
+// GenerationOptionsFromManifest (RuntimePipeline, runtime_pipeline.cpp:43-55), which
+// throw std::runtime_error with the library's message as the reference does.
 #pragma once
 
 #include <cstddef>
 #include <cstdint>
+#include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "soc_b200.h"
@@ -131,5 +138,107 @@ private:
     std::vector<int> running_token_ids_;
     int prefill_next_ = -1;
 };
+
+struct ChatMessage {
+    std::string role;
+    std::string content;
+};
+
+// The bundle's tokenizer (host only).  Move-only owner of a soc_tokenizer.
+class Tokenizer {
+public:
+    // TokenizerRuntimeLoader::LoadFromFile + ValidateTokenizerRuntime.
+    static Tokenizer LoadFromFile(const std::string& tokenizer_runtime_path) {
+        soc_tokenizer* t = nullptr;
+        Check(soc_b200_tokenizer_load(tokenizer_runtime_path.c_str(), &t));
+        return Tokenizer(t);
+    }
+    // The tokenizer a manifest names (its path resolved against the manifest's directory).
+    static Tokenizer LoadFromManifest(const std::string& manifest_path) {
+        std::size_t n = 0;
+        soc_b200_manifest_tokenizer_path(manifest_path.c_str(), nullptr, 0, &n);
+        std::string path(n + 1, '\0');
+        Check(soc_b200_manifest_tokenizer_path(manifest_path.c_str(), &path[0], path.size(), &n));
+        path.resize(n);
+        return LoadFromFile(path);
+    }
+    Tokenizer(Tokenizer&& o) noexcept : t_(std::exchange(o.t_, nullptr)) {}
+    Tokenizer& operator=(Tokenizer&& o) noexcept {
+        std::swap(t_, o.t_);
+        return *this;
+    }
+    Tokenizer(const Tokenizer&) = delete;
+    Tokenizer& operator=(const Tokenizer&) = delete;
+    ~Tokenizer() { soc_b200_tokenizer_free(t_); }
+
+    std::vector<int> Encode(const std::string& text) const {
+        std::vector<int32_t> ids(text.size() + 16);
+        int n = 0;
+        int rc = soc_b200_tokenizer_encode(t_, text.data(), text.size(), ids.data(), static_cast<int>(ids.size()), &n);
+        if (rc == SOC_B200_ERR_CAPACITY) {
+            ids.resize(static_cast<std::size_t>(n));
+            rc = soc_b200_tokenizer_encode(t_, text.data(), text.size(), ids.data(), n, &n);
+        }
+        Check(rc);
+        return std::vector<int>(ids.begin(), ids.begin() + n);
+    }
+    std::string Decode(const std::vector<int>& token_ids) const {
+        std::vector<int32_t> ids(token_ids.begin(), token_ids.end());
+        std::string out(64 + 16 * ids.size(), '\0');
+        std::size_t n = 0;
+        int rc = soc_b200_tokenizer_decode(t_, ids.data(), static_cast<int>(ids.size()), &out[0], out.size(), &n);
+        if (rc == SOC_B200_ERR_CAPACITY) {
+            out.assign(n, '\0');
+            rc = soc_b200_tokenizer_decode(t_, ids.data(), static_cast<int>(ids.size()), &out[0], out.size(), &n);
+        }
+        Check(rc);
+        out.resize(n);
+        return out;
+    }
+    // Qwen3TemplateBuilder::BuildPrompt.
+    std::string BuildPrompt(const std::vector<ChatMessage>& messages, bool add_generation_prompt, bool enable_thinking,
+                            const std::string& system_prompt_override = "") const {
+        std::vector<const char*> roles, contents;
+        std::size_t cap = 256 + system_prompt_override.size();
+        for (const ChatMessage& m : messages) {
+            roles.push_back(m.role.c_str());
+            contents.push_back(m.content.c_str());
+            cap += m.role.size() + m.content.size() + 32;
+        }
+        std::string out(cap, '\0');
+        std::size_t n = 0;
+        auto call = [&] {
+            return soc_b200_chat_prompt(t_, roles.data(), contents.data(), static_cast<int>(messages.size()),
+                                        add_generation_prompt, enable_thinking, system_prompt_override.c_str(), &out[0],
+                                        out.size(), &n);
+        };
+        int rc = call();
+        if (rc == SOC_B200_ERR_CAPACITY) {
+            out.assign(n, '\0');
+            rc = call();
+        }
+        Check(rc);
+        out.resize(n);
+        return out;
+    }
+    // StartupValidator::ValidateManifestAndTokenizer's vocab checks against a loaded model.
+    void CheckModel(const soc_model_info& info) const { Check(soc_b200_tokenizer_check_model(t_, info.vocab)); }
+    const soc_tokenizer* handle() const { return t_; }
+
+private:
+    explicit Tokenizer(soc_tokenizer* t) : t_(t) {}
+    static void Check(int rc) {
+        if (rc != SOC_B200_OK) throw std::runtime_error(soc_b200_last_error());
+    }
+    soc_tokenizer* t_ = nullptr;
+};
+
+// RuntimeGenerationOptions from the manifest's generation_config (defaults where absent).
+inline soc_generation_options GenerationOptionsFromManifest(const std::string& manifest_path) {
+    soc_generation_options o{};
+    if (soc_b200_manifest_generation_options(manifest_path.c_str(), &o) != SOC_B200_OK)
+        throw std::runtime_error(soc_b200_last_error());
+    return o;
+}
 
 }  // namespace soc::b200

@@ -12,7 +12,7 @@
 // per slice), releasing each ring slot with tcgen05.commit; warps 2-5 drain the other
 // accumulator with tcgen05.ld while the next tile accumulates.  Every mbarrier wait is
 // bounded: on expiry the kernel records DERR_WAIT_TIMEOUT, stops issuing, frees TMEM and
-// returns.  No load uses cluster multicast.
+// returns.  Every TMA load fills only this CTA's own shared memory.
 #include <cudaTypedefs.h>
 
 #include <algorithm>

@@ -282,7 +282,7 @@ class RefModel:
         self.lib = lib
         self.h = lib.socref_load(str(manifest_path).encode())
         if not self.h:
-            raise RuntimeError(lib.socref_last_error().decode())
+            raise RuntimeError(lib.socref_last_error().decode("utf-8", "replace"))
         self.cfg = json.loads(Path(manifest_path).read_text())["config"]
         self.vocab = self.cfg["vocab_size"]
         self.c = lib.socref_cache_new(self.h, max_seq)
@@ -302,7 +302,7 @@ class RefModel:
         ids = np.ascontiguousarray(ids, dtype=np.int32)
         out = np.empty((ids.size, self.vocab), dtype=np.float32)
         if self.lib.socref_forward_cached(self.h, self.c, _ip(ids), ids.size, int(pos), _fp(out)) != 0:
-            raise RuntimeError(self.lib.socref_last_error().decode())
+            raise RuntimeError(self.lib.socref_last_error().decode("utf-8", "replace"))
         return out
 
     def sample(self, logits_row) -> int:
@@ -314,7 +314,7 @@ class RefModel:
         k = np.empty((end - start, hkv, hd), dtype=np.float32)
         v = np.empty_like(k)
         if self.lib.socref_kv_read(self.c, layer, start, end, _fp(k), _fp(v)) != 0:
-            raise RuntimeError(self.lib.socref_last_error().decode())
+            raise RuntimeError(self.lib.socref_last_error().decode("utf-8", "replace"))
         return k, v
 
 
@@ -322,7 +322,7 @@ def ref_linear(x, w):
     x, w = _f32(x), _f32(w)
     y = np.empty((x.size // w.shape[1], w.shape[0]), dtype=np.float32)
     if ref_lib().socref_linear(_fp(x), y.shape[0], w.shape[1], _fp(w), w.shape[0], _fp(y)) != 0:
-        raise RuntimeError(ref_lib().socref_last_error().decode())
+        raise RuntimeError(ref_lib().socref_last_error().decode("utf-8", "replace"))
     return y
 
 
@@ -330,7 +330,7 @@ def ref_rmsnorm(x, w, eps=1e-6):
     x, w = _f32(x), _f32(w)
     y = np.empty_like(x)
     if ref_lib().socref_rmsnorm(_fp(x), x.size // w.size, w.size, _fp(w), eps, _fp(y)) != 0:
-        raise RuntimeError(ref_lib().socref_last_error().decode())
+        raise RuntimeError(ref_lib().socref_last_error().decode("utf-8", "replace"))
     return y
 
 
@@ -338,7 +338,7 @@ def ref_rope(x, theta, pos0):
     y = _f32(x).copy()
     T, Hh, D = y.shape
     if ref_lib().socref_rope(_fp(y), T, Hh, D, float(theta), int(pos0)) != 0:
-        raise RuntimeError(ref_lib().socref_last_error().decode())
+        raise RuntimeError(ref_lib().socref_last_error().decode("utf-8", "replace"))
     return y
 
 
@@ -347,7 +347,7 @@ def ref_attention(q, k, v, prefix):
     out = np.empty_like(q)
     if ref_lib().socref_attention(_fp(q), q.shape[0], q.shape[1], _fp(k), _fp(v), k.shape[0], k.shape[1],
                                   k.shape[2], int(prefix), _fp(out)) != 0:
-        raise RuntimeError(ref_lib().socref_last_error().decode())
+        raise RuntimeError(ref_lib().socref_last_error().decode("utf-8", "replace"))
     return out
 
 
@@ -392,11 +392,13 @@ class RefTokenizer:
             lib.socref_tokenizer_decode.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_char_p, C.c_int]
             lib.socref_chat_prompt.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, C.c_char_p, C.c_char_p,
                                                C.c_int]
+            lib.socref_chat_prompt_messages.argtypes = [C.c_void_p, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p),
+                                                        C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_char_p, C.c_int]
             lib._tok_bound = True
         self.lib = lib
         self.h = lib.socref_tokenizer_load(str(path).encode())
         if not self.h:
-            raise ValueError(lib.socref_last_error().decode())
+            raise ValueError(lib.socref_last_error().decode("utf-8", "replace"))
 
     def free(self):
         if self.h:
@@ -409,7 +411,7 @@ class RefTokenizer:
         ids = (C.c_int32 * cap)()
         n = self.lib.socref_tokenizer_encode(self.h, data, len(data), ids, cap)
         if n < 0:
-            raise ValueError(self.lib.socref_last_error().decode())
+            raise ValueError(self.lib.socref_last_error().decode("utf-8", "replace"))
         return list(ids[:n])
 
     def decode_bytes(self, ids):
@@ -418,7 +420,7 @@ class RefTokenizer:
         buf = C.create_string_buffer(cap)
         n = self.lib.socref_tokenizer_decode(self.h, arr, len(ids), buf, cap)
         if n < 0:
-            raise ValueError(self.lib.socref_last_error().decode())
+            raise ValueError(self.lib.socref_last_error().decode("utf-8", "replace"))
         return buf.raw[:n]
 
     def chat_prompt(self, user, add_generation_prompt=True, enable_thinking=True, system_prompt=""):
@@ -427,8 +429,20 @@ class RefTokenizer:
         n = self.lib.socref_chat_prompt(self.h, user.encode(), int(add_generation_prompt), int(enable_thinking),
                                         system_prompt.encode(), buf, cap)
         if n < 0:
-            raise ValueError(self.lib.socref_last_error().decode())
+            raise ValueError(self.lib.socref_last_error().decode("utf-8", "replace"))
         return buf.raw[:n].decode("utf-8")
+
+    def chat_prompt_messages(self, messages, add_generation_prompt=True, enable_thinking=True, system_prompt=""):
+        n = len(messages)
+        roles = (C.c_char_p * max(n, 1))(*[r.encode() for r, _ in messages])
+        contents = (C.c_char_p * max(n, 1))(*[c.encode() for _, c in messages])
+        cap = 1024 + sum(4 * len(c.encode()) + len(r) for r, c in messages) + len(system_prompt.encode())
+        buf = C.create_string_buffer(cap)
+        k = self.lib.socref_chat_prompt_messages(self.h, roles, contents, n, int(add_generation_prompt),
+                                                 int(enable_thinking), system_prompt.encode(), buf, cap)
+        if k < 0:
+            raise ValueError(self.lib.socref_last_error().decode("utf-8", "replace"))
+        return buf.raw[:k].decode("utf-8")
 
 
 def ref_sample(logits_row, temperature=1.0, top_k=1) -> int:
@@ -436,7 +450,7 @@ def ref_sample(logits_row, temperature=1.0, top_k=1) -> int:
     x = _f32(logits_row)
     r = int(ref_lib().socref_sample(_fp(x), x.size, float(temperature), int(top_k)))
     if r < 0:
-        raise ValueError(ref_lib().socref_last_error().decode())
+        raise ValueError(ref_lib().socref_last_error().decode("utf-8", "replace"))
     return r
 
 

@@ -237,4 +237,21 @@ int socref_chat_prompt(void* t, const char* user, int add_generation_prompt, int
     }
 }
 
+// Qwen3TemplateBuilder::BuildPrompt over n (role, content) messages.
+int socref_chat_prompt_messages(void* t, const char* const* roles, const char* const* contents, int n,
+                                int add_generation_prompt, int enable_thinking, const char* system_override, char* out,
+                                int cap) {
+    try {
+        const Qwen3TemplateBuilder builder(static_cast<TokenizerRuntime*>(t)->runtime_data().template_runtime);
+        std::vector<ChatMessage> messages;
+        for (int i = 0; i < n; ++i) messages.push_back(ChatMessage{roles[i], contents[i]});
+        const std::string s = builder.BuildPrompt(messages, add_generation_prompt != 0, enable_thinking != 0,
+                                                  system_override ? system_override : "");
+        std::memcpy(out, s.data(), std::min<std::size_t>(s.size(), static_cast<std::size_t>(cap)));
+        return static_cast<int>(s.size());
+    } catch (const std::exception& e) {
+        return Fail(e);
+    }
+}
+
 }  // extern "C"

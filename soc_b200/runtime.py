@@ -109,7 +109,7 @@ def lib() -> C.CDLL:
 
 def _check(rc: int) -> None:
     if rc != OK:
-        raise SocError(rc, lib().soc_b200_last_error().decode())
+        raise SocError(rc, lib().soc_b200_last_error().decode("utf-8", "replace"))
 
 
 def _i32(a) -> np.ndarray:

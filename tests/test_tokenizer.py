@@ -145,3 +145,80 @@ def test_tokenizer_vocab_checked_against_model(bpe_path):
     with pytest.raises(R.SocError, match="must not exceed qwen3 config vocab_size"):
         t.check_model(999)
     t.free()
+
+
+def _variant(name):
+    """Tokenizer documents that switch on the options the synthetic tokenizer leaves off."""
+    from soc_b200.bundle import bytes_to_unicode
+    doc = synthetic_bpe_tokenizer(2000)
+    if name == "prefix_space":
+        doc["pre_tokenizer"]["byte_level"]["add_prefix_space"] = True
+    elif name == "no_regex":
+        doc["pre_tokenizer"]["byte_level"]["use_regex"] = False
+    elif name == "subword_prefix_unk":
+        doc["bpe_model"]["continuing_subword_prefix"] = "##"
+        doc["bpe_model"]["unk_token"] = "<|endoftext|>"
+    elif name == "word_suffix":
+        doc["bpe_model"]["end_of_word_suffix"] = "</w>"
+        doc["decoder"]["bpe"] = {"enabled": True, "suffix": "</w>"}
+        b2u = bytes_to_unicode()
+        first = 256 + len(doc["bpe_model"]["merges"])
+        for b in range(256):  # replace filler ids by the suffixed byte symbols
+            doc["vocab"][first + b]["token"] = b2u[b] + "</w>"
+    elif name == "no_byte_level":
+        doc["pre_tokenizer"] = None
+        doc["decoder"] = None
+    return doc
+
+
+VARIANT_TEXTS = ["Hello world, the quick brown fox!", "  two  spaces", "abc", "x", "end.", "café 12",
+                 "<|im_start|>user\nhi<|im_end|>", ""]
+
+
+@pytest.mark.parametrize("name", ["prefix_space", "no_regex", "subword_prefix_unk", "word_suffix", "no_byte_level"])
+def test_tokenizer_options_match_reference(tmp_path, name):
+    p = tmp_path / "tok.json"
+    p.write_text(json.dumps(_variant(name)))
+    ours, ref = _pair(p)
+    for text in VARIANT_TEXTS:
+        try:
+            expect = ref.encode(text)
+        except ValueError as e:
+            with pytest.raises(R.SocError) as got:
+                ours.encode(text)
+            assert str(e) in str(got.value), (name, text)
+            continue
+        ids = ours.encode(text)
+        assert ids == expect, (name, text)
+        assert ours.decode_bytes(ids) == ref.decode_bytes(ids), (name, text)
+    ours.free()
+    ref.free()
+
+
+def test_missing_unk_token_rejected_like_reference(tmp_path):
+    doc = synthetic_bpe_tokenizer(1000)
+    doc["bpe_model"]["unk_token"] = "<nope>"
+    p = tmp_path / "tok.json"
+    p.write_text(json.dumps(doc))
+    if not O.ref_available():
+        pytest.skip("reference library not built (oracle/_ref)")
+    with pytest.raises(ValueError) as ref_err:
+        O.RefTokenizer(p)
+    with pytest.raises(R.SocError) as ours_err:
+        R.Tokenizer(p)
+    assert str(ref_err.value) in str(ours_err.value)
+
+
+@pytest.mark.parametrize("gen,think,system", [(True, True, ""), (True, False, "Custom system prompt."),
+                                              (False, True, "")])
+def test_multi_turn_chat_prompt_matches_reference(bpe_path, gen, think, system):
+    """The reference's own template test conversation (user, assistant, user), and one that
+    brings its own system message."""
+    ours, ref = _pair(bpe_path)
+    convs = [[("user", "Say hello."), ("assistant", "Hello."), ("user", "Now think first.")],
+             [("system", "Only facts."), ("user", "2+2?"), ("assistant", "4"), ("user", "And 3+3?")],
+             []]
+    for msgs in convs:
+        assert ours.chat_prompt(msgs, gen, think, system) == ref.chat_prompt_messages(msgs, gen, think, system)
+    ours.free()
+    ref.free()

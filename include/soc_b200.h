@@ -98,8 +98,11 @@ SOC_B200_API int soc_b200_model_info(const soc_model* model, soc_model_info* out
  * of this model (prefill, decode, generate, decode_noalloc): the id maximising
  * logit / temperature, the division IEEE single precision as in the reference, lowest id on
  * ties.  The reference returns the best of the top_k largest such scores, which is that
- * maximum for every top_k >= 1, so top_k is only validated.  Defaults: 1.0 and 1; the
- * argument checks and their messages are the reference's. */
+ * maximum for every top_k >= 1, so top_k is only validated.  One difference: when the
+ * largest score repeats and top_k > 1, the reference returns whichever of the tied ids its
+ * C++ library's partial_sort puts first (not specified by the language; the lowest id for
+ * top_k = 1), this library the lowest.  Defaults: 1.0 and 1; the argument checks and their
+ * messages are the reference's. */
 SOC_B200_API int soc_b200_set_sampler(soc_model* model, float temperature, size_t top_k);
 SOC_B200_API void soc_b200_free_model(soc_model* model);
 

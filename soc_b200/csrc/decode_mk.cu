@@ -777,7 +777,11 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                 }
             }
         }
-        for (int g = 0; g < G; ++g) {
+        // unrolled over MAXG with a guard: a loop bounded by the run-time G would index o / m /
+        // lsum dynamically and move them (and every update of them above) to local memory
+#pragma unroll
+        for (int g = 0; g < MAXG; ++g) {
+            if (g >= G) break;
             float* mr = merge + (cw * G + g) * (D + 2);
 #pragma unroll
             for (int q = 0; q < DL; ++q) mr[lane * DL + q] = o[g][q];

@@ -15,9 +15,11 @@
 // design works on two things: keeping HBM busy across the dependencies, and
 // making each dependency hand-off short.
 //   * warp 0, lane 0 is a producer: it walks this CTA's share of every weight
-//     matrix in execution order and streams it into a 5 x 32 KB shared-memory
+//     matrix in execution order and streams it into a 6 x 32 KB shared-memory
 //     ring with cp.async.bulk (TMA bulk copies, mbarrier completion, L2
-//     evict-first).  It never waits on activations.
+//     evict-first).  It never waits on activations; with an EOS id set it waits
+//     at each step boundary for the step's argmax, so that no weight of a step
+//     that will not run is loaded.
 //   * warps 1..7 are consumers: per matrix they stage the input vector once per
 //     CTA (double-buffered, one CTA barrier per phase), hold their slice of it in
 //     registers and reduce 16-byte weight vectors from the ring with fp32 FMAs

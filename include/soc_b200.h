@@ -94,6 +94,13 @@ SOC_B200_API void* soc_b200_stream(soc_ctx* ctx);
 SOC_B200_API int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_format, int tp_rank, int tp_size,
                          void* nccl_comm, soc_model** out);
 SOC_B200_API int soc_b200_model_info(const soc_model* model, soc_model_info* out);
+/* The checks RuntimePipeline::LoadBundle makes before it has a model (Mac/cpu/src/
+ * runtime_pipeline.cpp:36-41): the manifest and tokenizer loaders, StartupValidator::
+ * ValidateManifestAndTokenizer (startup_validator.cpp:5-23, 77-101) and the record checks of
+ * every tensor QwenModelLoader::LoadModel reads (qwen_model_loader.cpp:35-93, weight_loader.cpp:
+ * 17-30), with the same messages.  Host only: needs no device and reads no weight data (tensor
+ * files are only measured), so a host can reject a broken bundle before it opens a GPU. */
+SOC_B200_API int soc_b200_validate_bundle(const char* manifest_path);
 /* Sampler(SamplerConfig) (Mac/cpu/src/sampler.cpp:17-57) for every later next-token pick
  * of this model (prefill, decode, generate, decode_noalloc): the id maximising
  * logit / temperature, the division IEEE single precision as in the reference, lowest id on

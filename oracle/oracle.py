@@ -86,6 +86,7 @@ def ref_lib() -> C.CDLL:
         lib.socref_forward_cached.argtypes = [C.c_void_p, C.c_void_p, _I, C.c_int, C.c_int, _F]
         lib.socref_sample_greedy.argtypes = [_F, C.c_int]
         lib.socref_sample.argtypes = [_F, C.c_int, C.c_float, C.c_int]
+        lib.socref_load_bundle.argtypes = [C.c_char_p]
         lib.socref_kv_read.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _F, _F]
         lib.socref_linear.argtypes = [_F, C.c_int, C.c_int, _F, C.c_int, _F]
         lib.socref_rmsnorm.argtypes = [_F, C.c_int, C.c_int, _F, C.c_float, _F]
@@ -459,3 +460,11 @@ def sample_rule(logits_row, temperature=1.0) -> int:
     (float32 IEEE division, as the reference's comparator computes it)."""
     x = _f32(logits_row)
     return int(np.argmax(x / np.float32(temperature)))
+
+
+def ref_load_bundle(manifest_path) -> str | None:
+    """The reference's RuntimePipeline::LoadBundle: None when it loads, else its error message."""
+    lib = ref_lib()
+    if lib.socref_load_bundle(str(manifest_path).encode()) == 0:
+        return None
+    return lib.socref_last_error().decode("utf-8", "replace")

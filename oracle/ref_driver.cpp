@@ -24,6 +24,7 @@
 #include "header/rms_norm_module.h"
 #include "header/rope.h"
 #include "header/runtime_assets.h"
+#include "header/runtime_pipeline.h"
 #include "header/sampler.h"
 #include "header/startup_validator.h"
 #include "header/tokenizer_runtime.h"
@@ -75,6 +76,18 @@ void* socref_load(const char* manifest_path) {
 }
 
 void socref_free(void* p) { delete static_cast<RefModel*>(p); }
+
+// RuntimePipeline::LoadBundle (manifest, tokenizer, their validation, the model's tensors):
+// 0, or -1 with the reference's message in socref_last_error.
+int socref_load_bundle(const char* manifest_path) {
+    try {
+        const RuntimeBundle bundle = RuntimePipeline::LoadBundle(manifest_path);
+        (void)bundle;
+        return 0;
+    } catch (const std::exception& e) {
+        return Fail(e);
+    }
+}
 
 void* socref_cache_new(void* p, int max_seq) {
     try {

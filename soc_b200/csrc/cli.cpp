@@ -152,7 +152,10 @@ std::string chat_prompt(const soc_tokenizer* tok, const Options& o) {
 
 int run(const Options& cli) {
     Handles h;
-    // RuntimePipeline::LoadBundle: manifest, tokenizer, their cross checks, then the model.
+    // RuntimePipeline::LoadBundle: manifest, tokenizer, their cross checks and the tensor
+    // records, all on the host (a broken bundle is reported before the GPU is touched), then
+    // the model.
+    check(soc_b200_validate_bundle(cli.manifest.c_str()));
     check(soc_b200_tokenizer_load(tokenizer_path(cli.manifest).c_str(), &h.tok));
     check(soc_b200_open(cli.device, &h.ctx));
     check(soc_b200_load_bundle(h.ctx, cli.manifest.c_str(), cli.weight_format, 0, 1, nullptr, &h.model));

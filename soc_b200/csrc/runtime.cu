@@ -180,8 +180,9 @@ Config read_config(const Json& c) {
 }
 
 // WeightLoader::LoadTensor checks (Mac/cpu/src/weight_loader.cpp:17-30), then reads the bytes.
+// The record's own consistency first, then the file, then the shape the model expects (the
+// order in which WeightLoader::LoadTensor and RequireFloatingWeight report them).
 std::vector<char> load_record(const TensorRecord& r, const std::vector<size_t>& expect_shape) {
-    if (r.shape != expect_shape) throw_fmt("model loader encountered unexpected shape for: " + r.name);
     size_t numel = 1;
     for (size_t s : r.shape) numel *= s;
     const size_t expect = numel * dtype_width(r.dtype);
@@ -190,6 +191,7 @@ std::vector<char> load_record(const TensorRecord& r, const std::vector<size_t>& 
     if (stat(r.file.c_str(), &st) != 0) throw Error(SOC_B200_ERR_IO, "failed to open tensor file: " + r.file);
     if (static_cast<size_t>(st.st_size) < r.byte_size)
         throw Error(SOC_B200_ERR_IO, "tensor file is smaller than expected byte_size for: " + r.name);
+    if (r.shape != expect_shape) throw_fmt("model loader encountered unexpected shape for: " + r.name);
     std::vector<char> buf(r.byte_size);
     FILE* f = std::fopen(r.file.c_str(), "rb");
     if (!f) throw Error(SOC_B200_ERR_IO, "failed to open tensor file: " + r.file);
@@ -401,6 +403,91 @@ HostMat prepare_matrix(const Manifest& man, const std::string& name, size_t rows
         }
     }
     return out;
+}
+
+// WeightLoader::LoadTensor's record checks (weight_loader.cpp:17-30) without reading the data:
+// byte_size against the record's dtype and shape, then the file's length.
+void check_record(const TensorRecord& r) {
+    size_t numel = 1;
+    for (size_t s : r.shape) numel *= s;
+    if (numel * dtype_width(r.dtype) != r.byte_size)
+        throw_fmt("tensor record byte_size does not match dtype and shape for: " + r.name);
+    struct stat st {};
+    if (stat(r.file.c_str(), &st) != 0) throw Error(SOC_B200_ERR_IO, "failed to open tensor file: " + r.file);
+    if (static_cast<size_t>(st.st_size) < r.byte_size)
+        throw Error(SOC_B200_ERR_IO, "tensor file is smaller than expected byte_size for: " + r.name);
+}
+
+// RequireFloatingWeight (qwen_model_loader.cpp:17-26): the record, a float type, the expected
+// shape.  Block linears may also be group-quantised records with their scales (this library's
+// bundle extension).
+void check_weight(const Manifest& man, const std::string& name, const std::vector<size_t>& shape,
+                  bool may_be_quantised = false) {
+    const TensorRecord& r = man.find(name);
+    const int src = fmt_of_dtype(r.dtype);
+    if (may_be_quantised && (src == WF_I8G64 || src == WF_I4G32)) {
+        const size_t rows = shape[0], cols = shape[1];
+        if (r.shape != shape) throw_fmt("model loader encountered unexpected shape for: " + name);
+        const int g = quant_group(src);
+        if (cols % g != 0) throw_fmt("quantised tensor columns are not a multiple of the group for: " + name);
+        TensorRecord raw = r;
+        raw.dtype = "uint8";
+        raw.shape = {rows * fmt_row_bytes(src, cols)};
+        check_record(raw);
+        const TensorRecord& rs = man.find(name + ".scales");
+        if (rs.dtype != "float16") throw_fmt("quantisation scales must be float16 for: " + name);
+        check_record(rs);
+        if (rs.shape != std::vector<size_t>{rows, cols / g})
+            throw_fmt("model loader encountered unexpected shape for: " + rs.name);
+        return;
+    }
+    check_record(r);
+    if (r.dtype != "float16" && r.dtype != "bfloat16" && r.dtype != "float32")
+        throw_fmt("model loader requires floating-point weights for: " + name);
+    if (r.shape != shape) throw_fmt("model loader encountered unexpected shape for: " + name);
+}
+
+// RuntimePipeline::LoadBundle's checks (Mac/cpu/src/runtime_pipeline.cpp:36-41) on the host:
+// ManifestLoader + TokenizerRuntimeLoader, StartupValidator::ValidateManifestAndTokenizer, and
+// every record QwenModelLoader::LoadModel reads (qwen_model_loader.cpp:35-93), in that order.
+// Weights are not read; their files are only measured.
+void validate_bundle(const std::string& manifest_path) {
+    const Manifest man = load_manifest(manifest_path);
+    std::string tok_path;
+    {
+        size_t n = 0;
+        soc_b200_manifest_tokenizer_path(manifest_path.c_str(), nullptr, 0, &n);
+        tok_path.assign(n + 1, '\0');
+        if (soc_b200_manifest_tokenizer_path(manifest_path.c_str(), &tok_path[0], tok_path.size(), &n) != SOC_B200_OK)
+            throw Error(SOC_B200_ERR_FORMAT, soc_b200_last_error());
+        tok_path.resize(n);
+    }
+    soc_tokenizer* tok = nullptr;
+    int rc = soc_b200_tokenizer_load(tok_path.c_str(), &tok);
+    if (rc != SOC_B200_OK) throw Error(rc, soc_b200_last_error());
+    const Config c = read_config(man.config);
+    rc = soc_b200_tokenizer_check_model(tok, static_cast<long long>(c.vocab));
+    soc_b200_tokenizer_free(tok);
+    if (rc != SOC_B200_OK) throw Error(rc, soc_b200_last_error());
+
+    const size_t H = c.hidden, I = c.inter, D = c.hd, QW = c.hq * D, KW = c.hkv * D;
+    check_weight(man, "model.embed_tokens.weight", {c.vocab, H});
+    for (size_t l = 0; l < c.layers; ++l) {  // the reference loader's order
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        check_weight(man, p + "input_layernorm.weight", {H});
+        check_weight(man, p + "self_attn.q_proj.weight", {QW, H}, true);
+        check_weight(man, p + "self_attn.k_proj.weight", {KW, H}, true);
+        check_weight(man, p + "self_attn.v_proj.weight", {KW, H}, true);
+        check_weight(man, p + "self_attn.o_proj.weight", {H, QW}, true);
+        check_weight(man, p + "self_attn.q_norm.weight", {D});
+        check_weight(man, p + "self_attn.k_norm.weight", {D});
+        check_weight(man, p + "post_attention_layernorm.weight", {H});
+        check_weight(man, p + "mlp.gate_proj.weight", {I, H}, true);
+        check_weight(man, p + "mlp.up_proj.weight", {I, H}, true);
+        check_weight(man, p + "mlp.down_proj.weight", {H, I}, true);
+    }
+    check_weight(man, "model.norm.weight", {H});
+    if (!c.tied) check_weight(man, "lm_head.weight", {c.vocab, H});
 }
 
 }  // namespace
@@ -1227,6 +1314,11 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
     }
     *out = m.release();
     return SOC_B200_OK;
+}
+
+int soc_b200_validate_bundle(const char* manifest_path) {
+    if (!manifest_path) return fail(SOC_B200_ERR_INVALID, "null argument");
+    return guarded([&] { validate_bundle(manifest_path); });
 }
 
 int soc_b200_model_info(const soc_model* m, soc_model_info* out) {

@@ -89,6 +89,7 @@ _SIGNATURES = {
     "soc_b200_manifest_tokenizer_path": (C.c_int, [C.c_char_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
     "soc_b200_sampler_check": (C.c_int, [C.c_float, C.c_size_t]),
     "soc_b200_set_sampler": (C.c_int, [_VP, C.c_float, C.c_size_t]),
+    "soc_b200_validate_bundle": (C.c_int, [C.c_char_p]),
 }
 
 
@@ -369,6 +370,12 @@ class GenerationOptions(C.Structure):
     def check(self) -> None:
         """The sampler's argument checks (Mac/cpu/src/sampler.cpp:17-20)."""
         _check(lib().soc_b200_sampler_check(self.temperature, self.top_k))
+
+
+def validate_bundle(manifest_path) -> None:
+    """RuntimePipeline::LoadBundle's checks without a device (``soc_b200_validate_bundle``):
+    raises SocError with the reference loader's message for the first problem found."""
+    _check(lib().soc_b200_validate_bundle(str(manifest_path).encode()))
 
 
 def manifest_tokenizer_path(manifest_path) -> str:

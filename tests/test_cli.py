@@ -114,3 +114,31 @@ def test_cli_eos_and_capacity_match_reference(bpe_bundle):
         assert out == out_r
         if rc:
             assert err.splitlines()[0] == err_r.splitlines()[0]
+
+
+@pytest.mark.parametrize("fault", ["missing_tensor", "byte_size", "config", "tokenizer_vocab"])
+def test_broken_bundle_reported_like_reference(bpe_bundle, tmp_path, fault):
+    """Broken bundles fail in both runners with the same first line, before any device work
+    (so this runs without a GPU)."""
+    import json
+    import shutil
+    d = tmp_path / "b"
+    shutil.copytree(bpe_bundle.parent, d)
+    mp = d / "manifest.json"
+    m = json.loads(mp.read_text())
+    if fault == "missing_tensor":
+        m["tensors"] = [t for t in m["tensors"] if not t["name"].endswith("layers.1.mlp.gate_proj.weight")]
+    elif fault == "byte_size":
+        next(t for t in m["tensors"] if t["name"] == "model.norm.weight")["byte_size"] = 3
+    elif fault == "config":
+        m["config"]["num_key_value_heads"] = 3
+    else:
+        tp = d / m["tokenizer_runtime_file"]
+        doc = json.loads(tp.read_text())
+        doc["vocab_size"] = 4096
+        tp.write_text(json.dumps(doc))
+    mp.write_text(json.dumps(m))
+    rc, out, err = _run(OURS, "--manifest", mp, "--prompt", "hi")
+    rc_r, out_r, err_r = _run(REF, "--manifest", mp, "--prompt", "hi")
+    assert rc == rc_r == 1 and out == out_r == ""
+    assert err.splitlines()[0] == err_r.splitlines()[0]

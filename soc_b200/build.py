@@ -21,7 +21,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xcompiler", "-fvisibility=hidden"]
 
-SOURCES = ["runtime.cu", "kernels.cu", "decode_mk.cu", "gemm_tc.cu", "attn_prefill.cu", "nccl_rt.cu", "attn_decode.cu", "tokenizer.cu"]
+SOURCES = ["runtime.cu", "kernels.cu", "decode_mk.cu", "gemm_tc.cu", "attn_prefill.cu", "nccl_rt.cu", "attn_decode.cu", "tokenizer.cu",
+           "attn_prefill_tc.cu"]
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:

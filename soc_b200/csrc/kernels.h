@@ -60,6 +60,10 @@ int attention_splits(int rows, int hkv, int max_visible);
 // sequence `seq`) on tensor cores (attn_prefill.cu).  Same output layout as launch_attention.
 void launch_flash_prefill(const float* q, int n, int hq, int hkv, int head_dim, int seq, int start,
                           const KVLayerView& kv, float* out, cudaStream_t st);
+// The same attention on tcgen05 with S and O in tensor memory (attn_prefill_tc.cu); needs the
+// cache's TMA maps.  Not yet used by the forward path.
+void launch_flash_prefill_tc(const float* q, int n, int hq, int hkv, int head_dim, int seq, int start,
+                             const KVLayerView& kv, float* out, int* err, cudaStream_t st);
 
 // Seeded pseudo-random K and V (about N(0, 1), fp16) for positions [0, n_tokens) of sequence
 // `seq` in every layer; `pages` = that sequence's page-table row.

@@ -718,6 +718,13 @@ int flash_min_rows() {
     return e && *e ? std::atoi(e) : 32;
 }
 
+// SOC_B200_PREFILL_ATTENTION=tc runs the flash step on the tcgen05 kernel (attn_prefill_tc.cu)
+// instead; it is not the default until it has matched the mma.sync kernel on a B200.
+bool prefill_attention_tc() {
+    const char* e = std::getenv("SOC_B200_PREFILL_ATTENTION");
+    return e && std::string(e) == "tc";
+}
+
 // pf_seq >= 0: the rows are positions pf_start .. pf_start + n - 1 of sequence pf_seq (a
 // prefill chunk), which lets the attention use the flash kernel.
 void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first, int lm_rows, int splits,
@@ -767,6 +774,7 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
                        "residual all-reduce");
     };
     const bool flash = pf_seq >= 0 && flash_min_rows() > 0 && n >= flash_min_rows();
+    const bool flash_tc = flash && prefill_attention_tc() && kv->tm_ok;
     for (size_t l = 0; l < c.layers; ++l) {
         const LayerW& w = m->layers[l];
         if (tc) {
@@ -779,7 +787,10 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
         launch_qk_norm_rope_kv(m->qkv, rows, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
                                w.q_norm, w.k_norm, eps, m->rope_cs, m->rope_len, kv->view(static_cast<int>(l)), m->q,
                                m->ctx->d_err, st);
-        if (flash)
+        if (flash && flash_tc)
+            launch_flash_prefill_tc(m->q, n, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
+                                    pf_seq, pf_start, kv->view(static_cast<int>(l)), m->att, m->ctx->d_err, st);
+        else if (flash)
             launch_flash_prefill(m->q, n, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(c.hd),
                                  pf_seq, pf_start, kv->view(static_cast<int>(l)), m->att, st);
         else

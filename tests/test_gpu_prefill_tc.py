@@ -1,0 +1,62 @@
+"""The tcgen05 prefill attention (attn_prefill_tc.cu, SOC_B200_PREFILL_ATTENTION=tc) against
+the mma.sync flash kernel it is meant to replace: same prompt, same cache, logits within the
+parity tolerance and identical greedy ids, in one chunk and in two.
+
+Skipped unless SOC_B200_EXPERIMENTAL=1: the kernel has not yet run on a GPU, so it stays out
+of the default GPU suite until this test has passed on a B200."""
+import os
+
+import numpy as np
+import pytest
+
+from soc_b200 import runtime as R
+from soc_b200.bundle import tiny_config
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(os.environ.get("SOC_B200_EXPERIMENTAL") != "1",
+                                 reason="tcgen05 prefill attention not yet validated on a GPU")]
+LOGIT_TOL = 2e-2
+
+CASES = {
+    "d64_gqa2": (tiny_config(), "float16"),
+    "d128_gqa4_bf16": (tiny_config(num_attention_heads=8, num_key_value_heads=2, head_dim=128), "bfloat16"),
+}
+
+
+def _prefill(ctx, path, prompt, chunks, tc):
+    old = os.environ.get("SOC_B200_PREFILL_ATTENTION")
+    if tc:
+        os.environ["SOC_B200_PREFILL_ATTENTION"] = "tc"
+    else:
+        os.environ.pop("SOC_B200_PREFILL_ATTENTION", None)
+    try:
+        m = R.Model(ctx, path)
+        kv = R.KVCache(m, 1, 1024)
+        at, logits, nid = 0, None, None
+        for n in chunks:
+            logits, nid = m.forward_logits_cached(kv, 0, prompt[at:at + n])
+            at += n
+        ctx.synchronize()
+        k = kv.read(0, 1, 0, at)[0]
+        kv.free()
+        m.free()
+        return logits, nid, k
+    finally:
+        if old is None:
+            os.environ.pop("SOC_B200_PREFILL_ATTENTION", None)
+        else:
+            os.environ["SOC_B200_PREFILL_ATTENTION"] = old
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+@pytest.mark.parametrize("chunks", [(40,), (200,), (150, 130), (33, 300)], ids=str)
+def test_tc_prefill_matches_mma_sync(gpu_ctx, make_bundle, case, chunks):
+    cfg, dt = CASES[case]
+    p = make_bundle("tc_" + case, cfg, seed=11, dtype=dt)
+    prompt = np.random.default_rng(7).integers(0, cfg["vocab_size"], sum(chunks)).astype(np.int32)
+    ref_logits, ref_id, ref_k = _prefill(gpu_ctx, p, prompt, chunks, tc=False)
+    logits, nid, k = _prefill(gpu_ctx, p, prompt, chunks, tc=True)
+    assert np.isfinite(logits).all()
+    assert np.abs(logits - ref_logits).max() < LOGIT_TOL
+    assert nid == ref_id
+    assert np.abs(k - ref_k).max() < 1e-2

@@ -25,6 +25,7 @@
 #include "decode_mk.h"
 #include "gemm_tc.h"
 #include "nccl_rt.h"
+#include "tp_allreduce.h"
 #include "json.hpp"
 #include "kernels.h"
 
@@ -528,6 +529,7 @@ struct soc_model {
     // lm_head with a merged argmax
     int tp_rank = 0, tp_size = 1;
     ncclComm_t comm = nullptr;
+    TpExchange* ar = nullptr;  // peer-memory all-reduce (opt-in), else NCCL
     int v_loc = 0, v_off = 0;                 // lm_head rows held here
     float* logits_all = nullptr;              // [tp][rows][v_loc] gathered logits
     int logits_all_rows = 0;
@@ -769,9 +771,12 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
     // stream, the other ranks store theirs, and the all-reduce sums them.
     const int res_mode = m->tp_rank == 0 ? LIN_RESIDUAL : LIN_STORE;
     auto tp_sum = [&] {
-        if (m->tp_size > 1)
-            nccl_check(nccl().all_reduce(m->h, m->h, static_cast<size_t>(n) * H, ncclFloat32, ncclSum, m->comm, st),
-                       "residual all-reduce");
+        if (m->tp_size <= 1) return;
+        const size_t elems = static_cast<size_t>(n) * H;
+        if (m->ar != nullptr && elems <= m->ar->max_elems && elems % 4 == 0)
+            m->ar->all_reduce(m->h, elems, m->ctx->d_err, st);
+        else
+            nccl_check(nccl().all_reduce(m->h, m->h, elems, ncclFloat32, ncclSum, m->comm, st), "residual all-reduce");
     };
     const bool flash = pf_seq >= 0 && flash_min_rows() > 0 && n >= flash_min_rows();
     const bool flash_tc = flash && prefill_attention_tc() && kv->tm_ok;
@@ -1317,8 +1322,18 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
             m->mk_ok = true;
         }
         SOCB_CUDA(cudaDeviceSynchronize());
+        // Peer-memory all-reduce for decode-sized steps (up to 64 rows), last because setting
+        // it up is a collective: every rank reaches here once the rest of its load succeeded.
+        if (tp_size > 1 && tp_p2p_requested()) {
+            m->ar = new TpExchange();
+            m->ar->setup(m->comm, tp_rank, tp_size, static_cast<size_t>(64) * c.hidden, ctx->stream);
+        }
     });
     if (rc != SOC_B200_OK) {
+        if (m->ar) {
+            m->ar->release();
+            delete m->ar;
+        }
         for (void* p : m->allocs)
             if (p) cudaFree(p);
         return rc;
@@ -1375,6 +1390,10 @@ void soc_b200_free_model(soc_model* m) {
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);
     if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
+    if (m->ar) {
+        m->ar->release();
+        delete m->ar;
+    }
     for (void* p : m->allocs)
         if (p) cudaFree(p);
     delete m;

@@ -31,10 +31,16 @@ def _gpus():
     return torch.cuda.device_count()
 
 
+@pytest.mark.parametrize("allreduce", ["nccl", "p2p"])
 @pytest.mark.parametrize("case", sorted(CASES))
-def test_tensor_parallel_two_ranks_match_oracle(make_bundle, tmp_path, case):
+def test_tensor_parallel_two_ranks_match_oracle(make_bundle, tmp_path, case, allreduce):
+    """allreduce "p2p": the residual sums of decode-sized steps go through the peer-memory
+    all-reduce (SOC_B200_TP_ALLREDUCE=p2p); it runs only with SOC_B200_EXPERIMENTAL=1 until it
+    has passed on GPUs."""
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
+    if allreduce == "p2p" and os.environ.get("SOC_B200_EXPERIMENTAL") != "1":
+        pytest.skip("peer-memory all-reduce not yet validated on GPUs")
     cfg, dt = CASES[case]
     p = make_bundle("tp_" + case, cfg, seed=5, dtype=dt)
     out = tmp_path / "tp.npz"
@@ -42,7 +48,12 @@ def test_tensor_parallel_two_ranks_match_oracle(make_bundle, tmp_path, case):
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr",
            "127.0.0.1", "--master-port", str(port), str(HERE / "tp_worker.py"), "--bundle", str(p), "--out", str(out),
            "--vocab", str(cfg["vocab_size"])]
-    r = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+    env = dict(os.environ)
+    if allreduce == "p2p":
+        env["SOC_B200_TP_ALLREDUCE"] = "p2p"
+    else:
+        env.pop("SOC_B200_TP_ALLREDUCE", None)
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = np.load(out)
     prompt = res["prompt"]

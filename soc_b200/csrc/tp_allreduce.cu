@@ -17,7 +17,7 @@
 // for e, i.e. after every rank finished all-reduce e - 1, the last reader of that buffer; so
 // two buffers suffice.  The CTAs of one launch wait on one another (step 2 -> 3), so the
 // kernel is launched cooperatively (all CTAs resident).  Waits give up after 2 s with
-// DERR_WAIT_TIMEOUT.  Plain peer loads and stores only: no multicast, no TMA on peer memory.
+// DERR_WAIT_TIMEOUT.  Plain peer loads and stores only, and no TMA on peer memory.
 //
 // Opt-in (SOC_B200_TP_ALLREDUCE=p2p at load time, on every rank); rows beyond the buffer's
 // capacity still go through NCCL.  Not yet run on a GPU.

@@ -164,6 +164,27 @@ def test_module_ops_bit_exact_vs_reference():
     assert np.array_equal(O.attention(q, k, v, 5), O.ref_attention(q, k, v, 5))
 
 
+@pytest.mark.skipif(not O.ref_available(), reason="reference build oracle/_ref absent")
+@pytest.mark.parametrize("theta", [1e4, 1e6])
+@pytest.mark.parametrize("offset", [0, 2047, 4095, 40959])
+def test_rope_bit_exact_at_long_positions(theta, offset):
+    """The positions the long-context benchmarks reach (4K contexts, the 40,960-row RoPE table):
+    the oracle's angles (double precision, as the reference) stay bit-exact there too."""
+    r = np.random.default_rng(offset).standard_normal((3, 2, 128), dtype=np.float32)
+    assert np.array_equal(O.rope(r, theta, offset), O.ref_rope(r, theta, offset))
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference build oracle/_ref absent")
+@pytest.mark.parametrize("keys,prefix", [(300, 290), (1030, 1000), (64, 0)])
+def test_attention_bit_exact_long_context(keys, prefix):
+    rng = np.random.default_rng(keys)
+    T = keys - prefix if prefix else 8
+    q = rng.standard_normal((T, 8, 128), dtype=np.float32)
+    k = rng.standard_normal((keys, 2, 128), dtype=np.float32)
+    v = rng.standard_normal((keys, 2, 128), dtype=np.float32)
+    assert np.array_equal(O.attention(q, k, v, prefix), O.ref_attention(q, k, v, prefix))
+
+
 # ---- 3. golden vectors produced by the reference -------------------------------
 def _golden_files():
     return sorted(GOLDEN.glob("tiny_*.npz"))

@@ -14,11 +14,65 @@
  * Weight element types: 0 = float32, 1 = float16, 2 = bfloat16.
  */
 #include <math.h>
+#include <pthread.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 enum { OR_F32 = 0, OR_F16 = 1, OR_BF16 = 2 };
+
+/* ---- a parallel for over independent outputs ------------------------------
+ * The linears and the attention split their outputs (rows x features, rows x heads)
+ * into contiguous ranges, one per host thread.  Every output keeps its own sequential
+ * accumulation, so the results do not depend on the thread count (ORACLE_THREADS, else
+ * the online CPUs, at most 64). */
+typedef void (*range_fn)(void* ctx, long lo, long hi);
+typedef struct {
+    range_fn fn;
+    void* ctx;
+    long lo, hi;
+} par_job;
+
+static void* par_run(void* a) {
+    par_job* j = (par_job*)a;
+    j->fn(j->ctx, j->lo, j->hi);
+    return NULL;
+}
+
+static int par_threads(void) {
+    const char* e = getenv("ORACLE_THREADS");
+    long n = e && *e ? atol(e) : sysconf(_SC_NPROCESSORS_ONLN);
+    if (n < 1) n = 1;
+    if (n > 64) n = 64;
+    return (int)n;
+}
+
+/* fn over [0, n) in one range per thread when the work (n * cost) is large enough. */
+static void par_for(long n, long cost, range_fn fn, void* ctx) {
+    int nt = par_threads();
+    if (n * cost < 4000000L || nt <= 1 || n < 2) {
+        fn(ctx, 0, n);
+        return;
+    }
+    if (nt > n) nt = (int)n;
+    pthread_t th[64];
+    par_job jobs[64];
+    int started = 0;
+    for (int i = 0; i < nt; ++i) {
+        jobs[i].fn = fn;
+        jobs[i].ctx = ctx;
+        jobs[i].lo = n * i / nt;
+        jobs[i].hi = n * (i + 1) / nt;
+    }
+    for (int i = 1; i < nt; ++i) {
+        if (pthread_create(&th[i], NULL, par_run, &jobs[i]) != 0) break;
+        started = i;
+    }
+    par_run(&jobs[0]);
+    for (int i = 1; i <= started; ++i) pthread_join(th[i], NULL);
+    for (int i = started + 1; i < nt; ++i) par_run(&jobs[i]); /* threads that could not start */
+}
 
 /* IEEE half -> float, exact (restates Float16ToFloat32, Mac/cpu/src/dtype.cpp:76-106). */
 float oracle_f16_to_f32(uint16_t h) {
@@ -62,18 +116,29 @@ static inline float rd(const void* p, int dt, size_t i) {
     }
 }
 
+typedef struct {
+    const float* x;
+    int in, wdt, out;
+    const void* w;
+    float* y;
+} lin_ctx;
+
+static void lin_range(void* c, long lo, long hi) {
+    const lin_ctx* a = (const lin_ctx*)c;
+    for (long j = lo; j < hi; ++j) {
+        const long r = j / a->out, o = j % a->out;
+        const float* xr = a->x + (size_t)r * a->in;
+        const size_t base = (size_t)o * a->in;
+        float v = 0.0f;
+        for (int i = 0; i < a->in; ++i) v += xr[i] * rd(a->w, a->wdt, base + i);
+        a->y[(size_t)r * a->out + o] = v;
+    }
+}
+
 /* y[r, o] = sum_i x[r, i] * W[o, i]   (Linear::Forward, Mac/cpu/src/linear.cpp:69-81; no bias in Qwen3). */
 void oracle_linear(const float* x, int rows, int in, const void* w, int wdt, int out, float* y) {
-    for (int r = 0; r < rows; ++r) {
-        const float* xr = x + (size_t)r * in;
-        float* yr = y + (size_t)r * out;
-        for (int o = 0; o < out; ++o) {
-            size_t base = (size_t)o * in;
-            float v = 0.0f;
-            for (int i = 0; i < in; ++i) v += xr[i] * rd(w, wdt, base + i);
-            yr[o] = v;
-        }
-    }
+    lin_ctx c = {x, in, wdt, out, w, y};
+    par_for((long)rows * out, in, lin_range, &c);
 }
 
 /* RMSNorm over the last dim (RMSNormModule::Forward, Mac/cpu/src/rms_norm_module.cpp:52-66). */
@@ -110,47 +175,59 @@ void oracle_rope(float* x, int T, int heads, int D, double theta, int pos0) {
     }
 }
 
+typedef struct {
+    const float *q, *k, *v;
+    float* out;
+    int Hq, S, Hkv, D, prefix;
+} att_ctx;
+
+static void att_range(void* c, long lo, long hi) {
+    const att_ctx* a = (const att_ctx*)c;
+    const int Hq = a->Hq, Hkv = a->Hkv, D = a->D, S = a->S;
+    const int group = Hq / Hkv;
+    const float scale = 1.0f / sqrtf((float)D);
+    float* scores = (float*)malloc(sizeof(float) * (size_t)(S > 0 ? S : 1));
+    float* wts = (float*)malloc(sizeof(float) * (size_t)(S > 0 ? S : 1));
+    for (long j = lo; j < hi; ++j) {
+        const int t = (int)(j / Hq), h = (int)(j % Hq);
+        int vis = a->prefix + t + 1;
+        if (vis > S) vis = S;
+        const int kh = h / group;
+        const float* qv = a->q + ((size_t)t * Hq + h) * D;
+        float mx = -INFINITY;
+        for (int p = 0; p < vis; ++p) {
+            const float* kv = a->k + ((size_t)p * Hkv + kh) * D;
+            float sc = 0.0f;
+            for (int d = 0; d < D; ++d) sc += qv[d] * kv[d];
+            sc *= scale;
+            scores[p] = sc;
+            if (sc > mx) mx = sc;
+        }
+        float sum = 0.0f;
+        for (int p = 0; p < vis; ++p) {
+            const float wv = expf(scores[p] - mx);
+            wts[p] = wv;
+            sum += wv;
+        }
+        float* o = a->out + ((size_t)t * Hq + h) * D;
+        for (int d = 0; d < D; ++d) o[d] = 0.0f;
+        for (int p = 0; p < vis; ++p) {
+            const float nw = wts[p] / sum;
+            const float* vv = a->v + ((size_t)p * Hkv + kh) * D;
+            for (int d = 0; d < D; ++d) o[d] += nw * vv[d];
+        }
+    }
+    free(scores);
+    free(wts);
+}
+
 /* Causal GQA with a cached prefix (GroupedQueryAttention::ForwardWithPrefix,
  * Mac/cpu/src/grouped_query_attention.cpp:59-142).
  * q [T, Hq, D]; k, v [S, Hkv, D]; out [T, Hq, D]. */
 void oracle_attention(const float* q, int T, int Hq, const float* k, const float* v, int S, int Hkv, int D,
                       int prefix, float* out) {
-    const int group = Hq / Hkv;
-    const float scale = 1.0f / sqrtf((float)D);
-    float* scores = (float*)malloc(sizeof(float) * (size_t)(S > 0 ? S : 1));
-    float* wts = (float*)malloc(sizeof(float) * (size_t)(S > 0 ? S : 1));
-    for (int t = 0; t < T; ++t) {
-        int vis = prefix + t + 1;
-        if (vis > S) vis = S;
-        for (int h = 0; h < Hq; ++h) {
-            const int kh = h / group;
-            const float* qv = q + ((size_t)t * Hq + h) * D;
-            float mx = -INFINITY;
-            for (int p = 0; p < vis; ++p) {
-                const float* kv = k + ((size_t)p * Hkv + kh) * D;
-                float sc = 0.0f;
-                for (int d = 0; d < D; ++d) sc += qv[d] * kv[d];
-                sc *= scale;
-                scores[p] = sc;
-                if (sc > mx) mx = sc;
-            }
-            float sum = 0.0f;
-            for (int p = 0; p < vis; ++p) {
-                const float wv = expf(scores[p] - mx);
-                wts[p] = wv;
-                sum += wv;
-            }
-            float* o = out + ((size_t)t * Hq + h) * D;
-            for (int d = 0; d < D; ++d) o[d] = 0.0f;
-            for (int p = 0; p < vis; ++p) {
-                const float nw = wts[p] / sum;
-                const float* vv = v + ((size_t)p * Hkv + kh) * D;
-                for (int d = 0; d < D; ++d) o[d] += nw * vv[d];
-            }
-        }
-    }
-    free(scores);
-    free(wts);
+    att_ctx c = {q, k, v, out, Hq, S, Hkv, D, prefix};
+    par_for((long)T * Hq, (long)(prefix + T) * D * 2, att_range, &c);
 }
 
 /* Greedy pick: first strict maximum (Sampler::SampleFromLogits with top_k = 1,

@@ -28,6 +28,7 @@ const NcclApi& nccl() {
         api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
         api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
         api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+        api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
         api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
         api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
         api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));

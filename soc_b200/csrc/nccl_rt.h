@@ -10,6 +10,7 @@ struct NcclApi {
     ncclResult_t (*get_unique_id)(ncclUniqueId*);
     ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
     ncclResult_t (*comm_destroy)(ncclComm_t);
+    ncclResult_t (*comm_abort)(ncclComm_t);
     ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
     ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
     const char* (*error_string)(ncclResult_t);

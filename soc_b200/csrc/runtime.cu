@@ -704,6 +704,8 @@ void check_device_error(soc_model* m) {
     SOCB_CUDA(cudaStreamSynchronize(m->ctx->stream));
     if (e != 0) {
         SOCB_CUDA(cudaMemsetAsync(m->ctx->d_err, 0, sizeof(int), m->ctx->stream));
+        // a bounded wait gave up: if the peer exchange ran, its epochs may now disagree
+        if ((e & DERR_WAIT_TIMEOUT) && m->ar != nullptr) m->ar->poisoned = true;
         if (e & DERR_TOKEN_RANGE) throw Error(SOC_B200_ERR_RANGE, "embedding input token id out of range");
         if (e & DERR_KV_RANGE) throw Error(SOC_B200_ERR_CAPACITY, "kv cache write position out of range");
         throw Error(SOC_B200_ERR_DEVICE, "device kernel reported error status " + std::to_string(e));
@@ -737,6 +739,8 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
     const int H = static_cast<int>(c.hidden), I = static_cast<int>(c.inter);
     const int QW = static_cast<int>(c.hq * c.hd), QKV = static_cast<int>(m->qkv_dim());
     Rows rows{m->d_tokens, m->d_seq, m->d_pos, n};
+    if (m->ar != nullptr && m->ar->poisoned)
+        throw Error(SOC_B200_ERR_DEVICE, "peer all-reduce: an earlier exchange timed out; reload the model");
     if (splits < 1) splits = attention_splits(n, static_cast<int>(c.hkv), max_visible);
     if (splits > 1) ensure_attn_scratch(m, static_cast<size_t>(n) * c.hq * splits * (c.hd + 2));
     launch_embed(m->efmt, m->embed, H, static_cast<int>(c.vocab), m->d_tokens, n, m->h, m->ctx->d_err, st);
@@ -1118,7 +1122,7 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
     if (tp_size > 1 && nccl_comm == nullptr)
         return fail(SOC_B200_ERR_INVALID, "soc_b200_load_bundle: tensor parallelism needs an NCCL communicator");
     auto m = std::make_unique<soc_model>();
-    const int rc = guarded([&] {
+    int rc = guarded([&] {
         SOCB_CUDA(cudaSetDevice(ctx->device));
         m->ctx = ctx;
         const Manifest man = load_manifest(manifest_path);
@@ -1322,13 +1326,25 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
             m->mk_ok = true;
         }
         SOCB_CUDA(cudaDeviceSynchronize());
-        // Peer-memory all-reduce for decode-sized steps (up to 64 rows), last because setting
-        // it up is a collective: every rank reaches here once the rest of its load succeeded.
-        if (tp_size > 1 && tp_p2p_requested()) {
-            m->ar = new TpExchange();
-            m->ar->setup(m->comm, tp_rank, tp_size, static_cast<size_t>(64) * c.hidden, ctx->stream);
-        }
     });
+    // Peer-memory all-reduce for decode-sized steps (up to 64 rows), last because setting it
+    // up is collective: every rank comes here whether or not its load succeeded, and the
+    // ranks agree on success before each collective step, so one rank's failed load makes
+    // every rank's load fail instead of leaving the others waiting in NCCL.
+    if (tp_size > 1 && tp_p2p_requested()) {
+        const bool load_ok = rc == SOC_B200_OK;
+        const std::string load_err = load_ok ? std::string() : std::string(soc_b200_last_error());
+        const int rc2 = guarded([&] {
+            SOCB_CUDA(cudaSetDevice(ctx->device));
+            m->ar = new TpExchange();
+            m->ar->setup(static_cast<ncclComm_t>(nccl_comm), tp_rank, tp_size,
+                         static_cast<size_t>(64) * m->cfg.hidden, load_ok, ctx->stream);
+        });
+        if (!load_ok)
+            fail(rc, load_err);  // the load's own error is the one to report
+        else
+            rc = rc2;
+    }
     if (rc != SOC_B200_OK) {
         if (m->ar) {
             m->ar->release();
@@ -1816,18 +1832,19 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         const int grid = mk_grid(m->ctx->device);
         if (!mk_supported(H, I, hq, hkv, D, m->wfmt, grid) || m->efmt != m->wfmt)
             throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: model shape not supported by the persistent decode kernel");
+        if (!m->mk_ok || m->d_mk_layers == nullptr)
+            throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: the model was loaded without the persistent decode kernel");
         kv->check_seq(seq);
         check_ids(m, &last_id, 1);
         const int pos = kv->lengths[seq];
         if (pos == 0) throw Error(SOC_B200_ERR_INVALID, "GenerationContext decode requires a prefilled KV cache");
         if (pos + 1 > m->rope_len) throw Error(SOC_B200_ERR_CAPACITY, "decode position beyond the RoPE table");
-        kv->reserve(seq, pos + 1, st);
 
         const int G = hq / hkv;
         int S = (pos + 1 + 127) / 128;
         S = std::max(1, std::min(S, grid / hkv));
         const int nb = mk_flag_count(static_cast<int>(c.layers), hkv, grid);
-        // carve the array (256-byte aligned pieces)
+        // carve the array (256-byte aligned pieces); every check comes before any side effect
         char* base = static_cast<char*>(noalloc_scratch(m->ctx->device));
         size_t off = 0;
         auto carve = [&](size_t bytes) {
@@ -1846,6 +1863,8 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
             throw Error(SOC_B200_ERR_CAPACITY, "decode_noalloc: this model needs " + std::to_string(off) +
                                                    " bytes of scratch, above the static maximum of " +
                                                    std::to_string(kNoAllocScratchBytes));
+        // the cache's host page allocator; no device memory is allocated (the page table exists)
+        kv->reserve(seq, pos + 1, st);
         SOCB_CUDA(cudaMemsetAsync(bars, 0, sizeof(unsigned) * nb, st));
         SOCB_CUDA(cudaMemsetAsync(best, 0, sizeof(unsigned long long) * grid, st));
         SOCB_CUDA(cudaMemcpyAsync(ids, &last_id, sizeof(int), cudaMemcpyHostToDevice, st));
@@ -1888,8 +1907,6 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         p.err = m->ctx->d_err;
         p.att_splits = S;
         p.trace = nullptr;
-        if (p.layers == nullptr)
-            throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: the model was loaded without the persistent decode kernel");
         mk_launch(p, grid, st);
         count_launches(1);
         if (logits) SOCB_CUDA(cudaMemcpyAsync(logits, lg, sizeof(float) * V, cudaMemcpyDeviceToHost, st));

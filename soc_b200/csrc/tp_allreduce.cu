@@ -19,10 +19,12 @@
 // kernel is launched cooperatively (all CTAs resident).  Waits give up after 2 s with
 // DERR_WAIT_TIMEOUT.  Plain peer loads and stores only, and no TMA on peer memory.
 //
-// Opt-in (SOC_B200_TP_ALLREDUCE=p2p at load time, on every rank); rows beyond the buffer's
-// capacity still go through NCCL.  Not yet run on a GPU.
+// Opt-in (SOC_B200_TP_ALLREDUCE=p2p with SOC_B200_EXPERIMENTAL=1 at load time, on every
+// rank); rows beyond the buffer's capacity still go through NCCL.
+#include <chrono>
 #include <cstdlib>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/soc_b200.h"
@@ -117,44 +119,108 @@ __global__ void __launch_bounds__(AR_THREADS) k_tp_allreduce(float* __restrict__
 
 bool tp_p2p_requested() {
     const char* e = std::getenv("SOC_B200_TP_ALLREDUCE");
-    return e && std::string(e) == "p2p";
+    const char* x = std::getenv("SOC_B200_EXPERIMENTAL");
+    return e && std::string(e) == "p2p" && x && std::string(x) == "1";
 }
 
-void TpExchange::setup(ncclComm_t comm, int rank_, int tp_, size_t max_elems_, cudaStream_t st) {
+namespace {
+// Device buffer freed on every exit path.
+struct DevBuf {
+    void* p = nullptr;
+    explicit DevBuf(size_t bytes) { SOCB_CUDA(cudaMalloc(&p, bytes)); }
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+};
+
+// Waits for `st` at most `seconds`; on expiry aborts `comm` (ending its pending kernels) and throws.
+void wait_bounded(cudaStream_t st, ncclComm_t comm, double seconds, const char* what) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t e = cudaStreamQuery(st);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotReady) SOCB_CUDA(e);
+        const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (waited > seconds) {
+            nccl().comm_abort(comm);
+            cudaStreamSynchronize(st);
+            throw Error(SOC_B200_ERR_DEVICE, std::string(what) + ": the other ranks did not join within " +
+                                                 std::to_string(static_cast<int>(seconds)) +
+                                                 " s; the NCCL communicator was aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+}
+}  // namespace
+
+bool tp_agree(ncclComm_t comm, bool ok, cudaStream_t st, double seconds) {
+    DevBuf d(sizeof(int));
+    const int v = ok ? 1 : 0;
+    SOCB_CUDA(cudaMemcpyAsync(d.p, &v, sizeof(int), cudaMemcpyHostToDevice, st));
+    nccl_check(nccl().all_reduce(d.p, d.p, 1, ncclInt32, ncclMin, comm, st), "rank agreement all-reduce");
+    wait_bounded(st, comm, seconds, "rank agreement");
+    int all = 0;
+    SOCB_CUDA(cudaMemcpy(&all, d.p, sizeof(int), cudaMemcpyDeviceToHost));
+    return all == 1;
+}
+
+void TpExchange::setup(ncclComm_t comm, int rank_, int tp_, size_t max_elems_, bool load_ok, cudaStream_t st) {
     rank = rank_;
     tp = tp_;
     max_elems = max_elems_;
     const size_t data = 2 * static_cast<size_t>(tp) * max_elems;
     const size_t flags = (2 * static_cast<size_t>(tp) + 2) * FLAG_WORDS;
     bytes = (data + flags) * sizeof(float);
-    SOCB_CUDA(cudaMalloc(&own, bytes));
-    SOCB_CUDA(cudaMemset(own, 0, bytes));
+    // 1. local: the exchange buffer and its IPC handle (only when the rest of the load succeeded)
     cudaIpcMemHandle_t mine{};
-    SOCB_CUDA(cudaIpcGetMemHandle(&mine, own));
-    // all-gather the 64-byte handles through NCCL (device buffers)
-    char* d_h = nullptr;
-    SOCB_CUDA(cudaMalloc(&d_h, sizeof(cudaIpcMemHandle_t) * (tp + 1)));
-    SOCB_CUDA(cudaMemcpy(d_h + sizeof(cudaIpcMemHandle_t) * tp, &mine, sizeof(mine), cudaMemcpyHostToDevice));
-    nccl_check(nccl().all_gather(d_h + sizeof(cudaIpcMemHandle_t) * tp, d_h, sizeof(cudaIpcMemHandle_t), ncclInt8,
-                                 comm, st),
-               "exchange-buffer handle all-gather");
-    std::vector<cudaIpcMemHandle_t> all(tp);
-    SOCB_CUDA(cudaStreamSynchronize(st));
-    SOCB_CUDA(cudaMemcpy(all.data(), d_h, sizeof(cudaIpcMemHandle_t) * tp, cudaMemcpyDeviceToHost));
-    cudaFree(d_h);
-    peers.assign(tp, nullptr);
-    for (int p = 0; p < tp; ++p) {
-        if (p == rank) {
-            peers[p] = own;
-            continue;
+    bool ok = load_ok;
+    if (ok) {
+        try {
+            SOCB_CUDA(cudaMalloc(&own, bytes));
+            SOCB_CUDA(cudaMemset(own, 0, bytes));
+            SOCB_CUDA(cudaIpcGetMemHandle(&mine, own));
+        } catch (const Error&) {
+            ok = false;
         }
-        void* ptr = nullptr;
-        SOCB_CUDA(cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess));
-        peers[p] = static_cast<float*>(ptr);
     }
-    SOCB_CUDA(cudaMalloc(&d_peers, sizeof(float*) * tp));
-    SOCB_CUDA(cudaMemcpy(d_peers, peers.data(), sizeof(float*) * tp, cudaMemcpyHostToDevice));
+    // 2. every rank agrees before the handle all-gather
+    if (!tp_agree(comm, ok, st)) throw Error(SOC_B200_ERR_DEVICE, "peer all-reduce set-up failed on a rank");
+    // 3. all-gather the 64-byte handles through NCCL (device buffers), bounded
+    std::vector<cudaIpcMemHandle_t> all(tp);
+    {
+        DevBuf d_h(sizeof(cudaIpcMemHandle_t) * (tp + 1));
+        char* hb = static_cast<char*>(d_h.p);
+        SOCB_CUDA(cudaMemcpy(hb + sizeof(cudaIpcMemHandle_t) * tp, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+        nccl_check(nccl().all_gather(hb + sizeof(cudaIpcMemHandle_t) * tp, hb, sizeof(cudaIpcMemHandle_t), ncclInt8,
+                                     comm, st),
+                   "exchange-buffer handle all-gather");
+        wait_bounded(st, comm, 60.0, "exchange-buffer handle all-gather");
+        SOCB_CUDA(cudaMemcpy(all.data(), hb, sizeof(cudaIpcMemHandle_t) * tp, cudaMemcpyDeviceToHost));
+    }
+    // 4. local: map the peers' buffers
+    peers.assign(tp, nullptr);
+    ok = true;
+    try {
+        for (int p = 0; p < tp; ++p) {
+            if (p == rank) {
+                peers[p] = own;
+                continue;
+            }
+            void* ptr = nullptr;
+            SOCB_CUDA(cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess));
+            peers[p] = static_cast<float*>(ptr);
+        }
+        SOCB_CUDA(cudaMalloc(&d_peers, sizeof(float*) * tp));
+        SOCB_CUDA(cudaMemcpy(d_peers, peers.data(), sizeof(float*) * tp, cudaMemcpyHostToDevice));
+    } catch (const Error&) {
+        ok = false;
+    }
+    // 5. every rank mapped every buffer, or none uses the exchange
+    if (!tp_agree(comm, ok, st)) throw Error(SOC_B200_ERR_DEVICE, "peer all-reduce set-up failed on a rank");
     epoch = 0;
+    poisoned = false;
 }
 
 void TpExchange::release() {
@@ -168,6 +234,8 @@ void TpExchange::release() {
 }
 
 void TpExchange::all_reduce(float* h, size_t elems, int* err, cudaStream_t st) {
+    if (poisoned)
+        throw Error(SOC_B200_ERR_DEVICE, "peer all-reduce: an earlier exchange timed out; reload the model");
     if (elems > max_elems || elems % 4 != 0) throw Error(SOC_B200_ERR_INVALID, "peer all-reduce: size outside the buffer");
     unsigned e = ++epoch;
     int n = static_cast<int>(elems);

@@ -114,3 +114,37 @@ def test_batched_decode_long_contexts_cycle_the_page_ring(gpu_ctx, make_bundle, 
             os.environ.pop("SOC_B200_ATTENTION", None)
         else:
             os.environ["SOC_B200_ATTENTION"] = old
+
+
+def test_batched_int8_decode_contexts_near_4096(gpu_ctx, make_bundle):
+    """The config-3 form at its longest contexts: int8 g64 linears, 6 sequences with contexts
+    in [3800, 4096) of seeded random KV, two batched decode steps; three sequences against the
+    oracle (logits within 2e-2, greedy ids identical)."""
+    cfg, quant, _ = CASES["qwen06_2layer_int8"]
+    p = make_bundle("batched_qwen06_2layer_int8", cfg, seed=43, dtype="float16", quant=quant)
+    m = R.Model(gpu_ctx, p)
+    L, hkv, hd = cfg["num_hidden_layers"], cfg["num_key_value_heads"], cfg["head_dim"]
+    n = 6
+    rng = np.random.default_rng(48)
+    ctx = rng.integers(3800, 4096, n)
+    kv = R.KVCache(m, n, int(ctx.sum()) + 32 * n)
+    for s in range(n):
+        kv.fill_random(s, int(ctx[s]), 3000 + s)
+    toks = rng.integers(0, cfg["vocab_size"], n).astype(np.int32)
+    oracles = []
+    for s in (0, 3, 5):
+        om = O.OracleModel(p, 4128)
+        for layer in range(L):
+            om.set_cache(layer, O.kv_random(3000 + s, s, layer, 0, int(ctx[s]), hkv, hd, L),
+                         O.kv_random(3000 + s, s, layer, 1, int(ctx[s]), hkv, hd, L))
+        om.set_length(int(ctx[s]))
+        oracles.append((s, om))
+    for step in range(2):
+        lg, nxt = m.decode(kv, list(range(n)), toks)
+        for s, om in oracles:
+            ref = om.forward([int(toks[s])], int(ctx[s]) + step, last_only=True)[0]
+            assert np.abs(lg[s] - ref).max() <= LOGIT_TOL, (s, step, np.abs(lg[s] - ref).max())
+            assert int(nxt[s]) == O.argmax(ref)
+        toks = nxt.astype(np.int32)
+    kv.free()
+    m.free()

@@ -89,11 +89,36 @@ def test_tc_prefill_logits_match_oracle(gpu_ctx, make_bundle, tc_rows, case):
         kv = R.KVCache(m, 1, 512)
         lg, nid = m.forward_logits_cached(kv, 0, prompt)
         out[mode] = lg
-        tol = LOGIT_TOL if dt == "float16" else 4 * LOGIT_TOL  # bf16 GEMM inputs: 8-bit significand
-        assert np.abs(lg - ref).max() <= tol, (mode, np.abs(lg - ref).max())
-        if dt == "float16":
-            assert nid == O.argmax(ref)
+        assert np.abs(lg - ref).max() <= LOGIT_TOL, (mode, np.abs(lg - ref).max())
+        assert nid == O.argmax(ref), mode
         kv.free()
+    m.free()
+
+
+def test_prefill_2048_then_greedy_matches_oracle(gpu_ctx, make_bundle):
+    """Config-2 length on a 2-layer Qwen3-0.6B-shape fp16 bundle: one 2048-token prefill
+    (tensor-core GEMMs above 512 rows, flash attention over the whole causal triangle) with
+    the default kernel choices, its last-row logits and greedy id against the oracle, then 8
+    greedy decode steps against a 2048-entry cache, each step's logits and id against the
+    oracle's."""
+    cfg, dt = CASES["qwen06_shape_2layer"]
+    p = make_bundle("tc_qwen06_shape_2layer", cfg, seed=9, dtype=dt)
+    prompt = np.random.default_rng(31).integers(0, cfg["vocab_size"], 2048).astype(np.int32)
+    om = O.OracleModel(p, 2080)
+    ref = om.forward(prompt, 0, last_only=True)[0]
+    m = R.Model(gpu_ctx, p)
+    kv = R.KVCache(m, 1, 2080)
+    lg, nid = m.forward_logits_cached(kv, 0, prompt)
+    assert np.abs(lg - ref).max() <= LOGIT_TOL, np.abs(lg - ref).max()
+    assert nid == O.argmax(ref)
+    tok = nid
+    for i in range(8):
+        ref = om.forward([tok], 2048 + i, last_only=True)[0]
+        lg, nxt = m.decode(kv, [0], [tok])
+        assert np.abs(lg[0] - ref).max() <= LOGIT_TOL, (i, np.abs(lg[0] - ref).max())
+        assert int(nxt[0]) == O.argmax(ref), i
+        tok = int(nxt[0])
+    kv.free()
     m.free()
 
 

@@ -57,6 +57,8 @@ def test_tensor_parallel_two_ranks_match_oracle(make_bundle, tmp_path, case, all
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = np.load(out)
     prompt = res["prompt"]
+    assert "not available for a tensor-parallel shard" in str(res["noalloc_refusal"])
+    assert int(res["length_after_refusal"]) == len(prompt)
     om = O.OracleModel(p, 256)
     ref = om.forward(prompt, 0, last_only=True)[0]
     assert np.abs(res["prefill_logits"] - ref).max() <= LOGIT_TOL

@@ -35,6 +35,13 @@ def main():
     kv = R.KVCache(m, 1, 128)
     lg, nid = m.forward_logits_cached(kv, 0, prompt)
     out["prefill_logits"], out["prefill_id"] = lg, nid
+    # the no-alloc decode step is single-GPU only: refused on a shard, with nothing changed
+    try:
+        m.decode_noalloc(kv, 0, nid)
+        out["noalloc_refusal"] = np.array("")
+    except R.SocError as e:
+        out["noalloc_refusal"] = np.array(str(e))
+    out["length_after_refusal"] = np.array(kv.length(0))
     toks, logits = [nid], []
     for _ in range(3):
         lg, nxt = m.decode(kv, [0], [toks[-1]])

@@ -577,15 +577,15 @@ struct soc_model {
     size_t top_k = 1;
     int mk_grid = 0;
     MKLayer* d_mk_layers = nullptr;
-    unsigned* mk_bars = nullptr;
-    int mk_bar_n = 0;
+    void* mk_lm_tiles = nullptr;              // the lm_head in the kernel's tiled layout
     unsigned long long* mk_best = nullptr;
     int mk_best_n = 0;
-    float* mk_att_part = nullptr;
-    size_t mk_att_part_floats = 0;
+    unsigned long long* mk_part = nullptr;    // split-K attention partials (tagged words)
+    size_t mk_part_n = 0;
     int* mk_ids = nullptr;
-    float* mk_vec = nullptr;  // h | qkv | attn | act shared between the kernel's CTAs
+    unsigned long long* mk_vec = nullptr;     // h | qkv | attn | act as tagged words
     size_t mk_vec_n = 0;
+    unsigned mk_tag = 0;                      // tags used so far on mk_vec / mk_part
 
     void* dmalloc(size_t bytes) {
         void* p = nullptr;
@@ -917,51 +917,25 @@ __global__ void k_step_end(soc_model::LoopState* st, const int* next) {
     st->step += 1;
 }
 
-// Persistent-kernel decode of `steps` tokens of one sequence (see decode_mk.cu).
-void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids, float* logits, int eos = -1) {
+// Parameters of one persistent-kernel launch (decode_mk.cu) over the buffers given.
+MKParams mk_params(const soc_model* m, const soc_kv* kv, int seq, int start, int steps, int* d_ids, float* logits,
+                   int eos, int splits, unsigned long long* vec, unsigned long long* part, unsigned long long* best,
+                   unsigned tag0) {
     const Config& c = m->cfg;
-    cudaStream_t st = m->ctx->stream;
-    if (start + steps > m->rope_len) throw Error(SOC_B200_ERR_CAPACITY, "decode position beyond the RoPE table");
-    ensure_workspace(m, 16);
-    const int G = static_cast<int>(c.hq / c.hkv);
-    const int hkv = static_cast<int>(c.hkv);
-    const int nb = mk_flag_count(static_cast<int>(c.layers), hkv, m->mk_grid);
-    if (nb > m->mk_bar_n) {
-        m->dfree(m->mk_bars);
-        m->mk_bars = static_cast<unsigned*>(m->dmalloc(sizeof(unsigned) * nb));
-        m->mk_bar_n = nb;
-    }
-    if (steps > m->mk_best_n) {
-        m->dfree(m->mk_best);
-        m->mk_best_n = std::max(steps, 64);
-        m->mk_best = static_cast<unsigned long long*>(
-            m->dmalloc(sizeof(unsigned long long) * m->mk_best_n * m->mk_grid));
-    }
-    // split-K over the key range: about 128 keys per CTA, at most one CTA per (kv head, split)
-    const int max_ctx = start + steps;
-    int S = (max_ctx + 127) / 128;
-    S = std::max(1, std::min(S, m->mk_grid / hkv));
-    const size_t part = static_cast<size_t>(hkv) * S * G * (c.hd + 2);
-    if (part > m->mk_att_part_floats) {
-        m->dfree(m->mk_att_part);
-        m->mk_att_part = static_cast<float*>(m->dmalloc(sizeof(float) * part));
-        m->mk_att_part_floats = part;
-    }
-    SOCB_CUDA(cudaMemsetAsync(m->mk_bars, 0, sizeof(unsigned) * nb, st));
-    SOCB_CUDA(cudaMemsetAsync(m->mk_best, 0, sizeof(unsigned long long) * steps * m->mk_grid, st));
     MKParams p{};
     p.L = static_cast<int>(c.layers);
     p.H = static_cast<int>(c.hidden);
     p.I = static_cast<int>(c.inter);
     p.hq = static_cast<int>(c.hq);
-    p.hkv = hkv;
+    p.hkv = static_cast<int>(c.hkv);
     p.D = static_cast<int>(c.hd);
     p.V = static_cast<int>(c.vocab);
     p.eps = static_cast<float>(c.eps);
     p.wfmt = m->wfmt;
+    p.efmt = m->efmt;
     p.layers = m->d_mk_layers;
     p.embed = m->embed;
-    p.lm_head = m->lm_head;
+    p.lm_tiles = m->mk_lm_tiles;
     p.final_norm = m->final_norm;
     p.rope_cs = m->rope_cs;
     p.rope_len = m->rope_len;
@@ -977,15 +951,65 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
     p.logits = logits;
     p.temperature = m->temperature;
     p.eos = eos;
-    p.h = m->mk_vec;
-    p.qkv = p.h + c.hidden;
-    p.attn = p.qkv + (c.hq + 2 * c.hkv) * c.hd;
-    p.act = p.attn + c.hq * c.hd;
-    p.att_part = m->mk_att_part;
-    p.flags = m->mk_bars;
-    p.best = m->mk_best;
+    p.vec = vec;
+    p.part = part;
+    p.tag0 = tag0;
+    p.best = best;
     p.err = m->ctx->d_err;
-    p.att_splits = S;
+    p.att_splits = splits;
+    // ring chunks in flight (SOC_B200_MK_INFLIGHT, default 2)
+    static const int inflight = [] {
+        const char* e = std::getenv("SOC_B200_MK_INFLIGHT");
+        const int v = e && *e ? std::atoi(e) : 2;
+        return std::max(1, std::min(v, 4));
+    }();
+    p.inflight = inflight;
+    p.trace = nullptr;
+    return p;
+}
+
+// Tag base for a launch of `steps` steps on tagged buffers whose last launch ended at *tag:
+// tags only grow, and before they would wrap the buffers are cleared and counting restarts
+// (a stale word must never carry a tag a reader waits for).
+unsigned mk_next_tags(unsigned* tag, int steps, int L, unsigned long long* vec, size_t vec_n,
+                      unsigned long long* part, size_t part_n, cudaStream_t st) {
+    const unsigned long long need = mk_tags_per_launch(steps, L);
+    if (static_cast<unsigned long long>(*tag) + need >= 0xF0000000ull) {
+        SOCB_CUDA(cudaMemsetAsync(vec, 0, vec_n * sizeof(unsigned long long), st));
+        if (part_n) SOCB_CUDA(cudaMemsetAsync(part, 0, part_n * sizeof(unsigned long long), st));
+        *tag = 0;
+    }
+    const unsigned base = *tag;
+    *tag = static_cast<unsigned>(base + need);
+    return base;
+}
+
+// Persistent-kernel decode of `steps` tokens of one sequence (see decode_mk.cu).
+void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids, float* logits, int eos = -1) {
+    const Config& c = m->cfg;
+    cudaStream_t st = m->ctx->stream;
+    if (start + steps > m->rope_len) throw Error(SOC_B200_ERR_CAPACITY, "decode position beyond the RoPE table");
+    ensure_workspace(m, 16);
+    const int hkv = static_cast<int>(c.hkv);
+    if (steps > m->mk_best_n) {
+        m->dfree(m->mk_best);
+        m->mk_best_n = std::max(steps, 64);
+        m->mk_best = static_cast<unsigned long long*>(
+            m->dmalloc(sizeof(unsigned long long) * m->mk_best_n * m->mk_grid));
+    }
+    const int S = mk_att_splits(start + steps, hkv, m->mk_grid);
+    const size_t part = S > 1 ? mk_part_words(static_cast<int>(c.hq), hkv, static_cast<int>(c.hd), S) : 0;
+    if (part > m->mk_part_n) {
+        // a new buffer starts zeroed: no stale tags
+        m->dfree(m->mk_part);
+        m->mk_part = static_cast<unsigned long long*>(m->dmalloc(sizeof(unsigned long long) * part));
+        SOCB_CUDA(cudaMemsetAsync(m->mk_part, 0, sizeof(unsigned long long) * part, st));
+        m->mk_part_n = part;
+    }
+    SOCB_CUDA(cudaMemsetAsync(m->mk_best, 0, sizeof(unsigned long long) * steps * m->mk_grid, st));
+    const unsigned tag0 = mk_next_tags(&m->mk_tag, steps, static_cast<int>(c.layers), m->mk_vec, m->mk_vec_n,
+                                       m->mk_part, m->mk_part_n, st);
+    MKParams p = mk_params(m, kv, seq, start, steps, d_ids, logits, eos, S, m->mk_vec, m->mk_part, m->mk_best, tag0);
     // Optional phase trace (SOC_B200_MK_TRACE=<file>): raw u64 %globaltimer stamps of the first step.
     const char* trace_path = std::getenv("SOC_B200_MK_TRACE");
     unsigned long long* trace = nullptr;
@@ -1308,20 +1332,32 @@ int soc_b200_load_bundle(soc_ctx* ctx, const char* manifest_path, int weight_for
         const char* path = std::getenv("SOC_B200_DECODE_PATH");
         const bool want_mk = !(path && std::string(path) == "graph");
         const int grid = mk_grid(ctx->device);
-        if (want_mk && tp_size == 1 && mk_supported(static_cast<int>(H), static_cast<int>(I), static_cast<int>(c.hq),
-                                    static_cast<int>(c.hkv), static_cast<int>(D), fmt, grid) &&
-            m->efmt == fmt) {
+        if (want_mk && tp_size == 1 &&
+            mk_supported(static_cast<int>(c.layers), static_cast<int>(H), static_cast<int>(I), static_cast<int>(c.hq), static_cast<int>(c.hkv),
+                         static_cast<int>(D), static_cast<int>(c.vocab), fmt, m->efmt, grid)) {
+            // the kernel's own copy of every matrix, in its tiled layout (the row-major copies
+            // stay for prefill and batched decode)
+            const int Hi = static_cast<int>(H), Ii = static_cast<int>(I), QKVr = static_cast<int>(QW + 2 * KW);
+            const int QWi = static_cast<int>(QW);
+            auto tiled = [&](const void* w, const void* sc, int rows, int K, int f) -> void* {
+                void* d = m->dmalloc(mk_tiled_bytes(f, rows, K));
+                mk_tile_matrix(f, w, sc, rows, K, d, ctx->stream);
+                return d;
+            };
             std::vector<MKLayer> ml(c.layers);
             for (size_t l = 0; l < c.layers; ++l) {
                 const LayerW& w = m->layers[l];
-                ml[l] = MKLayer{w.wqkv, w.wo, w.wgu, w.wd, w.in_norm, w.post_norm, w.q_norm, w.k_norm};
+                ml[l] = MKLayer{tiled(w.wqkv, w.sqkv, QKVr, Hi, fmt), tiled(w.wo, w.so, Hi, QWi, fmt),
+                                tiled(w.wgu, w.sgu, 2 * Ii, Hi, fmt),  tiled(w.wd, w.sd, Hi, Ii, fmt),
+                                w.in_norm, w.post_norm, w.q_norm, w.k_norm};
             }
+            m->mk_lm_tiles = tiled(m->lm_head, nullptr, static_cast<int>(c.vocab), Hi, m->efmt);
             m->d_mk_layers = static_cast<MKLayer*>(m->dmalloc(sizeof(MKLayer) * c.layers));
             SOCB_CUDA(cudaMemcpy(m->d_mk_layers, ml.data(), sizeof(MKLayer) * c.layers, cudaMemcpyHostToDevice));
             m->mk_ids = static_cast<int*>(m->dmalloc(sizeof(int) * 2));
-            m->mk_vec_n = mk_vec_floats(static_cast<int>(H), static_cast<int>(I), static_cast<int>(c.hq),
-                                        static_cast<int>(c.hkv), static_cast<int>(D));
-            m->mk_vec = static_cast<float*>(m->dmalloc(sizeof(float) * m->mk_vec_n));
+            m->mk_vec_n = mk_vec_words(Hi, Ii, static_cast<int>(c.hq), static_cast<int>(c.hkv), static_cast<int>(D));
+            m->mk_vec = static_cast<unsigned long long*>(m->dmalloc(sizeof(unsigned long long) * m->mk_vec_n));
+            SOCB_CUDA(cudaMemset(m->mk_vec, 0, sizeof(unsigned long long) * m->mk_vec_n));
             m->mk_grid = grid;
             m->mk_ok = true;
         }
@@ -1784,13 +1820,15 @@ int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* 
 // engine that hands every byte of the GPU to its own pool at start-up, or a
 // caller that must not make cudaMalloc's implicit device synchronisation on its
 // latency path.  This entry point runs one batch-1 decode step through the
-// persistent decode kernel with all of that kernel's scratch -- residual and
-// activation vectors, split-K attention partials, dependency counters, the
-// argmax slot and the logits row -- in one file-scope device array of fixed size.
+// persistent decode kernel with all of that kernel's scratch -- the residual and
+// activation vectors (tagged words), split-K attention partials, the argmax
+// slots and the logits row -- in one file-scope device array of fixed size.
 // Every GPU that loads this library keeps that array (kNoAllocScratchBytes)
 // until the process exits.  All calls share the array and it keeps the last
-// call's contents: the counters and the argmax slot are cleared at the start of
-// each call; calls whose GPU work overlaps (other streams, other threads) race.
+// call's contents: the argmax slots are cleared at the start of each call, and
+// the tags of the vectors keep growing from call to call, so no word left by an
+// earlier call is taken for this call's; calls whose GPU work overlaps (other
+// streams, other threads) race.
 // ---------------------------------------------------------------------------
 namespace {
 constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB
@@ -1798,6 +1836,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 constexpr int kMaxDevices = 128;
 void* g_noalloc_addr[kMaxDevices] = {};
+unsigned g_noalloc_tag[kMaxDevices] = {};
 std::mutex g_noalloc_mu;
 
 // Device address of the scratch array on `device` (which must be current).  The host-side
@@ -1815,6 +1854,14 @@ void* noalloc_scratch(int device) {
     }
     return g_noalloc_addr[device];
 }
+
+// Tag base of the next call on `device`'s array: the array starts out zeroed (a static
+// device array is), and it is cleared again before the tags would wrap.
+unsigned noalloc_tags(int device, int steps, int L, unsigned long long* vec, size_t vec_n, unsigned long long* part,
+                      size_t part_n, cudaStream_t st) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    return mk_next_tags(&g_noalloc_tag[device], steps, L, vec, vec_n, part, part_n, st);
+}
 }  // namespace
 
 extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_t last_id, float* logits,
@@ -1830,7 +1877,7 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         const int H = static_cast<int>(c.hidden), I = static_cast<int>(c.inter), hq = static_cast<int>(c.hq);
         const int hkv = static_cast<int>(c.hkv), D = static_cast<int>(c.hd), V = static_cast<int>(c.vocab);
         const int grid = mk_grid(m->ctx->device);
-        if (!mk_supported(H, I, hq, hkv, D, m->wfmt, grid) || m->efmt != m->wfmt)
+        if (!mk_supported(static_cast<int>(c.layers), H, I, hq, hkv, D, V, m->wfmt, m->efmt, grid))
             throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: model shape not supported by the persistent decode kernel");
         if (!m->mk_ok || m->d_mk_layers == nullptr)
             throw Error(SOC_B200_ERR_INVALID, "decode_noalloc: the model was loaded without the persistent decode kernel");
@@ -1840,10 +1887,7 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         if (pos == 0) throw Error(SOC_B200_ERR_INVALID, "GenerationContext decode requires a prefilled KV cache");
         if (pos + 1 > m->rope_len) throw Error(SOC_B200_ERR_CAPACITY, "decode position beyond the RoPE table");
 
-        const int G = hq / hkv;
-        int S = (pos + 1 + 127) / 128;
-        S = std::max(1, std::min(S, grid / hkv));
-        const int nb = mk_flag_count(static_cast<int>(c.layers), hkv, grid);
+        const int S = mk_att_splits(pos + 1, hkv, grid);
         // carve the array (256-byte aligned pieces); every check comes before any side effect
         char* base = static_cast<char*>(noalloc_scratch(m->ctx->device));
         size_t off = 0;
@@ -1852,12 +1896,12 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
             off += (bytes + 255) / 256 * 256;
             return static_cast<void*>(q);
         };
-        auto* bars = static_cast<unsigned*>(carve(sizeof(unsigned) * nb));
+        const size_t nvec = mk_vec_words(H, I, hq, hkv, D);
+        const size_t npart = mk_part_words(hq, hkv, D, S);
         auto* best = static_cast<unsigned long long*>(carve(sizeof(unsigned long long) * grid));
         auto* ids = static_cast<int*>(carve(sizeof(int) * 2));
-        const size_t nvec = mk_vec_floats(H, I, hq, hkv, D);
-        auto* vec = static_cast<float*>(carve(sizeof(float) * nvec));
-        auto* part = static_cast<float*>(carve(sizeof(float) * static_cast<size_t>(hkv) * S * G * (D + 2)));
+        auto* vec = static_cast<unsigned long long*>(carve(sizeof(unsigned long long) * nvec));
+        auto* part = static_cast<unsigned long long*>(carve(sizeof(unsigned long long) * npart));
         auto* lg = static_cast<float*>(carve(sizeof(float) * V));
         if (off > kNoAllocScratchBytes)
             throw Error(SOC_B200_ERR_CAPACITY, "decode_noalloc: this model needs " + std::to_string(off) +
@@ -1865,48 +1909,12 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
                                                    std::to_string(kNoAllocScratchBytes));
         // the cache's host page allocator; no device memory is allocated (the page table exists)
         kv->reserve(seq, pos + 1, st);
-        SOCB_CUDA(cudaMemsetAsync(bars, 0, sizeof(unsigned) * nb, st));
         SOCB_CUDA(cudaMemsetAsync(best, 0, sizeof(unsigned long long) * grid, st));
         SOCB_CUDA(cudaMemcpyAsync(ids, &last_id, sizeof(int), cudaMemcpyHostToDevice, st));
-
-        MKParams p{};
-        p.L = static_cast<int>(c.layers);
-        p.H = H;
-        p.I = I;
-        p.hq = hq;
-        p.hkv = hkv;
-        p.D = D;
-        p.V = V;
-        p.eps = static_cast<float>(c.eps);
-        p.wfmt = m->wfmt;
-        p.layers = m->d_mk_layers;
-        p.embed = m->embed;
-        p.lm_head = m->lm_head;
-        p.final_norm = m->final_norm;
-        p.rope_cs = m->rope_cs;
-        p.rope_len = m->rope_len;
-        p.kpool = kv->k;
-        p.vpool = kv->v;
-        p.kv_layer_stride = kv->layer_stride();
-        p.page_table = kv->d_page_table + static_cast<size_t>(seq) * kv->max_pages;
-        p.page_tokens = kv->page_tokens;
-        p.max_pages = kv->max_pages;
-        p.ids = ids;
-        p.start = pos;
-        p.steps = 1;
-        p.logits = lg;
-        p.temperature = m->temperature;
-        p.eos = -1;
-        p.h = vec;
-        p.qkv = vec + H;
-        p.attn = p.qkv + (hq + 2 * hkv) * D;
-        p.act = p.attn + hq * D;
-        p.att_part = part;
-        p.flags = bars;
-        p.best = best;
-        p.err = m->ctx->d_err;
-        p.att_splits = S;
-        p.trace = nullptr;
+        // tags keep growing across calls on this device's array (whatever model made them), so a
+        // word left by an earlier call never carries a tag this call waits for
+        const unsigned tag0 = noalloc_tags(m->ctx->device, 1, static_cast<int>(c.layers), vec, nvec, part, npart, st);
+        MKParams p = mk_params(m, kv, seq, pos, 1, ids, lg, -1, S, vec, part, best, tag0);
         mk_launch(p, grid, st);
         count_launches(1);
         if (logits) SOCB_CUDA(cudaMemcpyAsync(logits, lg, sizeof(float) * V, cudaMemcpyDeviceToHost, st));

@@ -18,7 +18,11 @@ ids).  Metric: decode tokens/s = generated ids per second of job time.
 
 N > 1: one process per GPU (torchrun), each running its own replica of the job
 ("replicas only": batch-1 decode of one sequence does not shard); value sums all
-ranks' ids over the max-over-ranks time.
+ranks' ids over the max-over-ranks time.  The same line carries, under
+"partitioned", the two paths that do split across the GPUs, measured in the same
+run: config 3 (256 sequences sharded over the ranks, no collective) and config 4
+(Qwen3-8B tensor-parallel over the ranks, NCCL all-reduce after o_proj and
+down_proj), each with its own workload, value and roofline.
 """
 from __future__ import annotations
 
@@ -267,7 +271,7 @@ def run_soc(args, rank, world, local):
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=torch.device("cuda", local))
 
     def barrier():
         if world > 1:
@@ -377,10 +381,28 @@ def run_soc(args, rank, world, local):
     kv.free()
     model.free()
     ctx.close()
+    if world > 1 and not args.no_partitioned:
+        # The headline `value` above is config 0 (one sequence per GPU: replicas only).  The paths
+        # that are partitioned across GPUs are measured in the same run and reported beside it:
+        # config 3 with its 256 sequences sharded over the ranks, and config 4 tensor-parallel
+        # over the ranks (when the ranks divide the Qwen3-8B heads).
+        part = {}
+        c3 = config3_measure(rank, world, local, PART_STEPS, 3, C3_SEQS)
+        if rank == 0:
+            part["config3_sequence_sharded"] = c3
+        if 32 % world == 0 and 8 % world == 0:
+            c4 = config4_measure(rank, world, local, PART_STEPS, 3)
+            if rank == 0:
+                part["config4_tensor_parallel"] = c4
+        if rank == 0:
+            result["partitioned"] = part
     if world > 1:
         dist.destroy_process_group()
     if result is not None:
         print(json.dumps(result), flush=True)
+
+
+PART_STEPS = 16  # timed steps of each partitioned measurement beside the N > 1 headline
 
 
 # ------------------------------------------------------------------- config 2
@@ -469,24 +491,34 @@ def config3_contexts() -> np.ndarray:
 
 
 def run_config3(args, rank, world, local):
+    """Config 3 on its own (--workload config3): see config3_measure."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    result = config3_measure(rank, world, local, args.steps, args.warmup, min(C3_SEQS, args.c3_seqs))
+    if world > 1:
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+def config3_measure(rank, world, local, steps, warmup, total):
     """Config 3: batched ragged decode, Qwen3-0.6B with int8 group-64 linears (the config-0
     fp16 weights quantised at load time; embeddings, norms and the tied lm_head stay fp16).
     256 sequences with contexts U[128, 4096] (seed 4) of seeded ~N(0, 1) fp16 KV written on
     the device (soc_b200_kv_fill_random, seed 4000 + sequence index), sequences placed on the
     ranks by soc_b200.sharding.balanced_shards (equal counts, balanced total context),
     `steps` greedy decode steps of every local sequence per timed run (one soc_b200_decode
-    call per step: host ids in, host ids out).  Prints one JSON line (rank 0) with the
-    max-over-ranks time."""
+    call per step: host ids in, host ids out).  Returns the JSON object (rank 0) with the
+    max-over-ranks time; with world > 1 the process group must already be initialised."""
     import torch
     import torch.distributed as dist
     from soc_b200 import runtime as R
     from soc_b200.bundle import QWEN3_0_6B
     from soc_b200.sharding import balanced_shards
-
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
     def barrier():
         if world > 1:
@@ -497,11 +529,10 @@ def run_config3(args, rank, world, local):
     ctx = R.Context(local)
     model = R.Model(ctx, p, weight_format=R.WEIGHTS_INT8_G64)
     ctxs = config3_contexts()
-    total = min(C3_SEQS, args.c3_seqs)  # a smaller case of the same kernels (profiling)
     # equal counts per rank and balanced total context (the KV read bounds each step)
     mine = balanced_shards(ctxs[:total], world)[rank]
     n = len(mine)
-    steps, warmup = args.steps, max(args.warmup, 3)
+    warmup = max(warmup, 3)
     cap = int(sum(-(-(int(ctxs[g]) + steps + warmup + 1) // 16) * 16 for g in mine))
     kv = R.KVCache(model, n, cap)
     for i, g in enumerate(mine):
@@ -562,10 +593,7 @@ def run_config3(args, rank, world, local):
     kv.free()
     model.free()
     ctx.close()
-    if world > 1:
-        dist.destroy_process_group()
-    if result is not None:
-        print(json.dumps(result), flush=True)
+    return result
 
 
 # ------------------------------------------------------------------- config 4
@@ -573,21 +601,32 @@ C4_BATCH, C4_CTX = 32, 2048
 
 
 def run_config4(args, rank, world, local):
+    """Config 4 on its own (--workload config4): see config4_measure."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    result = config4_measure(rank, world, local, args.steps, args.warmup)
+    if world > 1:
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+def config4_measure(rank, world, local, steps, warmup):
     """Config 4: Qwen3-8B architecture, random bf16 weights N(0, 0.02) seed 5 (drawn by
     torch.randn on the GPU: 8.2 G values), tensor
     parallel over the ranks (TP = --gpus: heads and FFN columns sharded, all-reduce of the
     residual stream after o_proj and down_proj, vocab-parallel lm_head).  Batch 32 decode at
     context 2048 of seeded ~N(0, 1) KV (soc_b200_kv_fill_random, seed 5000 + sequence), one
-    soc_b200_decode call per step.  Prints one JSON line (rank 0), max-over-ranks time."""
+    soc_b200_decode call per step.  Returns the JSON object (rank 0), max-over-ranks time; with
+    world > 1 the process group must already be initialised."""
     import torch
     import torch.distributed as dist
     from soc_b200 import runtime as R
     from soc_b200.bundle import QWEN3_8B, cached_bundle
-
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     def barrier():
         if world > 1:
@@ -602,7 +641,7 @@ def run_config4(args, rank, world, local):
     ctx = R.Context(local)
     comm = R.tensor_parallel_comm(ctx) if world > 1 else None
     model = R.Model(ctx, p, tp_rank=rank, tp_size=world, comm=comm)
-    steps, warmup = args.steps, max(args.warmup, 3)
+    warmup = max(warmup, 3)
     kv = R.KVCache(model, C4_BATCH, C4_BATCH * (C4_CTX + steps + warmup + 16))
     for s in range(C4_BATCH):
         kv.fill_random(s, C4_CTX, 5000 + s)
@@ -658,10 +697,7 @@ def run_config4(args, rank, world, local):
     model.free()
     R.Context.nccl_comm_destroy(comm)
     ctx.close()
-    if world > 1:
-        dist.destroy_process_group()
-    if result is not None:
-        print(json.dumps(result), flush=True)
+    return result
 
 
 # ------------------------------------------------------------- config 1 sweep
@@ -746,6 +782,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="soc", choices=["soc", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-partitioned", action="store_true",
+                    help="N > 1: skip the config-3 (sequence-sharded) and config-4 (tensor-parallel) measurements")
     ap.add_argument("--workload", default="config0", choices=["config0", "linear-sweep", "config2", "config3", "config4"],
                     help="config0 (the headline line), linear-sweep (config 1, one line per case), config2, "
                          "config3 (batched ragged decode, sequence-sharded over --gpus), "

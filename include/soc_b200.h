@@ -233,6 +233,17 @@ SOC_B200_API int soc_b200_nccl_comm_destroy(void* comm);
 SOC_B200_API int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* scales, int out_features,
                     int in_features, const float* x, int rows, float* y, void* stream);
 
+/* The sampler's candidate list for row `row` of the logits that the last
+ * soc_b200_prefill (row 0) or soc_b200_decode (row = index in the batch) call
+ * left on the device: the k (1..64) tokens with the largest logit / temperature,
+ * larger first, the lower id first among equal values; top_logits gets their raw
+ * logits, top_token_ids their ids (host arrays of k).  Replaces the top_logits /
+ * top_token_ids that Sampler::SampleFromLogits fills in GenerationStepResult
+ * (Mac/gpu/src/runtime/sampler.cpp:58-68, generation_context.h:17-21).  Not
+ * after generate or decode_noalloc (their steps keep no logits).  With tensor
+ * parallelism every rank makes the same call (the vocab shards are gathered). */
+SOC_B200_API int soc_b200_topk(soc_model* model, int row, int k, float* top_logits, int32_t* top_token_ids);
+
 /* One batch-1 decode step of sequence `seq` that allocates no device memory.
  * No counterpart in the reference.  For callers that cannot call cudaMalloc
  * while serving (an engine that gives the whole GPU to its own pool at

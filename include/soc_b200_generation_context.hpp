@@ -29,14 +29,18 @@ namespace soc::b200 {
 
 struct GenerationStepResult {
     int token_id = -1;
-    std::vector<float> logits;  // filled when requested
+    std::vector<float> top_logits;   // the sampler's top_k candidates, larger first (generation_context.h:17-21)
+    std::vector<int> top_token_ids;
+    std::vector<float> logits;       // the whole row, filled when requested
 };
 
 class GenerationContext {
 public:
     // `model` and `kv` stay owned by the caller; `seq` is this context's slot in `kv`.
-    GenerationContext(soc_model* model, soc_kv* kv, int seq, std::size_t max_sequence_length)
-        : model_(model), kv_(kv), seq_(seq), max_sequence_length_(max_sequence_length) {
+    // `top_k`: candidates per step in GenerationStepResult (the Sampler's top_k, 1..64).
+    GenerationContext(soc_model* model, soc_kv* kv, int seq, std::size_t max_sequence_length, std::size_t top_k = 1)
+        : model_(model), kv_(kv), seq_(seq), max_sequence_length_(max_sequence_length),
+          top_k_(top_k < 1 ? 1 : (top_k > 64 ? 64 : top_k)) {
         soc_b200_model_info(model_, &info_);
     }
 
@@ -80,6 +84,11 @@ public:
             SOC_B200_OK)
             return Fail(soc_b200_last_error(), error_message);
         result->token_id = next;
+        result->top_logits.resize(top_k_);
+        std::vector<int32_t> ids(top_k_);
+        if (soc_b200_topk(model_, 0, static_cast<int>(top_k_), result->top_logits.data(), ids.data()) != SOC_B200_OK)
+            return Fail(soc_b200_last_error(), error_message);
+        result->top_token_ids.assign(ids.begin(), ids.end());
         running_token_ids_.push_back(next);
         return true;
     }
@@ -133,6 +142,7 @@ private:
     soc_kv* kv_;
     int seq_;
     std::size_t max_sequence_length_;
+    std::size_t top_k_ = 1;
     soc_model_info info_{};
     std::vector<int> prompt_token_ids_;
     std::vector<int> running_token_ids_;

@@ -637,21 +637,6 @@ __device__ __forceinline__ AFrag afrag_of(const Smem& sm, int base, int lane) {
     return f;
 }
 
-// The same fragments held in registers for the whole phase (narrow slices): the MMA loop then
-// loads only the weights, so nothing in it waits on a fragment load.
-template <int KT>
-struct AReg {
-    uint32_t r[KT][2];
-    __device__ __forceinline__ void load(const AFrag& f) {
-#pragma unroll
-        for (int kt = 0; kt < KT; ++kt) f.at(kt, r[kt][0], r[kt][1]);
-    }
-    __device__ __forceinline__ void at(int kt, uint32_t& a0, uint32_t& a2) const {
-        a0 = r[kt][0];
-        a2 = r[kt][1];
-    }
-};
-
 // Sum of the parts' rows (lanes 0..3 end up with rows 2q, 2q + 1 of the tile).
 template <typename TX>
 __device__ __forceinline__ void combine_parts(float& d0, float& d1) {
@@ -793,9 +778,6 @@ __device__ __forceinline__ bool matrix_phase(const MKParams& p, Smem& sm, const 
     const int e = load_slice<TX, TE, KS>(p, sm, in, sc, base, lane, ss);
     MK_TR(l, tr + 1);
     const AFrag afs = afrag_of<TX>(sm, base, lane);
-    constexpr bool IN_REGS = KT <= 8;
-    AReg<IN_REGS ? KT : 1> afr;
-    if constexpr (IN_REGS) afr.load(afs);
     const float unscale = pow2i(-e);
     const int kt0 = cw * KT;
     for (int u = a; u < b; ++k) {
@@ -808,12 +790,8 @@ __device__ __forceinline__ bool matrix_phase(const MKParams& p, Smem& sm, const 
             for (int i0 = 0; i0 < n; i0 += NT) {
                 const int nt = min(NT, n - i0);
                 float d0[NT], d1[NT];
-                if constexpr (IN_REGS)
-                    tiles_slice<TX, F, KT, NT>(sm.ring[slot] + static_cast<size_t>(i0) * mt.tb, mt.tb, nt, kt0, lane,
-                                               afr, d0, d1);
-                else
-                    tiles_slice<TX, F, KT, NT>(sm.ring[slot] + static_cast<size_t>(i0) * mt.tb, mt.tb, nt, kt0, lane,
-                                               afs, d0, d1);
+                tiles_slice<TX, F, KT, NT>(sm.ring[slot] + static_cast<size_t>(i0) * mt.tb, mt.tb, nt, kt0, lane, afs,
+                                           d0, d1);
 #pragma unroll
                 for (int i = 0; i < NT; ++i) {
                     if (i < nt) {

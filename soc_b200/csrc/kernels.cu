@@ -913,3 +913,90 @@ void launch_argmax_merge(const unsigned long long* keys_all, int shards, int row
 }
 
 }  // namespace socb
+
+namespace socb {
+
+// ---------------------------------------------------------------- top-k candidates
+// The sampler's candidate list (Sampler::SampleFromLogits, Mac/gpu/src/runtime/sampler.cpp:36-68):
+// the k largest logit / temperature of a row, larger first; among equal values the lower token
+// id first (the order the device argmax already uses).  Two launches: every CTA sorts a chunk of
+// the row as orderable keys (argmax_key) and keeps its first k; one CTA sorts those candidates
+// and writes the first k ids with their raw logits.  Element g of the row lives at
+//   base + (g / seg_len) * seg_stride + g % seg_len
+// (one segment per tensor-parallel vocab shard after the all-gather; one segment otherwise).
+namespace {
+constexpr int TOPK_CHUNK = 4096;
+
+__device__ __forceinline__ float topk_elem(const float* base, int g, int seg_len, size_t seg_stride) {
+    return base[static_cast<size_t>(g / seg_len) * seg_stride + g % seg_len];
+}
+
+// Descending bitonic sort of n (a power of two) keys in shared memory by the whole CTA.
+__device__ void bitonic_desc(unsigned long long* s, int n) {
+    for (int size = 2; size <= n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool desc = (i & size) == 0;
+                    const unsigned long long a = s[i], b = s[j];
+                    if (desc ? (a < b) : (a > b)) {
+                        s[i] = b;
+                        s[j] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__global__ void k_topk_chunks(const float* __restrict__ base, int V, int seg_len, size_t seg_stride, float temp,
+                              int k, unsigned long long* __restrict__ cand) {
+    __shared__ unsigned long long s[TOPK_CHUNK];
+    const int first = blockIdx.x * TOPK_CHUNK;
+    for (int i = threadIdx.x; i < TOPK_CHUNK; i += blockDim.x) {
+        const int g = first + i;
+        unsigned long long key = 0ull;  // below every real key
+        if (g < V) {
+            const float raw = topk_elem(base, g, seg_len, seg_stride);
+            const float v = temp == 1.0f ? raw : __fdiv_rn(raw, temp);
+            if (v == v) key = argmax_key(v, g);
+        }
+        s[i] = key;
+    }
+    __syncthreads();
+    bitonic_desc(s, TOPK_CHUNK);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) cand[static_cast<size_t>(blockIdx.x) * k + i] = s[i];
+}
+
+__global__ void k_topk_merge(const unsigned long long* __restrict__ cand, int n, int k, const float* __restrict__ base,
+                             int seg_len, size_t seg_stride, float* __restrict__ top_logits, int* __restrict__ top_ids) {
+    __shared__ unsigned long long s[TOPK_CHUNK];
+    int np = 1;
+    while (np < n) np <<= 1;
+    for (int i = threadIdx.x; i < np; i += blockDim.x) s[i] = i < n ? cand[i] : 0ull;
+    __syncthreads();
+    bitonic_desc(s, np);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        const unsigned long long key = s[i];
+        const int id = key == 0ull ? -1 : argmax_key_index(key);
+        top_ids[i] = id;
+        top_logits[i] = id < 0 ? -INFINITY : topk_elem(base, id, seg_len, seg_stride);
+    }
+}
+}  // namespace
+
+int topk_scratch_keys(int V, int k) { return ((V + TOPK_CHUNK - 1) / TOPK_CHUNK) * k; }
+
+void launch_topk(const float* base, int V, int seg_len, size_t seg_stride, float temperature, int k,
+                 unsigned long long* cand, float* top_logits, int* top_ids, cudaStream_t st) {
+    const int chunks = (V + TOPK_CHUNK - 1) / TOPK_CHUNK;
+    if (k < 1 || k > TOPK_MAX || chunks * k > TOPK_CHUNK) throw Error(-2, "top-k: k out of range for this vocab");
+    k_topk_chunks<<<chunks, 512, 0, st>>>(base, V, seg_len, seg_stride, temperature, k, cand);
+    k_topk_merge<<<1, 512, 0, st>>>(cand, chunks * k, k, base, seg_len, seg_stride, top_logits, top_ids);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(2);
+}
+
+}  // namespace socb

@@ -79,6 +79,12 @@ void launch_argmax(const float* logits, int vocab, int ld, int rows, float tempe
 void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_off, float temperature, unsigned long long* keys,
                         cudaStream_t st);
 void launch_argmax_merge(const unsigned long long* keys_all, int shards, int rows, int* next_ids, cudaStream_t st);
+// Top-k candidates of one logits row (k <= TOPK_MAX); element g at base + (g / seg_len) * seg_stride
+// + g % seg_len.  `cand` holds topk_scratch_keys(V, k) keys; outputs are device arrays of k.
+constexpr int TOPK_MAX = 64;
+int topk_scratch_keys(int V, int k);
+void launch_topk(const float* base, int V, int seg_len, size_t seg_stride, float temperature, int k,
+                 unsigned long long* cand, float* top_logits, int* top_ids, cudaStream_t st);
 
 void launch_rmsnorm(const float* x, int rows, int n, const float* w, float eps, float* y, cudaStream_t st);
 

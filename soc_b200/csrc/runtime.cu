@@ -557,6 +557,10 @@ struct soc_model {
     CUtensorMap tm_dq_qkv{}, tm_dq_o{}, tm_dq_gu{}, tm_dq_d{};  // descriptors over wdq, one per shape
     float* logits = nullptr;
     int logits_rows = 0;
+    int logits_last_rows = 0;  // rows of m->logits the last prefill / decode left (0: none)
+    unsigned long long* topk_cand = nullptr;  // top-k scratch: candidates, then k logits and k ids
+    float* topk_vals = nullptr;
+    int* topk_ids = nullptr;
     float* attn_scratch = nullptr;
     size_t attn_scratch_floats = 0;
     // device-fed decode loop (CUDA graph of one step, replayed per token)
@@ -566,6 +570,20 @@ struct soc_model {
     };
     LoopState* d_loop = nullptr;
     cudaGraphExec_t step_graph = nullptr;
+    // short prefill chunks replayed as one CUDA graph (the launches, not the bytes, bound them)
+    struct PrefillKey {
+        const void *kv, *h, *xa, *logits;
+        int seq, start, n, lm;
+        float temperature;
+        bool operator==(const PrefillKey& o) const {
+            return kv == o.kv && h == o.h && xa == o.xa && logits == o.logits && seq == o.seq && start == o.start &&
+                   n == o.n && lm == o.lm && temperature == o.temperature;
+        }
+    };
+    cudaGraphExec_t pf_graph = nullptr;
+    PrefillKey pf_key{};
+    long long pf_graph_kernels = 0;
+    bool pf_graph_broken = false;  // a capture failed once: prefill chunks run directly
     const soc_kv* graph_kv = nullptr;
     int graph_splits = 0;
     long long graph_kernels = 0;
@@ -861,24 +879,70 @@ void check_ids(const soc_model* m, const int32_t* ids, int n) {
 
 // Copies the logits of `rows` rows (full vocab) to host memory.  With tensor parallelism
 // the vocab shards are all-gathered first, so every rank must make the same call.
-void logits_to_host(soc_model* m, int rows, float* host, cudaStream_t st) {
+// All-gathers the vocab shards of `rows` logits rows into m->logits_all ([tp][rows][v_loc]).
+void gather_logits(soc_model* m, int rows, cudaStream_t st) {
     const size_t V = m->cfg.vocab, vl = static_cast<size_t>(m->v_loc);
-    if (m->tp_size == 1) {
-        SOCB_CUDA(cudaMemcpyAsync(host, m->logits, sizeof(float) * V * rows, cudaMemcpyDeviceToHost, st));
-        return;
-    }
     if (rows > m->logits_all_rows) {
         m->dfree(m->logits_all);
         m->logits_all = static_cast<float*>(m->dmalloc(sizeof(float) * rows * V));
         m->logits_all_rows = rows;
     }
     nccl_check(nccl().all_gather(m->logits, m->logits_all, vl * rows, ncclFloat32, m->comm, st), "logits all-gather");
+}
+
+void logits_to_host(soc_model* m, int rows, float* host, cudaStream_t st) {
+    const size_t V = m->cfg.vocab, vl = static_cast<size_t>(m->v_loc);
+    if (m->tp_size == 1) {
+        SOCB_CUDA(cudaMemcpyAsync(host, m->logits, sizeof(float) * V * rows, cudaMemcpyDeviceToHost, st));
+        return;
+    }
+    gather_logits(m, rows, st);
     for (int r = 0; r < m->tp_size; ++r)
         SOCB_CUDA(cudaMemcpy2DAsync(host + r * vl, V * sizeof(float), m->logits_all + r * vl * rows, vl * sizeof(float),
                                     vl * sizeof(float), rows, cudaMemcpyDeviceToHost, st));
 }
 
 constexpr int kPrefillChunk = 4096;
+constexpr int kPrefillGraphRows = 64;  // prefill chunks up to this many rows run as a cached graph
+
+// One prefill chunk (rows in m->d_tokens / d_seq / d_pos already) through a CUDA graph of its
+// whole forward, captured on first use and replayed while the chunk's shape, cache slot,
+// position and buffers stay the same (a generation job's prompt, over and over).  The values the
+// kernels take as arguments (flash attention's start, the last-row lm_head) are in the key.
+void prefill_graph(soc_model* m, soc_kv* kv, int seq, int start, int n, bool last) {
+    cudaStream_t st = m->ctx->stream;
+    // everything the forward allocates lazily is allocated before a capture
+    ensure_logits(m, 1);
+    if (m->tc_ok) m->ctx->ws();
+    const soc_model::PrefillKey key{kv, m->h, m->xa, m->logits, seq, start, n, last ? 1 : 0, m->temperature};
+    if (!m->pf_graph || !(m->pf_key == key)) {
+        if (m->pf_graph) cudaGraphExecDestroy(m->pf_graph);
+        m->pf_graph = nullptr;
+        cudaGraph_t g = nullptr;
+        const long long before = launches_so_far();
+        SOCB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        try {
+            forward_rows(m, kv, n, start + n, last ? n - 1 : 0, last ? 1 : 0, 1, seq, start);
+        } catch (...) {
+            cudaStreamEndCapture(st, &g);
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            count_launches(-(launches_so_far() - before));
+            m->pf_graph_broken = true;
+            forward_rows(m, kv, n, start + n, last ? n - 1 : 0, last ? 1 : 0, 1, seq, start);
+            return;
+        }
+        m->pf_graph_kernels = launches_so_far() - before;
+        count_launches(-(launches_so_far() - before));
+        SOCB_CUDA(cudaStreamEndCapture(st, &g));
+        const cudaError_t e = cudaGraphInstantiate(&m->pf_graph, g, 0);
+        cudaGraphDestroy(g);
+        SOCB_CUDA(e);
+        m->pf_key = key;
+    }
+    SOCB_CUDA(cudaGraphLaunch(m->pf_graph, st));
+    count_launches(m->pf_graph_kernels);
+}
 
 // Prefill `n` host ids at the end of `seq`; leaves the last row's logits/next id on the device.
 void prefill_impl(soc_model* m, soc_kv* kv, int seq, const int32_t* ids, int n, bool ids_on_device) {
@@ -899,7 +963,10 @@ void prefill_impl(soc_model* m, soc_kv* kv, int seq, const int32_t* ids, int n, 
         SOCB_CUDA(cudaMemcpyAsync(m->d_pos, ps.data(), sizeof(int) * cn, cudaMemcpyHostToDevice, st));
         const bool last = off + cn == n;
         // (the pageable host vectors are staged by the driver before cudaMemcpyAsync returns)
-        forward_rows(m, kv, cn, start + off + cn, last ? cn - 1 : 0, last ? 1 : 0, 1, seq, start + off);
+        if (m->tp_size == 1 && cn <= kPrefillGraphRows && !m->pf_graph_broken)
+            prefill_graph(m, kv, seq, start + off, cn, last);
+        else
+            forward_rows(m, kv, cn, start + off + cn, last ? cn - 1 : 0, last ? 1 : 0, 1, seq, start + off);
     }
     kv->lengths[seq] = start + n;
 }
@@ -1431,6 +1498,8 @@ int soc_b200_set_sampler(soc_model* m, float temperature, size_t top_k) {
             if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
             m->step_graph = nullptr;
             m->graph_kv = nullptr;
+            if (m->pf_graph) cudaGraphExecDestroy(m->pf_graph);
+            m->pf_graph = nullptr;
         }
         m->temperature = temperature;
         m->top_k = top_k;
@@ -1442,6 +1511,7 @@ void soc_b200_free_model(soc_model* m) {
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);
     if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
+    if (m->pf_graph) cudaGraphExecDestroy(m->pf_graph);
     if (m->ar) {
         m->ar->release();
         delete m->ar;
@@ -1612,6 +1682,7 @@ int soc_b200_prefill(soc_model* m, soc_kv* kv, int seq, const int32_t* ids, int 
     return guarded([&] {
         SOCB_CUDA(cudaSetDevice(m->ctx->device));
         prefill_impl(m, kv, seq, ids, n, false);
+        m->logits_last_rows = 1;
         cudaStream_t st = m->ctx->stream;
         if (logits_last) logits_to_host(m, 1, logits_last, st);
         int nid = 0;
@@ -1647,6 +1718,7 @@ int soc_b200_decode(soc_model* m, soc_kv* kv, int n_seqs, const int* seq_ids, co
             ensure_logits(m, 1);
             SOCB_CUDA(cudaMemcpyAsync(m->mk_ids, last_ids, sizeof(int), cudaMemcpyHostToDevice, st));
             run_mk(m, kv, seq_ids[0], pos[0], 1, m->mk_ids, m->logits);
+            m->logits_last_rows = 1;
             if (logits)
                 SOCB_CUDA(cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->cfg.vocab, cudaMemcpyDeviceToHost, st));
             if (next_ids) SOCB_CUDA(cudaMemcpyAsync(next_ids, m->mk_ids + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -1659,6 +1731,7 @@ int soc_b200_decode(soc_model* m, soc_kv* kv, int n_seqs, const int* seq_ids, co
         SOCB_CUDA(cudaMemcpyAsync(m->d_seq, seq_ids, sizeof(int) * n_seqs, cudaMemcpyHostToDevice, st));
         SOCB_CUDA(cudaMemcpyAsync(m->d_pos, pos.data(), sizeof(int) * n_seqs, cudaMemcpyHostToDevice, st));
         forward_rows(m, kv, n_seqs, max_vis, 0, n_seqs, 0);
+        m->logits_last_rows = n_seqs;
         if (logits) logits_to_host(m, n_seqs, logits, st);
         if (next_ids) SOCB_CUDA(cudaMemcpyAsync(next_ids, m->d_next, sizeof(int) * n_seqs, cudaMemcpyDeviceToHost, st));
         check_device_error(m);
@@ -1671,6 +1744,7 @@ int soc_b200_decode(soc_model* m, soc_kv* kv, int n_seqs, const int* seq_ids, co
 static void generate_dev(soc_model* m, soc_kv* kv, int seq, const int32_t* prompt, int n_prompt, int max_new,
                          int32_t* d_out, bool prompt_on_device, int eos = -1) {
     kv->check_seq(seq);
+    m->logits_last_rows = 0;  // the device loop does not keep the steps' logits
     if (max_new <= 0) throw Error(SOC_B200_ERR_INVALID, "generate requires max_new >= 1");
     kv->reset(seq);
     cudaStream_t st = m->ctx->stream;
@@ -1811,6 +1885,43 @@ int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* 
     });
 }
 
+int soc_b200_topk(soc_model* m, int row, int k, float* top_logits, int32_t* top_token_ids) {
+    if (!m || !top_logits || !top_token_ids) return fail(SOC_B200_ERR_INVALID, "null argument");
+    if (k < 1 || k > TOPK_MAX) return fail(SOC_B200_ERR_INVALID, "top-k: k must be in [1, 64]");
+    return guarded([&] {
+        if (row < 0 || row >= m->logits_last_rows)
+            throw Error(SOC_B200_ERR_INVALID, "top-k: no logits row " + std::to_string(row) +
+                                                  " from the last prefill or decode call");
+        SOCB_CUDA(cudaSetDevice(m->ctx->device));
+        cudaStream_t st = m->ctx->stream;
+        const int V = static_cast<int>(m->cfg.vocab);
+        if (!m->topk_cand) {
+            m->topk_cand = static_cast<unsigned long long*>(
+                m->dmalloc(sizeof(unsigned long long) * static_cast<size_t>(topk_scratch_keys(V, TOPK_MAX))));
+            m->topk_vals = static_cast<float*>(m->dmalloc(sizeof(float) * TOPK_MAX));
+            m->topk_ids = static_cast<int*>(m->dmalloc(sizeof(int) * TOPK_MAX));
+        }
+        const float* base;
+        int seg_len;
+        size_t seg_stride;
+        if (m->tp_size == 1) {
+            base = m->logits + static_cast<size_t>(row) * m->v_loc;
+            seg_len = V;
+            seg_stride = 0;
+        } else {
+            // every rank makes this call: the shards of the rows are gathered, then each rank picks
+            gather_logits(m, m->logits_last_rows, st);
+            base = m->logits_all + static_cast<size_t>(row) * m->v_loc;
+            seg_len = m->v_loc;
+            seg_stride = static_cast<size_t>(m->logits_last_rows) * m->v_loc;
+        }
+        launch_topk(base, V, seg_len, seg_stride, m->temperature, k, m->topk_cand, m->topk_vals, m->topk_ids, st);
+        SOCB_CUDA(cudaMemcpyAsync(top_logits, m->topk_vals, sizeof(float) * k, cudaMemcpyDeviceToHost, st));
+        SOCB_CUDA(cudaMemcpyAsync(top_token_ids, m->topk_ids, sizeof(int) * k, cudaMemcpyDeviceToHost, st));
+        SOCB_CUDA(cudaStreamSynchronize(st));
+    });
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
@@ -1922,6 +2033,7 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         SOCB_CUDA(cudaMemcpyAsync(&nid, ids + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
         check_device_error(m);
         kv->lengths[seq] = pos + 1;
+        m->logits_last_rows = 0;  // this step's logits are in the static array, not the model's
         if (next_id) *next_id = nid;
     });
 }

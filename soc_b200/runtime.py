@@ -78,6 +78,7 @@ _SIGNATURES = {
     "soc_b200_generate_device": (C.c_int, [_VP, _VP, C.c_int, _VP, C.c_int, C.c_int, _VP]),
     "soc_b200_linear": (C.c_int, [_VP, C.c_int, _VP, _VP, C.c_int, C.c_int, _VP, C.c_int, _VP, _VP]),
     "soc_b200_decode_noalloc": (C.c_int, [_VP, _VP, C.c_int, C.c_int32, _FP, _I32P]),
+    "soc_b200_topk": (C.c_int, [_VP, C.c_int, C.c_int, _FP, _I32P]),
     "soc_b200_tokenizer_load": (C.c_int, [C.c_char_p, C.POINTER(_VP)]),
     "soc_b200_tokenizer_free": (None, [_VP]),
     "soc_b200_tokenizer_encode": (C.c_int, [_VP, C.c_char_p, C.c_size_t, _I32P, C.c_int, C.POINTER(C.c_int)]),
@@ -191,6 +192,7 @@ class Model:
                                           C.byref(h)))
         self.ctx = ctx
         self.h = h
+        self.top_k = 1  # the sampler's candidate count (set_sampler)
         info = ModelInfo()
         _check(lib().soc_b200_model_info(h, C.byref(info)))
         self.info = info
@@ -221,6 +223,7 @@ class Model:
     def set_sampler(self, temperature: float = 1.0, top_k: int = 1) -> None:
         """Sampler(SamplerConfig) for later picks: argmax of logit / temperature (``soc_b200_set_sampler``)."""
         _check(lib().soc_b200_set_sampler(self.h, float(temperature), int(top_k)))
+        self.top_k = int(top_k)
 
     def decode_noalloc(self, kv: "KVCache", seq: int, last_id: int, want_logits=True):
         """One decode step that allocates no device memory (``soc_b200_decode_noalloc``):
@@ -230,6 +233,14 @@ class Model:
         _check(lib().soc_b200_decode_noalloc(self.h, kv.h, seq, int(last_id),
                                              _fp(logits) if logits is not None else None, _ip(nid)))
         return logits, int(nid[0])
+
+    def topk(self, row: int, k: int) -> tuple[np.ndarray, np.ndarray]:
+        """The sampler's k candidates of logits row `row` of the last prefill / decode call
+        (``soc_b200_topk``): raw logits and token ids, larger logit / temperature first."""
+        vals = np.empty(k, dtype=np.float32)
+        ids = np.empty(k, dtype=np.int32)
+        _check(lib().soc_b200_topk(self.h, row, k, _fp(vals), _ip(ids)))
+        return vals, ids
 
     def generate(self, kv: "KVCache", seq: int, prompt, max_new: int, eos: int = -1) -> list[int]:
         prompt = _i32(prompt)
@@ -287,6 +298,8 @@ class KVCache:
 class GenerationStepResult:
     token_id: int
     logits: np.ndarray | None = None
+    top_logits: np.ndarray | None = None     # the sampler's top_k candidates (generation_context.h:17-21)
+    top_token_ids: np.ndarray | None = None
 
 
 class GenerationContext:
@@ -326,9 +339,10 @@ class GenerationContext:
             raise SocError(ERR_CAPACITY, "GenerationContext sequence length would exceed max_sequence_length")
         logits, nxt = self.model.decode(self.kv, [self.seq], [last_token_id])
         tok = int(nxt[0])
+        top_vals, top_ids = self.model.topk(0, min(max(self.model.top_k, 1), 64))
         self.running_token_ids.append(tok)
         self._last_logits = logits[0]
-        return GenerationStepResult(tok, logits[0])
+        return GenerationStepResult(tok, logits[0], top_vals, top_ids)
 
     def generate(self, prompt_token_ids, max_new_tokens: int, eos_token_id: int = -1) -> list[int]:
         """generation_context.cpp:118-172, with the decode loop resident on the device."""

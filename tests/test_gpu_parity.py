@@ -359,3 +359,68 @@ def test_linear_kernel_against_fp64(gpu_ctx, rows, shape):
     torch.cuda.synchronize()
     err = (y.double().cpu() - ref).abs().max().item()
     assert err <= 1e-4 * (in_f ** 0.5), err
+
+
+def _topk_ref(row, k, temperature=1.0):
+    """The sampler's candidates from a logits row: larger logit / temperature first, lower id
+    first among equal values (Mac/gpu/src/runtime/sampler.cpp:36-68 with that tie rule)."""
+    v = (row / np.float32(temperature)).astype(np.float32)
+    order = np.lexsort((np.arange(row.size), -v))
+    return order[:k]
+
+
+@pytest.mark.parametrize("path", ["mk", "graph"])
+def test_topk_candidates_match_the_logits_row(models, path):
+    """soc_b200_topk after a prefill and after decode steps: the k candidates are exactly the k
+    largest of the row the same call returned (ids and raw logits), the first one is the
+    greedy pick, and under a temperature the order is that of logit / temperature."""
+    p, m = models("qwen06_shape_2layer", path)
+    cfg = CASES["qwen06_shape_2layer"][0]
+    kv = R.KVCache(m, 1, 256)
+    prompt = _prompt(cfg, 9, 4)
+    lg, nid = m.forward_logits_cached(kv, 0, prompt)
+    vals, ids = m.topk(0, 16)
+    ref = _topk_ref(lg, 16)
+    assert np.array_equal(ids, ref)
+    assert np.array_equal(vals, lg[ref])
+    assert int(ids[0]) == nid
+    tok = nid
+    for k in (1, 8, 64):
+        lgd, nxt = m.decode(kv, [0], [tok])
+        vals, ids = m.topk(0, k)
+        ref = _topk_ref(lgd[0], k)
+        assert np.array_equal(ids, ref), k
+        assert np.array_equal(vals, lgd[0][ref])
+        assert int(ids[0]) == int(nxt[0])
+        tok = int(nxt[0])
+    m.set_sampler(0.7, 8)
+    try:
+        lgd, nxt = m.decode(kv, [0], [tok])
+        vals, ids = m.topk(0, 8)
+        assert np.array_equal(ids, _topk_ref(lgd[0], 8, 0.7))
+        assert int(ids[0]) == int(nxt[0])
+    finally:
+        m.set_sampler(1.0, 1)
+    with pytest.raises(R.SocError, match="k must be in"):
+        m.topk(0, 65)
+    with pytest.raises(R.SocError, match="no logits row 1"):
+        m.topk(1, 4)
+    kv.free()
+
+
+def test_generation_context_step_carries_top_candidates(models):
+    p, m = models("qwen06_shape_2layer", "mk")
+    cfg = CASES["qwen06_shape_2layer"][0]
+    m.set_sampler(1.0, 8)
+    try:
+        gc = R.GenerationContext(m, 64)
+        prompt = _prompt(cfg, 7, 5)
+        gc.prefill(prompt)
+        first = O.argmax(gc._last_logits)
+        gc.running_token_ids.append(first)
+        res = gc.decode_next_token(first)
+        assert res.top_token_ids.shape == (8,) and res.top_logits.shape == (8,)
+        assert int(res.top_token_ids[0]) == res.token_id
+        assert np.array_equal(res.top_token_ids, _topk_ref(res.logits, 8))
+    finally:
+        m.set_sampler(1.0, 1)

@@ -64,6 +64,10 @@ def test_tensor_parallel_two_ranks_match_oracle(make_bundle, tmp_path, case, all
     assert np.abs(res["prefill_logits"] - ref).max() <= LOGIT_TOL
     assert int(res["prefill_id"]) == O.argmax(ref)
     ids = res["decode_ids"]
+    row0 = res["decode_logits"][0]
+    order = np.lexsort((np.arange(row0.size), -row0))[:8]
+    assert np.array_equal(res["topk_ids"], order)
+    assert np.array_equal(res["topk_vals"], row0[order])
     for i in range(3):
         ref = om.forward([int(ids[i])], len(prompt) + i, last_only=True)[0]
         assert np.abs(res["decode_logits"][i] - ref).max() <= LOGIT_TOL

@@ -43,10 +43,12 @@ def main():
         out["noalloc_refusal"] = np.array(str(e))
     out["length_after_refusal"] = np.array(kv.length(0))
     toks, logits = [nid], []
-    for _ in range(3):
+    for i in range(3):
         lg, nxt = m.decode(kv, [0], [toks[-1]])
         logits.append(lg[0])
         toks.append(int(nxt[0]))
+        if i == 0:  # the sampler's candidates over the gathered vocab shards (every rank calls)
+            out["topk_vals"], out["topk_ids"] = m.topk(0, 8)
     out["decode_logits"], out["decode_ids"] = np.stack(logits), np.array(toks)
     out["generate"] = np.array(m.generate(kv, 0, prompt, 5))
     kv.free()

@@ -740,11 +740,11 @@ int flash_min_rows() {
     return e && *e ? std::atoi(e) : 32;
 }
 
-// SOC_B200_PREFILL_ATTENTION=tc runs the flash step on the tcgen05 kernel (attn_prefill_tc.cu)
-// instead; it is not the default until it has matched the mma.sync kernel on a B200.
+// The flash step of a prefill chunk runs on the tcgen05 kernel (attn_prefill_tc.cu: S and O in
+// tensor memory); SOC_B200_PREFILL_ATTENTION=mma selects the mma.sync kernel (attn_prefill.cu).
 bool prefill_attention_tc() {
     const char* e = std::getenv("SOC_B200_PREFILL_ATTENTION");
-    return e && std::string(e) == "tc";
+    return !(e && std::string(e) == "mma");
 }
 
 // pf_seq >= 0: the rows are positions pf_start .. pf_start + n - 1 of sequence pf_seq (a

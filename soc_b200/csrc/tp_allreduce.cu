@@ -19,8 +19,8 @@
 // kernel is launched cooperatively (all CTAs resident).  Waits give up after 2 s with
 // DERR_WAIT_TIMEOUT.  Plain peer loads and stores only, and no TMA on peer memory.
 //
-// Opt-in (SOC_B200_TP_ALLREDUCE=p2p with SOC_B200_EXPERIMENTAL=1 at load time, on every
-// rank); rows beyond the buffer's capacity still go through NCCL.
+// Opt-in (SOC_B200_TP_ALLREDUCE=p2p at load time, on every rank); rows beyond the buffer's
+// capacity still go through NCCL.  Validated on 2 GPUs (the tensor-parallel parity test).
 #include <chrono>
 #include <cstdlib>
 #include <string>
@@ -119,8 +119,7 @@ __global__ void __launch_bounds__(AR_THREADS) k_tp_allreduce(float* __restrict__
 
 bool tp_p2p_requested() {
     const char* e = std::getenv("SOC_B200_TP_ALLREDUCE");
-    const char* x = std::getenv("SOC_B200_EXPERIMENTAL");
-    return e && std::string(e) == "p2p" && x && std::string(x) == "1";
+    return e && std::string(e) == "p2p";
 }
 
 namespace {

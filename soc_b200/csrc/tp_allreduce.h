@@ -9,8 +9,8 @@
 
 namespace socb {
 
-// SOC_B200_TP_ALLREDUCE=p2p together with SOC_B200_EXPERIMENTAL=1: use the peer-memory
-// all-reduce instead of NCCL's (every rank must set the same).
+// SOC_B200_TP_ALLREDUCE=p2p: use the peer-memory all-reduce instead of NCCL's (every rank must
+// set the same).
 bool tp_p2p_requested();
 
 // Every rank's verdict on a local step, combined over `comm` (minimum of `ok`), with the

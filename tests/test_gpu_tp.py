@@ -35,12 +35,9 @@ def _gpus():
 @pytest.mark.parametrize("case", sorted(CASES))
 def test_tensor_parallel_two_ranks_match_oracle(make_bundle, tmp_path, case, allreduce):
     """allreduce "p2p": the residual sums of decode-sized steps go through the peer-memory
-    all-reduce (SOC_B200_TP_ALLREDUCE=p2p); it runs only with SOC_B200_EXPERIMENTAL=1 until it
-    has passed on GPUs."""
+    all-reduce (SOC_B200_TP_ALLREDUCE=p2p) instead of NCCL's."""
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
-    if allreduce == "p2p" and os.environ.get("SOC_B200_EXPERIMENTAL") != "1":
-        pytest.skip("peer-memory all-reduce not yet validated on GPUs")
     cfg, dt = CASES[case]
     p = make_bundle("tp_" + case, cfg, seed=5, dtype=dt)
     out = tmp_path / "tp.npz"

@@ -57,6 +57,7 @@ constexpr int KPF = 4;                   // keys per warp per attention batch
 constexpr int UNIT_KEYS = 64;            // keys per attention unit (two batches per warp)
 constexpr unsigned SPIN_LIMIT = 1u << 22;
 constexpr int LMAX = 48;                 // layers whose weight pointers are kept in shared memory
+constexpr int XS_PAD = 16;               // halves of padding per part row of xs
 
 enum Ph { P_QKV = 0, P_ATT = 1, P_O = 2, P_GU = 3, P_D = 4 };
 // producer / tile-range phases (the lm_head is phase 4 of "layer" L)
@@ -64,7 +65,9 @@ enum MPh { M_QKV = 0, M_O = 1, M_GU = 2, M_D = 3, M_LM = 4 };
 
 struct __align__(128) Smem {
     uint8_t ring[SLOTS][SLOT_BYTES];
-    uint16_t xs[NSPLIT][NW * KS_MAX];  // split input slices (natural order); attention scratch
+    // split input slices in A-fragment order (xs_pos); attention scratch.  The rows are padded
+    // so that part rows start 8 banks apart (the A loads of one step hit distinct banks).
+    uint16_t xs[NSPLIT][NW * KS_MAX + XS_PAD];
     float red[2][NW][MAX_ROWS];        // per-warp partial sums, double-buffered across phases
     float wss[2][NW];                  // per-warp sums of squares (same double buffering)
     float lss[NW], lmax[NW];           // the lm_head's staging
@@ -148,6 +151,28 @@ __device__ __forceinline__ unsigned long long ld_word(const unsigned long long* 
     return w;
 }
 __device__ __forceinline__ uint32_t word_tag(unsigned long long w) { return static_cast<uint32_t>(w >> 32); }
+// Loads issued ahead of a poll (norm weights, RoPE rows, cached keys).  They are relaxed (strong)
+// loads so that they stay in program order with the poll's loads: a weak load may be scheduled
+// after the poll, which would put a second memory round trip on the critical path.
+__device__ __forceinline__ uint32_t ld_ahead_u32(const void* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint2 ld_ahead_u64(const void* p) {
+    uint2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float ld_ahead_f32(const float* p) { return __uint_as_float(ld_ahead_u32(p)); }
+__device__ __forceinline__ float2 ld_ahead_f2(const float2* p) {
+    const uint2 v = ld_ahead_u64(p);
+    return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+}
+// Largest of the lanes' values, for values >= 0 (their bit patterns order like the values).
+__device__ __forceinline__ float warp_max_nonneg(float v) {
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
+}
 __device__ __forceinline__ float word_val(unsigned long long w) { return __uint_as_float(static_cast<uint32_t>(w)); }
 
 __device__ __forceinline__ uint32_t mk_tag(const MKParams& p, int t, int l, int ph) {
@@ -220,6 +245,7 @@ __device__ __forceinline__ bool poll_strided(const unsigned long long* src, int 
     return true;
 }
 
+
 // One word, waiting (bounded) for its tag.
 __device__ __forceinline__ float poll_one(const unsigned long long* src, uint32_t tag, int* err) {
     float v[1] = {0.0f};
@@ -260,8 +286,10 @@ __device__ __forceinline__ unsigned long long poll_keys(const unsigned long long
 
 // Trace slot `e` of layer `l` (first step only, consumer thread 0).  Slots per layer: 0 start;
 // per matrix phase (base 1 qkv, 6 o, 11 gu, 16 down): +0 entry, +1 slice ready, +2 products
-// done, +3 after the CTA barrier, +4 outputs stored; 26 + phase: first chunk resident; attention:
-// 21 input ready, 23 q/k/v staged, 24 keys done, 25 partials merged, 22 done.
+// done, +3 after the CTA barrier, +4 outputs stored; 26 + phase: first chunk resident; 36 +
+// phase: first chunk's products done; 30 / 31: the residual of the o / down epilogue in hand;
+// attention: 21 input ready, 32 normed and rotated, 23 q/k/v staged, 33 first keys unpacked,
+// 24 keys done, 25 partials merged, 34 merge weights ready, 35 outputs stored, 22 done.
 // Layer L holds the lm_head: 1 input ready, 2 staged, 4 done.
 #define MK_TR(l, e)                                                                                                  \
     do {                                                                                                             \
@@ -362,7 +390,15 @@ __device__ __forceinline__ int split_exponent(float mx) {
     return max(-100, min(100, 14 - ex));
 }
 
-// Writes this lane's M values (already scaled) as parts into xs[part][base + 32 i + lane].
+// Position of input element x in a part row of xs: within each 16-column step the elements a
+// lane with q = lane % 4 feeds to the MMA (2q, 2q + 1, 2q + 8, 2q + 9) sit together at 4q, so
+// the lane reads its A registers of a step with one 8-byte load.
+__device__ __forceinline__ int xs_pos(int x) {
+    const int j = x & 15;
+    return (x & ~15) | (((j & 7) >> 1) << 2) | ((j >> 3) << 1) | (j & 1);
+}
+
+// Writes this lane's M values (already scaled) as parts into xs[part][xs_pos(base + 32 i + lane)].
 template <typename TX, int M>
 __device__ __forceinline__ void write_parts(Smem& sm, int base, int lane, const float (&v)[M]) {
 #pragma unroll
@@ -370,7 +406,7 @@ __device__ __forceinline__ void write_parts(Smem& sm, int base, int lane, const 
         uint16_t o[NSPLIT];
         Split<TX>::run(v[i], o);
 #pragma unroll
-        for (int s = 0; s < Split<TX>::N; ++s) sm.xs[s][base + 32 * i + lane] = o[s];
+        for (int s = 0; s < Split<TX>::N; ++s) sm.xs[s][xs_pos(base + 32 * i + lane)] = o[s];
     }
 }
 
@@ -583,7 +619,10 @@ template <typename TX, typename TE, int KS>
 __device__ __forceinline__ int load_slice(const MKParams& p, Smem& sm, const Input& in, const StepCtx& sc, int base,
                                           int lane, float& ss) {
     constexpr int M = KS / 32;
-    float v[M];
+    float v[M], nv[M];
+    // the norm weights do not depend on the input: load them before waiting for it
+#pragma unroll
+    for (int i = 0; i < M; ++i) nv[i] = in.norm ? ld_ahead_f32(in.norm + base + 32 * i + lane) : 1.0f;
     if (in.words == nullptr) {
         const TE* e = static_cast<const TE*>(p.embed) + static_cast<size_t>(sc.tok) * p.H + base + lane;
 #pragma unroll
@@ -601,10 +640,10 @@ __device__ __forceinline__ int load_slice(const MKParams& p, Smem& sm, const Inp
 #pragma unroll
     for (int i = 0; i < M; ++i) {
         ss += v[i] * v[i];
-        if (in.norm) v[i] *= __ldg(in.norm + base + 32 * i + lane);
+        v[i] *= nv[i];
         mx = fmaxf(mx, fabsf(v[i]));
     }
-    mx = warp_max(mx);
+    mx = warp_max_nonneg(mx);
     const int e = split_exponent(mx);
     const float sc2 = pow2i(e);
 #pragma unroll
@@ -614,18 +653,16 @@ __device__ __forceinline__ int load_slice(const MKParams& p, Smem& sm, const Inp
     return e;
 }
 
-// The A fragment of 16-column step kt of this warp's slice: rows g < parts hold the input's
-// parts (read from xs), the other rows are zero.
-// Rows g < parts read the input's parts; the other lanes' A registers are zero.
+// The A fragment of 16-column step kt of this warp's slice.  Rows g < parts hold the input's
+// parts (read from xs); the other rows repeat them (row g reads part g mod parts).  Row g of the
+// product depends only on row g of A, and only rows g < parts are used, so the repeats cost
+// nothing and every lane loads without a branch.
 struct AFrag {
-    const uint16_t* row;  // this lane's part row at the slice start (nullptr: a zero row)
+    const uint16_t* row;  // this lane's part row at the slice start, plus 4 q (xs_pos order)
     __device__ __forceinline__ void at(int kt, uint32_t& a0, uint32_t& a2) const {
-        if (row != nullptr) {
-            a0 = *reinterpret_cast<const uint32_t*>(row + kt * 16);
-            a2 = *reinterpret_cast<const uint32_t*>(row + kt * 16 + 8);
-        } else {
-            a0 = a2 = 0u;
-        }
+        const uint2 v = *reinterpret_cast<const uint2*>(row + kt * 16);
+        a0 = v.x;
+        a2 = v.y;
     }
 };
 
@@ -633,7 +670,7 @@ template <typename TX>
 __device__ __forceinline__ AFrag afrag_of(const Smem& sm, int base, int lane) {
     const int g = lane >> 2, q = lane & 3;
     AFrag f;
-    f.row = g < Split<TX>::N ? sm.xs[g] + base + 2 * q : nullptr;
+    f.row = sm.xs[g % Split<TX>::N] + base + 4 * q;
     return f;
 }
 
@@ -805,6 +842,7 @@ __device__ __forceinline__ bool matrix_phase(const MKParams& p, Smem& sm, const 
                 }
             }
         }
+        if (u == a) MK_TR(l, 36 + tr / 5);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[slot]);
         u += n;
@@ -853,6 +891,8 @@ __device__ __forceinline__ bool matrix_phase(const MKParams& p, Smem& sm, const 
             } else {
                 hr = word_tag(res_w) == out.res_tag ? word_val(res_w) : poll_one(out.res + r, out.res_tag, p.err);
             }
+            if (tr == 6) MK_TR(l, 30);
+            if (tr == 16) MK_TR(l, 31);
             st_word(out.words + r, hr + y, out.tag);
         }
     }
@@ -919,9 +959,12 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
         float nw[DL];
 #pragma unroll
         for (int q = 0; q < DL; ++q) {
-            cs[q] = p.rope_cs[static_cast<size_t>(pos) * HALF + (lane * DL + q) % HALF];
-            nw[q] = (cw < G ? ly.q_norm : ly.k_norm)[lane * DL + q];
+            cs[q] = ld_ahead_f2(p.rope_cs + static_cast<size_t>(pos) * HALF + (lane * DL + q) % HALF);
+            nw[q] = ld_ahead_f32((cw < G ? ly.q_norm : ly.k_norm) + lane * DL + q);
         }
+        // the page of the new position (the warp that appends k and v)
+        const int page_new =
+            (cw == G && owns_new) ? static_cast<int>(ld_ahead_u32(p.page_table + pos / p.page_tokens)) : 0;
         Raw kraw[KPF], vraw[KPF];
         const int key0 = kb + cw;
 #pragma unroll
@@ -931,8 +974,13 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                 const int pg = __ldg(p.page_table + key / p.page_tokens);
                 const size_t off =
                     ((static_cast<size_t>(pg) * p.hkv + j) * p.page_tokens + key % p.page_tokens) * D + lane * DL;
-                kraw[i] = __ldcg(reinterpret_cast<const Raw*>(kp + off));
-                vraw[i] = __ldcg(reinterpret_cast<const Raw*>(vp + off));
+                if constexpr (DL == 4) {
+                    kraw[i] = ld_ahead_u64(kp + off);
+                    vraw[i] = ld_ahead_u64(vp + off);
+                } else {
+                    kraw[i] = ld_ahead_u32(kp + off);
+                    vraw[i] = ld_ahead_u32(vp + off);
+                }
             }
         }
         // -- this layer's q (and, for the split holding the new position, k and v) rows
@@ -960,13 +1008,14 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                 const float partner = __shfl_xor_sync(0xffffffffu, v[q], 16);
                 o[q] = first ? (v[q] * cs[q].x - partner * cs[q].y) : (partner * cs[q].y + v[q] * cs[q].x);
             }
+            MK_TR(l, 32);
             if (cw < G) {
 #pragma unroll
                 for (int q = 0; q < DL; ++q) qs[cw * D + lane * DL + q] = o[q];
             } else {
-                const int page = __ldg(p.page_table + pos / p.page_tokens);
                 const size_t off =
-                    ((static_cast<size_t>(page) * p.hkv + j) * p.page_tokens + pos % p.page_tokens) * D + lane * DL;
+                    ((static_cast<size_t>(page_new) * p.hkv + j) * p.page_tokens + pos % p.page_tokens) * D +
+                    lane * DL;
 #pragma unroll
                 for (int q = 0; q < DL; ++q) {
                     const __half kh = __float2half_rn(o[q]), vh = __float2half_rn(vv[q]);
@@ -1031,6 +1080,7 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                         unpack_kv(vraw[i0 + bb], vf[bb]);
                     }
                 }
+                if (base == key0 && i0 == 0) MK_TR(l, 33);
 #pragma unroll
                 for (int g = 0; g < MAXG; ++g) {
                     if (g >= G) break;
@@ -1106,6 +1156,7 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
             }
         }
         nbar();
+        MK_TR(l, 34);
         for (int idx = ctid; idx < G * D; idx += CT) {
             const int g = idx / D, d = idx % D;
             const float M = vs[2 * g], L = vs[2 * g + 1];
@@ -1122,6 +1173,7 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                 }
             }
         }
+        MK_TR(l, 35);
         nbar();
     }
     // split-K: the unit of split 0 of each kv head combines the partials of its splits (after
@@ -1170,7 +1222,7 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
 
 // ------------------------------------------------------------------ lm_head
 // Every warp takes whole tiles (all H columns), so the whole final-normed h is staged once as
-// parts: parts 0 and 1 in xs[0] / xs[1], the bf16 third part after the staging floats in xs[2].
+// parts, part s in xs[s] (xs_pos order).
 template <typename TE, int KSH>
 __device__ __forceinline__ void lm_phase(const MKParams& p, Smem& sm, const StepCtx& sc, long long& k, int cw, int lane,
                                       unsigned long long& wbest) {
@@ -1179,17 +1231,19 @@ __device__ __forceinline__ void lm_phase(const MKParams& p, Smem& sm, const Step
     int a, b;
     cta_tiles(mt.tiles, blockIdx.x, gridDim.x, 0, M_LM, a, b);
     const int base = cw * KSH;
-    float v[M];
+    float v[M], nv[M];
+#pragma unroll
+    for (int i = 0; i < M; ++i) nv[i] = ld_ahead_f32(p.final_norm + base + 32 * i + lane);
     poll_slice<M>(p.vec + base, lane, mk_tag(p, sc.t, p.L - 1, P_D), v, p.err);
     float ss = 0.0f, mx = 0.0f;
 #pragma unroll
     for (int i = 0; i < M; ++i) {
         ss += v[i] * v[i];
-        v[i] *= __ldg(p.final_norm + base + 32 * i + lane);
+        v[i] *= nv[i];
         mx = fmaxf(mx, fabsf(v[i]));
     }
     ss = warp_sum(ss);
-    mx = warp_max(mx);
+    mx = warp_max_nonneg(mx);
     if (lane == 0) {
         sm.lss[cw] = ss;
         sm.lmax[cw] = mx;
@@ -1211,7 +1265,7 @@ __device__ __forceinline__ void lm_phase(const MKParams& p, Smem& sm, const Step
         Split<TE>::run(v[i] * sc2, o);
         const int r = base + 32 * i + lane;
 #pragma unroll
-        for (int s2 = 0; s2 < Split<TE>::N; ++s2) sm.xs[s2][r] = o[s2];
+        for (int s2 = 0; s2 < Split<TE>::N; ++s2) sm.xs[s2][xs_pos(r)] = o[s2];
     }
     nbar();
     MK_TR(p.L, 2);
@@ -1383,6 +1437,8 @@ __device__ void consumers(const MKParams& p, Smem& sm, int cw, int lane) {
         if (lane == 0) p.ids[p.steps] = bk <= 1ull ? 0 : argmax_key_index(bk);
     }
 }
+
+static_assert(sizeof(Smem) <= 227 * 1024, "shared memory of the persistent kernel");
 
 template <typename TX, typename TE, int F, int KSH, int KSA, int KSI, int D>
 __global__ void __launch_bounds__(THREADS, 1) k_decode_mk(MKParams p) {

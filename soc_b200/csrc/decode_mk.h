@@ -56,7 +56,7 @@ struct MKParams {
     unsigned long long* trace;
 };
 
-constexpr int MK_TRACE_PER_LAYER = 32;
+constexpr int MK_TRACE_PER_LAYER = 48;
 constexpr int MK_TRACE_CHUNKS = 64;
 __host__ __device__ inline size_t mk_trace_stride(int L) { return static_cast<size_t>(L + 1) * MK_TRACE_PER_LAYER + 3 * MK_TRACE_CHUNKS; }
 

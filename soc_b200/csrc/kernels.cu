@@ -841,18 +841,45 @@ void launch_kv_fill_random(__half* kpool, __half* vpool, size_t layer_stride, co
 // round-to-nearest one the reference's float division performs, so ties it creates between
 // neighbouring logits are ties here too; temperature 1 compares the logits themselves.
 // NaNs never win.
-// keys != nullptr: write the row's best (value, global index) key instead of the id, for a
-// vocab shard whose first global index is v_off (merged across shards by k_argmax_merge).
-__global__ void k_argmax(const float* __restrict__ logits, int V, int ld, int v_off, float temp,
-                         int* __restrict__ next_ids, unsigned long long* __restrict__ keys) {
-    __shared__ unsigned long long red[32];
-    const float* row = logits + static_cast<size_t>(blockIdx.x) * ld;
+//
+// One block per ARGMAX_COLS columns of a row (grid: column blocks x rows), so that even a single
+// row spreads over dozens of SMs: every thread has four 16-byte loads in flight, the block reduces
+// its best (value, index) key and merges it into keys[row] with a 64-bit atomic maximum (keys[row]
+// starts at zero, which no value's key equals).  v_off is the global index of column 0 (a vocab
+// shard under tensor parallelism).
+constexpr int ARGMAX_THREADS = 256;
+constexpr int ARGMAX_COLS = ARGMAX_THREADS * 16;
+
+__global__ void __launch_bounds__(ARGMAX_THREADS) k_argmax(const float* __restrict__ logits, int V, int ld, int v_off,
+                                                         float temp, unsigned long long* __restrict__ keys) {
+    __shared__ unsigned long long red[ARGMAX_THREADS / 32];
+    const float* row = logits + static_cast<size_t>(blockIdx.y) * ld;
+    const int c0 = blockIdx.x * ARGMAX_COLS;
     unsigned long long best = 0ull;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = temp == 1.0f ? row[i] : __fdiv_rn(row[i], temp);
-        if (v != v) continue;
-        const unsigned long long k = argmax_key(v, v_off + i);
-        best = k > best ? k : best;
+    auto take = [&](float x, int i) {
+        const float v = temp == 1.0f ? x : __fdiv_rn(x, temp);
+        if (v == v) {
+            const unsigned long long k = argmax_key(v, v_off + i);
+            best = k > best ? k : best;
+        }
+    };
+    const bool vec = (ld % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && c0 + ARGMAX_COLS <= V;
+    if (vec) {
+        float4 f[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            f[j] = __ldcs(reinterpret_cast<const float4*>(row + c0) + threadIdx.x + ARGMAX_THREADS * j);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = c0 + 4 * (threadIdx.x + ARGMAX_THREADS * j);
+            take(f[j].x, i);
+            take(f[j].y, i + 1);
+            take(f[j].z, i + 2);
+            take(f[j].w, i + 3);
+        }
+    } else {
+        const int c1 = min(V, c0 + ARGMAX_COLS);
+        for (int i = c0 + threadIdx.x; i < c1; i += ARGMAX_THREADS) take(row[i], i);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -861,19 +888,11 @@ __global__ void k_argmax(const float* __restrict__ logits, int V, int ld, int v_
     }
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        unsigned long long b = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+    if (threadIdx.x == 0) {
+        unsigned long long b = 0ull;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
-            b = other > b ? other : b;
-        }
-        if (threadIdx.x == 0) {
-            if (keys != nullptr)
-                keys[blockIdx.x] = b;
-            else
-                next_ids[blockIdx.x] = b == 0ull ? 0 : argmax_key_index(b);
-        }
+        for (int w = 0; w < ARGMAX_THREADS / 32; ++w) b = red[w] > b ? red[w] : b;
+        if (b != 0ull) atomicMax(keys + blockIdx.y, b);
     }
 }
 
@@ -890,19 +909,27 @@ __global__ void k_argmax_merge(const unsigned long long* __restrict__ keys_all, 
     next_ids[r] = b == 0ull ? 0 : argmax_key_index(b);
 }
 
-void launch_argmax(const float* logits, int vocab, int ld, int rows, float temperature, int* next_ids, cudaStream_t st) {
-    if (rows <= 0) return;
-    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, 0, temperature, next_ids, nullptr);
-    SOCB_CUDA(cudaGetLastError());
-    count_launches(1);
+__global__ void k_zero_keys(unsigned long long* keys, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) keys[i] = 0ull;
 }
 
 void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_off, float temperature,
                         unsigned long long* keys, cudaStream_t st) {
     if (rows <= 0) return;
-    k_argmax<<<rows, 1024, 0, st>>>(logits, vocab, ld, v_off, temperature, nullptr, keys);
+    // a kernel rather than a memset node, so that the step stays a graph of kernels only
+    k_zero_keys<<<(rows + 255) / 256, 256, 0, st>>>(keys, rows);
+    const dim3 grid((vocab + ARGMAX_COLS - 1) / ARGMAX_COLS, rows);
+    k_argmax<<<grid, ARGMAX_THREADS, 0, st>>>(logits, vocab, ld, v_off, temperature, keys);
     SOCB_CUDA(cudaGetLastError());
-    count_launches(1);
+    count_launches(2);
+}
+
+void launch_argmax(const float* logits, int vocab, int ld, int rows, float temperature, unsigned long long* keys,
+                   int* next_ids, cudaStream_t st) {
+    if (rows <= 0) return;
+    launch_argmax_keys(logits, vocab, ld, rows, 0, temperature, keys, st);
+    launch_argmax_merge(keys, 1, rows, next_ids, st);
 }
 
 void launch_argmax_merge(const unsigned long long* keys_all, int shards, int rows, int* next_ids, cudaStream_t st) {
@@ -919,19 +946,24 @@ namespace socb {
 // ---------------------------------------------------------------- top-k candidates
 // The sampler's candidate list (Sampler::SampleFromLogits, Mac/gpu/src/runtime/sampler.cpp:36-68):
 // the k largest logit / temperature of a row, larger first; among equal values the lower token
-// id first (the order the device argmax already uses).  Two launches: every CTA sorts a chunk of
-// the row as orderable keys (argmax_key) and keeps its first k; one CTA sorts those candidates
-// and writes the first k ids with their raw logits.  Element g of the row lives at
+// id first (the order the device argmax already uses).  As orderable keys (argmax_key, unique per
+// token) the top k of a set is the top k of the union of its parts' top k, so the row is reduced
+// in rounds: every CTA of the first launch sorts TOPK_CHUNK elements and keeps its first k; every
+// CTA of a later launch merges up to TOPK_GROUP such lists and keeps its first k, until one list is
+// left; the last launch writes the ids with their raw logits.  Element g of the row lives at
 //   base + (g / seg_len) * seg_stride + g % seg_len
 // (one segment per tensor-parallel vocab shard after the all-gather; one segment otherwise).
 namespace {
-constexpr int TOPK_CHUNK = 4096;
+constexpr int TOPK_CHUNK = 1024;  // elements per CTA of the first round
+constexpr int TOPK_GROUP = 16;    // lists merged per CTA of the later rounds (16 x 64 keys at most)
+constexpr int TOPK_THREADS = 512;
 
 __device__ __forceinline__ float topk_elem(const float* base, int g, int seg_len, size_t seg_stride) {
     return base[static_cast<size_t>(g / seg_len) * seg_stride + g % seg_len];
 }
 
-// Descending bitonic sort of n (a power of two) keys in shared memory by the whole CTA.
+// Descending bitonic sort of n (a power of two, n <= 2 * TOPK_THREADS) keys in shared memory by
+// the whole CTA.
 __device__ void bitonic_desc(unsigned long long* s, int n) {
     for (int size = 2; size <= n; size <<= 1) {
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
@@ -951,8 +983,9 @@ __device__ void bitonic_desc(unsigned long long* s, int n) {
     }
 }
 
-__global__ void k_topk_chunks(const float* __restrict__ base, int V, int seg_len, size_t seg_stride, float temp,
-                              int k, unsigned long long* __restrict__ cand) {
+__global__ void __launch_bounds__(TOPK_THREADS) k_topk_chunks(const float* __restrict__ base, int V, int seg_len,
+                                                              size_t seg_stride, float temp, int k,
+                                                              unsigned long long* __restrict__ cand) {
     __shared__ unsigned long long s[TOPK_CHUNK];
     const int first = blockIdx.x * TOPK_CHUNK;
     for (int i = threadIdx.x; i < TOPK_CHUNK; i += blockDim.x) {
@@ -970,33 +1003,59 @@ __global__ void k_topk_chunks(const float* __restrict__ base, int V, int seg_len
     for (int i = threadIdx.x; i < k; i += blockDim.x) cand[static_cast<size_t>(blockIdx.x) * k + i] = s[i];
 }
 
-__global__ void k_topk_merge(const unsigned long long* __restrict__ cand, int n, int k, const float* __restrict__ base,
-                             int seg_len, size_t seg_stride, float* __restrict__ top_logits, int* __restrict__ top_ids) {
-    __shared__ unsigned long long s[TOPK_CHUNK];
+// Lists [TOPK_GROUP b, TOPK_GROUP (b + 1)) of `lists` sorted lists of k keys -> list b of `out`;
+// with one CTA (the last round) the ids and raw logits instead.
+__global__ void __launch_bounds__(TOPK_THREADS) k_topk_merge(const unsigned long long* __restrict__ in, int lists,
+                                                             int k, unsigned long long* __restrict__ out,
+                                                             const float* __restrict__ base, int seg_len,
+                                                             size_t seg_stride, float* __restrict__ top_logits,
+                                                             int* __restrict__ top_ids) {
+    __shared__ unsigned long long s[TOPK_GROUP * 64];
+    const int l0 = blockIdx.x * TOPK_GROUP, nl = min(TOPK_GROUP, lists - l0);
+    const int n = nl * k;
     int np = 1;
     while (np < n) np <<= 1;
-    for (int i = threadIdx.x; i < np; i += blockDim.x) s[i] = i < n ? cand[i] : 0ull;
+    for (int i = threadIdx.x; i < np; i += blockDim.x) s[i] = i < n ? in[static_cast<size_t>(l0) * k + i] : 0ull;
     __syncthreads();
     bitonic_desc(s, np);
     for (int i = threadIdx.x; i < k; i += blockDim.x) {
         const unsigned long long key = s[i];
-        const int id = key == 0ull ? -1 : argmax_key_index(key);
-        top_ids[i] = id;
-        top_logits[i] = id < 0 ? -INFINITY : topk_elem(base, id, seg_len, seg_stride);
+        if (out != nullptr) {
+            out[static_cast<size_t>(blockIdx.x) * k + i] = key;
+        } else {
+            const int id = key == 0ull ? -1 : argmax_key_index(key);
+            top_ids[i] = id;
+            top_logits[i] = id < 0 ? -INFINITY : topk_elem(base, id, seg_len, seg_stride);
+        }
     }
 }
 }  // namespace
 
-int topk_scratch_keys(int V, int k) { return ((V + TOPK_CHUNK - 1) / TOPK_CHUNK) * k; }
+// First-round lists, then each later round's (at most a sixteenth as many), side by side.
+int topk_scratch_keys(int V, int k) {
+    const int chunks = (V + TOPK_CHUNK - 1) / TOPK_CHUNK;
+    return 2 * chunks * k;
+}
 
 void launch_topk(const float* base, int V, int seg_len, size_t seg_stride, float temperature, int k,
                  unsigned long long* cand, float* top_logits, int* top_ids, cudaStream_t st) {
-    const int chunks = (V + TOPK_CHUNK - 1) / TOPK_CHUNK;
-    if (k < 1 || k > TOPK_MAX || chunks * k > TOPK_CHUNK) throw Error(-2, "top-k: k out of range for this vocab");
-    k_topk_chunks<<<chunks, 512, 0, st>>>(base, V, seg_len, seg_stride, temperature, k, cand);
-    k_topk_merge<<<1, 512, 0, st>>>(cand, chunks * k, k, base, seg_len, seg_stride, top_logits, top_ids);
+    if (k < 1 || k > TOPK_MAX || V < 1) throw Error(-2, "top-k: k out of range");
+    int lists = (V + TOPK_CHUNK - 1) / TOPK_CHUNK;
+    k_topk_chunks<<<lists, TOPK_THREADS, 0, st>>>(base, V, seg_len, seg_stride, temperature, k, cand);
+    int launches = 1;
+    unsigned long long* in = cand;
+    unsigned long long* out = cand + static_cast<size_t>(lists) * k;
+    while (lists > TOPK_GROUP) {
+        const int groups = (lists + TOPK_GROUP - 1) / TOPK_GROUP;
+        k_topk_merge<<<groups, TOPK_THREADS, 0, st>>>(in, lists, k, out, base, seg_len, seg_stride, nullptr, nullptr);
+        ++launches;
+        // the next round reads this one's lists and writes over the ones it just read
+        std::swap(in, out);
+        lists = groups;
+    }
+    k_topk_merge<<<1, TOPK_THREADS, 0, st>>>(in, lists, k, nullptr, base, seg_len, seg_stride, top_logits, top_ids);
     SOCB_CUDA(cudaGetLastError());
-    count_launches(2);
+    count_launches(launches + 1);
 }
 
 }  // namespace socb

@@ -73,7 +73,9 @@ void launch_kv_fill_random(__half* kpool, __half* vpool, size_t layer_stride, co
                            unsigned long long seed, cudaStream_t st);
 
 // temperature: the pick maximises logit / temperature (IEEE single division; 1 = the logits).
-void launch_argmax(const float* logits, int vocab, int ld, int rows, float temperature, int* next_ids, cudaStream_t st);
+// `keys` is scratch for one 64-bit key per row.
+void launch_argmax(const float* logits, int vocab, int ld, int rows, float temperature, unsigned long long* keys,
+                   int* next_ids, cudaStream_t st);
 // Vocab-parallel greedy pick: per-row (value, global index) keys of one shard, and the merge
 // of all shards' keys [shards][rows] (lowest global index wins ties, as above).
 void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_off, float temperature, unsigned long long* keys,

@@ -567,17 +567,20 @@ struct soc_model {
     struct LoopState {
         int* out;
         int seq, start, step;
+        int steps, eos;  // the device loop runs while step < steps and out[step] != eos (eos >= 0)
     };
     LoopState* d_loop = nullptr;
-    cudaGraphExec_t step_graph = nullptr;
+    cudaGraphExec_t step_graph = nullptr;  // the decode loop: a WHILE node around one step
+    int loop_steps_queued = 0;             // steps the last graph decode loop was launched for
     // short prefill chunks replayed as one CUDA graph (the launches, not the bytes, bound them)
     struct PrefillKey {
         const void *kv, *h, *xa, *logits;
+        unsigned long long epoch;  // buf_epoch at capture
         int seq, start, n, lm;
         float temperature;
         bool operator==(const PrefillKey& o) const {
-            return kv == o.kv && h == o.h && xa == o.xa && logits == o.logits && seq == o.seq && start == o.start &&
-                   n == o.n && lm == o.lm && temperature == o.temperature;
+            return kv == o.kv && h == o.h && xa == o.xa && logits == o.logits && epoch == o.epoch && seq == o.seq &&
+                   start == o.start && n == o.n && lm == o.lm && temperature == o.temperature;
         }
     };
     cudaGraphExec_t pf_graph = nullptr;
@@ -586,6 +589,7 @@ struct soc_model {
     bool pf_graph_broken = false;  // a capture failed once: prefill chunks run directly
     const soc_kv* graph_kv = nullptr;
     int graph_splits = 0;
+    unsigned long long graph_epoch = 0;  // buf_epoch when step_graph was captured
     long long graph_kernels = 0;
     // persistent batch-1 decode kernel (decode_mk.cu)
     bool mk_ok = false;
@@ -611,8 +615,11 @@ struct soc_model {
         allocs.push_back(p);
         return p;
     }
-    void dfree(void* p) {
+    // Bumped whenever a buffer is freed: a captured graph that baked in the old pointer is stale.
+    unsigned long long buf_epoch = 0;
+    void dfree(void* p, bool graphs_may_hold = true) {
         if (!p) return;
+        if (graphs_may_hold) ++buf_epoch;
         cudaFree(p);
         for (auto& a : allocs)
             if (a == p) a = nullptr;
@@ -703,10 +710,8 @@ void ensure_logits(soc_model* m, int rows) {
     m->dfree(m->logits);
     m->logits = static_cast<float*>(m->dmalloc(sizeof(float) * rows * m->v_loc));
     m->logits_rows = rows;
-    if (m->tp_size > 1) {
-        m->dfree(m->d_keys);
-        m->d_keys = static_cast<unsigned long long*>(m->dmalloc(sizeof(unsigned long long) * rows * m->tp_size));
-    }
+    m->dfree(m->d_keys);
+    m->d_keys = static_cast<unsigned long long*>(m->dmalloc(sizeof(unsigned long long) * rows * m->tp_size));
 }
 
 void ensure_attn_scratch(soc_model* m, size_t floats) {
@@ -861,7 +866,7 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
                           lm_rows, m->final_norm, eps, m->logits, m->v_loc, LIN_STORE, st);
         }
         if (m->tp_size == 1) {
-            launch_argmax(m->logits, m->v_loc, m->v_loc, lm_rows, m->temperature, m->d_next, st);
+            launch_argmax(m->logits, m->v_loc, m->v_loc, lm_rows, m->temperature, m->d_keys, m->d_next, st);
         } else {
             unsigned long long* mine = m->d_keys + static_cast<size_t>(m->tp_rank) * lm_rows;
             launch_argmax_keys(m->logits, m->v_loc, m->v_loc, lm_rows, m->v_off, m->temperature, mine, st);
@@ -914,7 +919,8 @@ void prefill_graph(soc_model* m, soc_kv* kv, int seq, int start, int n, bool las
     // everything the forward allocates lazily is allocated before a capture
     ensure_logits(m, 1);
     if (m->tc_ok) m->ctx->ws();
-    const soc_model::PrefillKey key{kv, m->h, m->xa, m->logits, seq, start, n, last ? 1 : 0, m->temperature};
+    const soc_model::PrefillKey key{kv, m->h, m->xa, m->logits, m->buf_epoch, seq, start, n, last ? 1 : 0,
+                                    m->temperature};
     if (!m->pf_graph || !(m->pf_key == key)) {
         if (m->pf_graph) cudaGraphExecDestroy(m->pf_graph);
         m->pf_graph = nullptr;
@@ -939,6 +945,7 @@ void prefill_graph(soc_model* m, soc_kv* kv, int seq, int start, int n, bool las
         cudaGraphDestroy(g);
         SOCB_CUDA(e);
         m->pf_key = key;
+        m->pf_key.epoch = m->buf_epoch;
     }
     SOCB_CUDA(cudaGraphLaunch(m->pf_graph, st));
     count_launches(m->pf_graph_kernels);
@@ -982,6 +989,24 @@ __global__ void k_step_begin(const soc_model::LoopState* st, int* tokens, int* s
 __global__ void k_step_end(soc_model::LoopState* st, const int* next) {
     st->out[st->step + 1] = next[0];
     st->step += 1;
+}
+
+__device__ __forceinline__ unsigned loop_continues(const soc_model::LoopState* st) {
+    const int s = st->step;
+    return (s < st->steps && !(st->eos >= 0 && st->out[s] == st->eos)) ? 1u : 0u;
+}
+
+// Before the loop: whether its first step runs (the generation context stops on an EOS input).
+__global__ void k_loop_gate(const soc_model::LoopState* st, cudaGraphConditionalHandle h) {
+    cudaGraphSetConditional(h, loop_continues(st));
+}
+
+// End of a step inside the loop: record the id, then whether the next step runs.  The step
+// counter grows by one per iteration and the loop ends at st->steps, so it always ends.
+__global__ void k_step_end_loop(soc_model::LoopState* st, const int* next, cudaGraphConditionalHandle h) {
+    st->out[st->step + 1] = next[0];
+    st->step += 1;
+    cudaGraphSetConditional(h, loop_continues(st));
 }
 
 // Parameters of one persistent-kernel launch (decode_mk.cu) over the buffers given.
@@ -1092,7 +1117,7 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
         std::vector<unsigned long long> host(trace_n);
         SOCB_CUDA(cudaMemcpyAsync(host.data(), trace, trace_n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, st));
         SOCB_CUDA(cudaStreamSynchronize(st));
-        m->dfree(trace);
+        m->dfree(trace, false);
         if (FILE* f = std::fopen(trace_path, "wb")) {
             const int hdr[4] = {m->mk_grid, static_cast<int>(c.layers), MK_TRACE_PER_LAYER, steps};
             std::fwrite(hdr, sizeof(int), 4, f);
@@ -1103,10 +1128,11 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
 }
 
 // `steps` decode steps of sequence `seq`, whose cache holds `start` tokens and whose
-// next input id is d_out[0]; writes ids 1..steps of d_out.  One step is captured as a
-// CUDA graph (bound to this cache and split count) and replayed per token.  eos >= 0: the
-// persistent kernel stops at the first step whose input id is eos (ids after it are not
-// written); the graph and tensor-parallel paths run every step.
+// next input id is d_out[0]; writes ids 1..steps of d_out.  Without the persistent kernel the
+// loop is one CUDA graph (bound to this cache, split count and buffers): a WHILE node around one
+// captured step.  eos >= 0: both stop on the device at the first step whose input id is eos (ids
+// after it are not written); the tensor-parallel path (collectives stay out of graphs) runs every
+// step.
 void decode_loop(soc_model* m, soc_kv* kv, int seq, int start, int steps, int32_t* d_out, int eos = -1) {
     if (m->mk_ok) {
         run_mk(m, kv, seq, start, steps, d_out, nullptr, eos);
@@ -1120,7 +1146,7 @@ void decode_loop(soc_model* m, soc_kv* kv, int seq, int start, int steps, int32_
     if (!m->d_loop) m->d_loop = static_cast<soc_model::LoopState*>(m->dmalloc(sizeof(soc_model::LoopState)));
     if (m->tp_size > 1) {
         // Tensor-parallel steps are queued one by one (their collectives stay out of graphs).
-        const soc_model::LoopState init{d_out, seq, start, 0};
+        const soc_model::LoopState init{d_out, seq, start, 0, steps, -1};
         SOCB_CUDA(cudaMemcpyAsync(m->d_loop, &init, sizeof(init), cudaMemcpyHostToDevice, st));
         for (int i = 0; i < steps; ++i) {
             k_step_begin<<<1, 1, 0, st>>>(m->d_loop, m->d_tokens, m->d_seq, m->d_pos);
@@ -1130,35 +1156,62 @@ void decode_loop(soc_model* m, soc_kv* kv, int seq, int start, int steps, int32_
         }
         return;
     }
-    if (!m->step_graph || m->graph_kv != kv || m->graph_splits != splits) {
+    if (!m->step_graph || m->graph_kv != kv || m->graph_splits != splits || m->graph_epoch != m->buf_epoch) {
+        // One graph runs the whole loop: a gate kernel, then a WHILE node whose body is one
+        // decode step ending in the kernel that decides whether the next step runs.
         if (m->step_graph) cudaGraphExecDestroy(m->step_graph);
         m->step_graph = nullptr;
-        cudaGraph_t g = nullptr;
+        cudaGraph_t g = nullptr, tmp = nullptr;
+        SOCB_CUDA(cudaGraphCreate(&g, 0));
         const long long before = launches_so_far();
-        SOCB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         try {
-            k_step_begin<<<1, 1, 0, st>>>(m->d_loop, m->d_tokens, m->d_seq, m->d_pos);
-            forward_rows(m, kv, 1, start + steps, 0, 1, splits);
-            k_step_end<<<1, 1, 0, st>>>(m->d_loop, m->d_next);
+            cudaGraphConditionalHandle h{};
+            SOCB_CUDA(cudaGraphConditionalHandleCreate(&h, g, 0, 0));
+            SOCB_CUDA(cudaStreamBeginCaptureToGraph(st, g, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
+            k_loop_gate<<<1, 1, 0, st>>>(m->d_loop, h);
+            SOCB_CUDA(cudaStreamEndCapture(st, &tmp));
+            cudaGraphNode_t gate = nullptr;
+            size_t nn = 1;
+            SOCB_CUDA(cudaGraphGetNodes(g, &gate, &nn));
+            cudaGraphNodeParams cp{};
+            cp.type = cudaGraphNodeTypeConditional;
+            cp.conditional.handle = h;
+            cp.conditional.type = cudaGraphCondTypeWhile;
+            cp.conditional.size = 1;
+            cudaGraphNode_t loop = nullptr;
+            SOCB_CUDA(cudaGraphAddNode(&loop, g, &gate, 1, &cp));
+            const cudaGraph_t body = cp.conditional.phGraph_out[0];
+            SOCB_CUDA(cudaStreamBeginCaptureToGraph(st, body, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
+            try {
+                k_step_begin<<<1, 1, 0, st>>>(m->d_loop, m->d_tokens, m->d_seq, m->d_pos);
+                forward_rows(m, kv, 1, start + steps, 0, 1, splits);
+                k_step_end_loop<<<1, 1, 0, st>>>(m->d_loop, m->d_next, h);
+            } catch (...) {
+                cudaStreamEndCapture(st, &tmp);
+                throw;
+            }
+            SOCB_CUDA(cudaStreamEndCapture(st, &tmp));
             // captured launches did not run: move them from the counter to the graph's size
             m->graph_kernels = launches_so_far() - before + 2;
             count_launches(-(launches_so_far() - before));
+            SOCB_CUDA(cudaGraphInstantiate(&m->step_graph, g, 0));
         } catch (...) {
-            cudaStreamEndCapture(st, &g);
-            if (g) cudaGraphDestroy(g);
+            count_launches(-(launches_so_far() - before));
+            cudaGraphDestroy(g);
+            cudaGetLastError();
             throw;
         }
-        SOCB_CUDA(cudaStreamEndCapture(st, &g));
-        const cudaError_t e = cudaGraphInstantiate(&m->step_graph, g, 0);
         cudaGraphDestroy(g);
-        SOCB_CUDA(e);
         m->graph_kv = kv;
         m->graph_splits = splits;
+        m->graph_epoch = m->buf_epoch;
     }
-    const soc_model::LoopState init{d_out, seq, start, 0};
+    const soc_model::LoopState init{d_out, seq, start, 0, steps, eos};
     SOCB_CUDA(cudaMemcpyAsync(m->d_loop, &init, sizeof(init), cudaMemcpyHostToDevice, st));
-    for (int i = 0; i < steps; ++i) SOCB_CUDA(cudaGraphLaunch(m->step_graph, st));
-    count_launches(m->graph_kernels * steps);
+    SOCB_CUDA(cudaGraphLaunch(m->step_graph, st));
+    // counted as if every step runs; soc_b200_generate corrects the count after an EOS stop
+    count_launches(1 + m->graph_kernels * steps);
+    m->loop_steps_queued = steps;
 }
 
 }  // namespace
@@ -1565,10 +1618,15 @@ void soc_b200_free_kv(soc_kv* kv) {
     if (!kv) return;
     cudaSetDevice(kv->m->ctx->device);
     cudaStreamSynchronize(kv->m->ctx->stream);
+    // graphs captured against this cache write its pools: a later cache may reuse the address
     if (kv->m->graph_kv == kv) {
         cudaGraphExecDestroy(kv->m->step_graph);
         kv->m->step_graph = nullptr;
         kv->m->graph_kv = nullptr;
+    }
+    if (kv->m->pf_graph && kv->m->pf_key.kv == kv) {
+        cudaGraphExecDestroy(kv->m->pf_graph);
+        kv->m->pf_graph = nullptr;
     }
     cudaFree(kv->k);
     cudaFree(kv->v);
@@ -1773,15 +1831,23 @@ int soc_b200_generate(soc_model* m, soc_kv* kv, int seq, const int32_t* prompt, 
         try {
             // ids after an eos stop are never written: clear them so the scan below is defined
             if (eos_token_id >= 0) SOCB_CUDA(cudaMemsetAsync(d_out, 0xff, sizeof(int32_t) * max_new, m->ctx->stream));
+            m->loop_steps_queued = 0;
             generate_dev(m, kv, seq, prompt, n_prompt, max_new, d_out, false, eos_token_id);
             SOCB_CUDA(cudaMemcpyAsync(out_ids, d_out, sizeof(int32_t) * max_new, cudaMemcpyDeviceToHost,
                                       m->ctx->stream));
             check_device_error(m);
+            if (eos_token_id >= 0 && m->loop_steps_queued > 0) {
+                // the graph loop counted every step it was launched for: take off those an EOS skipped
+                soc_model::LoopState fin{};
+                SOCB_CUDA(cudaMemcpy(&fin, m->d_loop, sizeof(fin), cudaMemcpyDeviceToHost));
+                count_launches(-static_cast<long long>(m->loop_steps_queued - fin.step) * m->graph_kernels);
+            }
         } catch (...) {
-            m->dfree(d_out);
+            m->dfree(d_out, false);
             throw;
         }
-        m->dfree(d_out);
+        // no captured graph holds the output buffer (the step graph reads it through LoopState)
+        m->dfree(d_out, false);
         int n = max_new;
         if (eos_token_id >= 0)
             for (int i = 0; i < max_new; ++i)

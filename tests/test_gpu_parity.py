@@ -95,6 +95,28 @@ def test_generate_matches_oracle_greedy(models, case, path):
 
 
 @pytest.mark.parametrize("path", ["mk", "graph"])
+def test_captured_graphs_follow_their_cache_and_buffers(models, path):
+    """Short prefills and graph-path decode steps replay captured CUDA graphs.  A graph bakes in
+    the device pointers of its KV cache and of the model's scratch: a new cache (which the host
+    allocator often places at the freed one's address) and a longer prompt (which regrows the
+    scratch) must each capture again instead of replaying against freed memory."""
+    p, m = models("qwen06_shape_2layer", path)
+    cfg = CASES["qwen06_shape_2layer"][0]
+    short, long_ = _prompt(cfg, 40, 31), _prompt(cfg, 300, 32)
+    toks, _ = O.OracleModel(p, 512).generate(short, 6)
+    long_toks, _ = O.OracleModel(p, 512).generate(long_, 3)
+    for i in range(3):
+        kv = R.KVCache(m, 1, 512)
+        assert m.generate(kv, 0, short, 6) == toks, f"fresh cache {i}"
+        kv.free()
+    kv = R.KVCache(m, 1, 512)
+    assert m.generate(kv, 0, long_, 3) == long_toks
+    kv.reset(0)
+    assert m.generate(kv, 0, short, 6) == toks
+    kv.free()
+
+
+@pytest.mark.parametrize("path", ["mk", "graph"])
 def test_generate_long_context_split_k(models, path):
     """Decode at contexts 300..340 (several attention splits per kv head)."""
     p, m = models("tied_f16_gqa2_d64", path)
@@ -124,7 +146,15 @@ def test_generate_eos_stops_and_truncates_cache(models, path, at):
     assert int(nxt[0]) == toks[first + 1]
     assert kv.length(0) == len(prompt) + first + 1
     # the next generation on the same model runs every step again
+    n0 = R.kernel_launches()
     assert m.generate(kv, 0, prompt, 8) == toks[:8]
+    full = R.kernel_launches() - n0
+    if path == "graph":
+        # the graph loop stops on the device too: its launch count, corrected by the device's
+        # own step counter, shows that the seven steps after an EOS at the prefill's pick never ran
+        n0 = R.kernel_launches()
+        assert m.generate(kv, 0, prompt, 8, eos=toks[0]) == toks[:1]
+        assert full - (R.kernel_launches() - n0) >= 7 * 10  # at least ten kernels per step
     kv.free()
 
 

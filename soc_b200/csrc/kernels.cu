@@ -956,29 +956,56 @@ namespace socb {
 namespace {
 constexpr int TOPK_CHUNK = 1024;  // elements per CTA of the first round
 constexpr int TOPK_GROUP = 16;    // lists merged per CTA of the later rounds (16 x 64 keys at most)
-constexpr int TOPK_THREADS = 512;
+constexpr int TOPK_THREADS = 512;  // two keys per thread: TOPK_CHUNK = 2 * TOPK_THREADS
 
 __device__ __forceinline__ float topk_elem(const float* base, int g, int seg_len, size_t seg_stride) {
     return base[static_cast<size_t>(g / seg_len) * seg_stride + g % seg_len];
 }
 
-// Descending bitonic sort of n (a power of two, n <= 2 * TOPK_THREADS) keys in shared memory by
-// the whole CTA.
-__device__ void bitonic_desc(unsigned long long* s, int n) {
-    for (int size = 2; size <= n; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = threadIdx.x; i < n; i += blockDim.x) {
-                const int j = i ^ stride;
-                if (j > i) {
-                    const bool desc = (i & size) == 0;
-                    const unsigned long long a = s[i], b = s[j];
-                    if (desc ? (a < b) : (a > b)) {
-                        s[i] = b;
-                        s[j] = a;
-                    }
-                }
-            }
+// Descending bitonic sort of 1,024 keys by the CTA's 512 threads: thread t holds keys t (a0) and
+// t + 512 (a1).  Compare-exchange partners less than 32 apart sit in the same warp and swap by
+// shuffles; 512 apart, in the same thread; in between, through shared memory `s` (1,024 keys) with a
+// barrier per stage (19 barriers in all instead of 55).
+__device__ __forceinline__ unsigned long long cx(unsigned long long a, unsigned long long b, bool keep_max) {
+    return keep_max ? (a > b ? a : b) : (a < b ? a : b);
+}
+
+__device__ void bitonic1024_desc(unsigned long long& a0, unsigned long long& a1, unsigned long long* s) {
+    const int t = threadIdx.x;
+    for (int size = 2; size <= 2 * TOPK_THREADS; size <<= 1) {
+        int stride = size >> 1;
+        if (stride == TOPK_THREADS) {
+            // keys t and t + 512 of one descending run: the lower index keeps the larger
+            const unsigned long long hi = a0 > a1 ? a0 : a1, lo = a0 > a1 ? a1 : a0;
+            a0 = hi;
+            a1 = lo;
+            stride >>= 1;
+        }
+        if (stride >= 32) {
+            s[t] = a0;
+            s[t + TOPK_THREADS] = a1;
             __syncthreads();
+            for (; stride >= 32; stride >>= 1) {
+                // pair q: the lower index i and i + stride
+                const int i = (t / stride) * 2 * stride + t % stride, j = i + stride;
+                const bool desc = (i & size) == 0;
+                const unsigned long long x = s[i], y = s[j];
+                if (desc ? (x < y) : (x > y)) {
+                    s[i] = y;
+                    s[j] = x;
+                }
+                __syncthreads();
+            }
+            a0 = s[t];
+            a1 = s[t + TOPK_THREADS];
+            __syncthreads();
+        }
+        for (; stride > 0; stride >>= 1) {
+            const unsigned long long b0 = __shfl_xor_sync(0xffffffffu, a0, stride);
+            const unsigned long long b1 = __shfl_xor_sync(0xffffffffu, a1, stride);
+            const bool lower = (t & stride) == 0;
+            a0 = cx(a0, b0, lower == ((t & size) == 0));
+            a1 = cx(a1, b1, lower == (((t + TOPK_THREADS) & size) == 0));
         }
     }
 }
@@ -988,19 +1015,20 @@ __global__ void __launch_bounds__(TOPK_THREADS) k_topk_chunks(const float* __res
                                                               unsigned long long* __restrict__ cand) {
     __shared__ unsigned long long s[TOPK_CHUNK];
     const int first = blockIdx.x * TOPK_CHUNK;
-    for (int i = threadIdx.x; i < TOPK_CHUNK; i += blockDim.x) {
-        const int g = first + i;
+    unsigned long long a[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int g = first + threadIdx.x + h * TOPK_THREADS;
         unsigned long long key = 0ull;  // below every real key
         if (g < V) {
             const float raw = topk_elem(base, g, seg_len, seg_stride);
             const float v = temp == 1.0f ? raw : __fdiv_rn(raw, temp);
             if (v == v) key = argmax_key(v, g);
         }
-        s[i] = key;
+        a[h] = key;
     }
-    __syncthreads();
-    bitonic_desc(s, TOPK_CHUNK);
-    for (int i = threadIdx.x; i < k; i += blockDim.x) cand[static_cast<size_t>(blockIdx.x) * k + i] = s[i];
+    bitonic1024_desc(a[0], a[1], s);
+    if (static_cast<int>(threadIdx.x) < k) cand[static_cast<size_t>(blockIdx.x) * k + threadIdx.x] = a[0];
 }
 
 // Lists [TOPK_GROUP b, TOPK_GROUP (b + 1)) of `lists` sorted lists of k keys -> list b of `out`;
@@ -1010,16 +1038,19 @@ __global__ void __launch_bounds__(TOPK_THREADS) k_topk_merge(const unsigned long
                                                              const float* __restrict__ base, int seg_len,
                                                              size_t seg_stride, float* __restrict__ top_logits,
                                                              int* __restrict__ top_ids) {
-    __shared__ unsigned long long s[TOPK_GROUP * 64];
+    __shared__ unsigned long long s[TOPK_CHUNK];
     const int l0 = blockIdx.x * TOPK_GROUP, nl = min(TOPK_GROUP, lists - l0);
-    const int n = nl * k;
-    int np = 1;
-    while (np < n) np <<= 1;
-    for (int i = threadIdx.x; i < np; i += blockDim.x) s[i] = i < n ? in[static_cast<size_t>(l0) * k + i] : 0ull;
-    __syncthreads();
-    bitonic_desc(s, np);
-    for (int i = threadIdx.x; i < k; i += blockDim.x) {
-        const unsigned long long key = s[i];
+    const int n = nl * k;  // <= 1,024; the rest of the 1,024 sorted keys are zero
+    unsigned long long a[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int i = threadIdx.x + h * TOPK_THREADS;
+        a[h] = i < n ? in[static_cast<size_t>(l0) * k + i] : 0ull;
+    }
+    bitonic1024_desc(a[0], a[1], s);
+    const int i = threadIdx.x;
+    if (i < k) {
+        const unsigned long long key = a[0];
         if (out != nullptr) {
             out[static_cast<size_t>(blockIdx.x) * k + i] = key;
         } else {

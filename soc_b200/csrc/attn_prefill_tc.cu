@@ -147,8 +147,10 @@ __global__ void __launch_bounds__(T_THREADS, 1)
     uint8_t* ps = vs + 2 * KV_BYTES;                // [2 regions] P, 128 rows x 128 keys
     TBars* bars = reinterpret_cast<TBars*>(ps + 2 * REGION);
 
-    const int qb = gridDim.x - 1 - blockIdx.x;  // longest causal extents first
-    const int head = blockIdx.y, kvh = head / (hq / hkv);
+    // CTAs start in blockIdx order, x fastest: every head's longest causal extent comes first, then
+    // every head's next longest, so the heaviest CTAs never wait for a second wave
+    const int qb = gridDim.y - 1 - blockIdx.y;
+    const int head = blockIdx.x, kvh = head / (hq / hkv);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r0 = qb * TBM;
     const int last_row = min(n, r0 + TBM) - 1;
@@ -366,7 +368,7 @@ void flash_tc_d(const float* q, int n, int hq, int hkv, int seq, int start, cons
         set = true;
     }
     const float qscale = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-    dim3 grid((n + TBM - 1) / TBM, hq);
+    dim3 grid(hq, (n + TBM - 1) / TBM);
     k_flash_prefill_tc<D><<<grid, T_THREADS, smem, st>>>(q, n, hq, hkv, seq, start, kv, qscale, out, *kv.tmk,
                                                           *kv.tmv, err);
 }

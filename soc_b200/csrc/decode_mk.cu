@@ -943,14 +943,17 @@ __device__ __forceinline__ void ld_row(const float* p, float (&v)[DL]) {
     }
 }
 
-// Attention units of layer l on this CTA: unit u = (kv head j, split s), u < hkv * S.
-// Scratch: the xs area (free between the qkv and o phases).
+// Attention units of layer l on this CTA: unit u = (GU query heads from h, split s), u < hq / GU * S.
+// With GU = 1 (short contexts) the query heads of one kv head j run as separate units on separate
+// CTAs, each reading j's keys, and the first of them appends the new k and v; with GU = hq / hkv
+// (long contexts, more key splits) a unit takes every query head of j.  Scratch: the xs area (free
+// between the qkv and o phases).
 template <int D>
 __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, const MKLayer& ly, int l,
                                              const StepCtx& sc, int cw, int lane) {
     constexpr int DL = D / 32, HALF = D / 2;
     using Raw = typename KVRaw<DL>::type;
-    const int S = p.att_splits, G = p.hq / p.hkv, units = p.hkv * S;
+    const int S = p.att_splits, G = p.hq / p.hkv, GU = p.att_group, units = p.hq / GU * S;
     const int GRID = gridDim.x;
     const int ctid = cw * 32 + lane;
     __half* kp = p.kpool + l * p.kv_layer_stride;
@@ -966,14 +969,15 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
     float* ks = scr + MAXG * D;           // [D] new key (fp16-rounded)
     float* vs = scr + (MAXG + 1) * D;     // [D] new value (fp16-rounded)
     constexpr int MS = D + 4;             // a warp's merge row: o[D], max, sum (16-byte aligned rows)
-    float* merge = scr + (MAXG + 2) * D;  // [NW][G][MS]
+    float* merge = scr + (MAXG + 2) * D;  // [NW][GU][MS]
     bool traced = false;
     // the units u with unit_cta(u) == this CTA: [ceil(me units / GRID), ceil((me + 1) units / GRID))
     const unsigned me = blockIdx.x;
     const int u_begin = static_cast<int>((me * units + GRID - 1) / static_cast<unsigned>(GRID));
     const int u_end = static_cast<int>(((me + 1) * units + GRID - 1) / static_cast<unsigned>(GRID));
     for (int u = u_begin; u < u_end; ++u) {
-        const int j = u / S, s = u % S;
+        // heads h .. h + GU - 1 (all of kv head j's, or one), split s
+        const int h = u / S * GU, s = u % S, j = h / G, gs = h % G;
         const int kb = s * chunk, ke = min(nvis, kb + chunk);
         const bool owns_new = pos >= kb && pos < ke;
         // -- loads that do not depend on this step's q/k/v: RoPE row, norm weights, cached keys
@@ -982,11 +986,11 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
 #pragma unroll
         for (int q = 0; q < DL; ++q) {
             cs[q] = ld_ahead_f2(p.rope_cs + static_cast<size_t>(pos) * HALF + (lane * DL + q) % HALF);
-            nw[q] = ld_ahead_f32((cw < G ? ly.q_norm : ly.k_norm) + lane * DL + q);
+            nw[q] = ld_ahead_f32((cw < GU ? ly.q_norm : ly.k_norm) + lane * DL + q);
         }
         // the page of the new position (the warp that appends k and v)
         const int page_new =
-            (cw == G && owns_new) ? static_cast<int>(ld_ahead_u32(p.page_table + pos / p.page_tokens)) : 0;
+            (cw == GU && owns_new && gs == 0) ? static_cast<int>(ld_ahead_u32(p.page_table + pos / p.page_tokens)) : 0;
         Raw kraw[KPF], vraw[KPF];
         const int key0 = kb + cw;
 #pragma unroll
@@ -1006,11 +1010,11 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
             }
         }
         // -- this layer's q (and, for the split holding the new position, k and v) rows
-        if (cw < G || (cw == G && owns_new)) {
-            const int hrow = cw < G ? (j * G + cw) * D : (p.hq + j) * D;
+        if (cw < GU || (cw == GU && owns_new)) {
+            const int hrow = cw < GU ? (h + cw) * D : (p.hq + j) * D;
             float v[DL], vv[DL];
             poll_words<DL, 1>(qkvw + hrow + lane * DL, tq, v, p.err);
-            if (cw == G) poll_words<DL, 1>(qkvw + (p.hq + p.hkv + j) * D + lane * DL, tq, vv, p.err);
+            if (cw == GU) poll_words<DL, 1>(qkvw + (p.hq + p.hkv + j) * D + lane * DL, tq, vv, p.err);
             if (!traced) {
                 MK_TR(l, 21);
                 traced = true;
@@ -1031,9 +1035,10 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                 o[q] = first ? (v[q] * cs[q].x - partner * cs[q].y) : (partner * cs[q].y + v[q] * cs[q].x);
             }
             MK_TR(l, 32);
-            if (cw < G) {
+            if (cw < GU) {
                 st_row<DL>(qs + cw * D + lane * DL, o);
             } else {
+                // every unit of kv head j rounds the new k and v the same way; the first appends them
                 const size_t off =
                     ((static_cast<size_t>(page_new) * p.hkv + j) * p.page_tokens + pos % p.page_tokens) * D +
                     lane * DL;
@@ -1041,8 +1046,10 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
 #pragma unroll
                 for (int q = 0; q < DL; ++q) {
                     const __half kh = __float2half_rn(o[q]), vh = __float2half_rn(vv[q]);
-                    kp[off + q] = kh;
-                    vp[off + q] = vh;
+                    if (gs == 0) {
+                        kp[off + q] = kh;
+                        vp[off + q] = vh;
+                    }
                     kr[q] = __half2float(kh);
                     vr[q] = __half2float(vh);
                 }
@@ -1062,7 +1069,7 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                 o[g][q] = 0.0f;
                 qr[g][q] = 0.0f;
             }
-            if (g < G) ld_row<DL>(qs + g * D + lane * DL, qr[g]);
+            if (g < GU) ld_row<DL>(qs + g * D + lane * DL, qr[g]);
         }
         for (int base = key0; base < ke; base += NW * KPF) {
             if (base != key0) {
@@ -1105,7 +1112,7 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                 if (base == key0 && i0 == 0) MK_TR(l, 33);
 #pragma unroll
                 for (int g = 0; g < MAXG; ++g) {
-                    if (g >= G) break;
+                    if (g >= GU) break;
                     float d[KB];
 #pragma unroll
                     for (int bb = 0; bb < KB; ++bb) {
@@ -1146,8 +1153,8 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
         // lsum dynamically and move them to local memory
 #pragma unroll
         for (int g = 0; g < MAXG; ++g) {
-            if (g >= G) break;
-            float* mr = merge + (cw * G + g) * MS;
+            if (g >= GU) break;
+            float* mr = merge + (cw * GU + g) * MS;
             st_row<DL>(mr + lane * DL, o[g]);
             if (lane == 0) {
                 mr[D] = m[g];
@@ -1157,17 +1164,18 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
         MK_TR(l, 24);
         nbar();
         MK_TR(l, 25);
-        unsigned long long* part = p.part + (static_cast<size_t>(j) * S + s) * G * (D + 2);
+        // partials [hkv][S][G][D + 2]: this head's at (j, s, gs)
+        unsigned long long* part = p.part + ((static_cast<size_t>(j) * S + s) * G + gs) * (D + 2);
         // each warp's weight in the merge, once per (warp, head): f = exp(m_w - M), and the sum L
         float* fw = ks;  // [G][NW] (the new key is no longer needed)
-        if (cw < G) {
+        if (cw < GU) {
             const int g = cw;
-            const float mw = lane < NW ? merge[(lane * G + g) * MS + D] : -INFINITY;
+            const float mw = lane < NW ? merge[(lane * GU + g) * MS + D] : -INFINITY;
             float M = mw;
 #pragma unroll
             for (int o2 = 4; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
             const float f = (lane < NW && mw != -INFINITY) ? expf(mw - M) : 0.0f;
-            float L = lane < NW ? merge[(lane * G + g) * MS + D + 1] * f : 0.0f;
+            float L = lane < NW ? merge[(lane * GU + g) * MS + D + 1] * f : 0.0f;
 #pragma unroll
             for (int o2 = 4; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
             if (lane < NW) fw[g * NW + lane] = f;
@@ -1178,14 +1186,14 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
         }
         nbar();
         MK_TR(l, 34);
-        for (int idx = ctid; idx < G * D; idx += CT) {
+        for (int idx = ctid; idx < GU * D; idx += CT) {
             const int g = idx / D, d = idx % D;
             const float M = vs[2 * g], L = vs[2 * g + 1];
             float acc = 0.0f;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) acc += merge[(w * G + g) * MS + d] * fw[g * NW + w];
+            for (int w = 0; w < NW; ++w) acc += merge[(w * GU + g) * MS + d] * fw[g * NW + w];
             if (S == 1) {
-                st_word(attw + (static_cast<size_t>(j) * G + g) * D + d, L > 0.0f ? acc / L : 0.0f, ta);
+                st_word(attw + static_cast<size_t>(h + g) * D + d, L > 0.0f ? acc / L : 0.0f, ta);
             } else {
                 st_word(part + g * (D + 2) + d, acc, ta);
                 if (d == 0) {
@@ -1201,22 +1209,22 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
     // every unit of this CTA has written its own partials, so no unit waits on a later one)
     if (S > 1) {
         const int sstride = G * (D + 2);  // words between the same entry of consecutive splits
-        float* mq = scr;                  // [G][S] split maxima, then [G][S] split sums
+        float* mq = scr;                  // [GU][32] split maxima, then [GU][32] split sums
         float* lq = scr + MAXG * 32;
         for (int u = u_begin; u < u_end; ++u) {
             if (u % S != 0) continue;
-            const int j = u / S;
-            const unsigned long long* hp = p.part + static_cast<size_t>(j) * S * sstride;
+            const int h = u / S * GU, j = h / G, gs = h % G;
+            const unsigned long long* hp = p.part + static_cast<size_t>(j) * S * sstride + gs * (D + 2);
             // (max, sum) of every split and head: one thread per pair, both words in one round
-            if (ctid < S * G) {
-                const int q = ctid / G, g = ctid % G;
+            if (ctid < S * GU) {
+                const int q = ctid / GU, g = ctid % GU;
                 float ml[2];
                 poll_words<2, 1>(hp + q * sstride + g * (D + 2) + D, ta, ml, p.err);
                 mq[g * 32 + q] = ml[0];
                 lq[g * 32 + q] = ml[1];
             }
             nbar();
-            for (int idx = ctid; idx < G * D; idx += CT) {
+            for (int idx = ctid; idx < GU * D; idx += CT) {
                 const int g = idx / D, d = idx % D;
                 float M = -INFINITY;
                 for (int q = 0; q < S; ++q) M = fmaxf(M, mq[g * 32 + q]);
@@ -1234,7 +1242,7 @@ __device__ __forceinline__ void attention_phase(const MKParams& p, Smem& sm, con
                         }
                     }
                 }
-                st_word(attw + (static_cast<size_t>(j) * G + g) * D + d, L > 0.0f ? acc / L : 0.0f, ta);
+                st_word(attw + static_cast<size_t>(h + g) * D + d, L > 0.0f ? acc / L : 0.0f, ta);
             }
             nbar();
         }
@@ -1585,18 +1593,23 @@ size_t mk_part_words(int hq, int hkv, int D, int splits) {
     return static_cast<size_t>(hkv) * splits * (hq / hkv) * (D + 2);
 }
 
-int mk_att_splits(int max_ctx, int hkv, int grid) {
+int mk_att_plan(int max_ctx, int hq, int hkv, int grid, int* group) {
     // up to UNIT_KEYS keys per unit, at most one unit per CTA, at most 32 splits (the combine's
-    // shared arrays)
-    int S = (max_ctx + UNIT_KEYS - 1) / UNIT_KEYS;
-    return std::max(1, std::min(std::min(S, grid / hkv), 32));
+    // shared arrays).  One query head per unit while that still leaves every unit at most UNIT_KEYS
+    // keys (measured 4 % faster per batch-1 step at short contexts: half the work per unit, twice
+    // the units); beyond that every query head of a kv head per unit, which allows twice the splits.
+    const int need = (max_ctx + UNIT_KEYS - 1) / UNIT_KEYS;
+    const bool per_head = need <= grid / hq;
+    *group = per_head ? 1 : hq / hkv;
+    const int units_per_split = per_head ? hq : hkv;
+    return std::max(1, std::min(std::min(need, grid / units_per_split), 32));
 }
 
 bool mk_supported(int L, int H, int I, int hq, int hkv, int D, int V, int wfmt, int efmt, int grid) {
     if (L < 1 || L > LMAX) return false;
     void (*fn)(MKParams) = nullptr;
     if (!kernel_for(wfmt, efmt, H, hq * D, I, D, &fn)) return false;
-    if (hq % hkv != 0 || hq / hkv > MAXG || hkv > grid || grid > 256) return false;
+    if (hq % hkv != 0 || hq / hkv > MAXG || hq > grid || grid > 256) return false;
     if (V % 8 != 0 || V < 8) return false;
     // quantised slices must hold whole groups
     const int g = wfmt == WF_I8G64 ? 64 : wfmt == WF_I4G32 ? 32 : 16;

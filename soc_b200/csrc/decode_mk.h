@@ -50,6 +50,7 @@ struct MKParams {
     unsigned long long* best;  // [steps][grid] per-CTA argmax keys (zero = not yet written)
     int* err;
     int att_splits;
+    int att_group;  // query heads per attention unit (mk_att_plan)
     int inflight;  // ring chunks the producer keeps in flight (1 .. ring slots)
     // optional phase trace of the first step (nullptr = off): %globaltimer stamps,
     // [grid][mk_trace_stride(L)]; slots in decode_mk.cu
@@ -70,8 +71,9 @@ inline unsigned long long mk_tags_per_launch(int steps, int L) {
 size_t mk_vec_words(int H, int I, int hq, int hkv, int D);
 // Words of the split-K attention partials for `splits` key splits.
 size_t mk_part_words(int hq, int hkv, int D, int splits);
-// Key splits of the attention for contexts up to max_ctx on a grid of `grid` CTAs.
-int mk_att_splits(int max_ctx, int hkv, int grid);
+// Key splits of the attention for contexts up to max_ctx on a grid of `grid` CTAs, and the query
+// heads per attention unit (*group: 1, or hq / hkv).
+int mk_att_plan(int max_ctx, int hq, int hkv, int grid, int* group);
 // Whether the persistent kernel supports this shape on a grid of `grid` CTAs.
 bool mk_supported(int L, int H, int I, int hq, int hkv, int D, int V, int wfmt, int efmt, int grid);
 int mk_grid(int device);

@@ -1011,7 +1011,8 @@ __global__ void k_step_end_loop(soc_model::LoopState* st, const int* next, cudaG
 
 // Parameters of one persistent-kernel launch (decode_mk.cu) over the buffers given.
 MKParams mk_params(const soc_model* m, const soc_kv* kv, int seq, int start, int steps, int* d_ids, float* logits,
-                   int eos, int splits, unsigned long long* vec, unsigned long long* part, unsigned long long* best,
+                   int eos, int splits, int group, unsigned long long* vec, unsigned long long* part,
+                   unsigned long long* best,
                    unsigned tag0) {
     const Config& c = m->cfg;
     MKParams p{};
@@ -1049,6 +1050,7 @@ MKParams mk_params(const soc_model* m, const soc_kv* kv, int seq, int start, int
     p.best = best;
     p.err = m->ctx->d_err;
     p.att_splits = splits;
+    p.att_group = group;
     // ring chunks in flight (SOC_B200_MK_INFLIGHT, default 2)
     static const int inflight = [] {
         const char* e = std::getenv("SOC_B200_MK_INFLIGHT");
@@ -1089,7 +1091,8 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
         m->mk_best = static_cast<unsigned long long*>(
             m->dmalloc(sizeof(unsigned long long) * m->mk_best_n * m->mk_grid));
     }
-    const int S = mk_att_splits(start + steps, hkv, m->mk_grid);
+    int group = 1;
+    const int S = mk_att_plan(start + steps, static_cast<int>(c.hq), hkv, m->mk_grid, &group);
     const size_t part = S > 1 ? mk_part_words(static_cast<int>(c.hq), hkv, static_cast<int>(c.hd), S) : 0;
     if (part > m->mk_part_n) {
         // a new buffer starts zeroed: no stale tags
@@ -1101,7 +1104,8 @@ void run_mk(soc_model* m, soc_kv* kv, int seq, int start, int steps, int* d_ids,
     SOCB_CUDA(cudaMemsetAsync(m->mk_best, 0, sizeof(unsigned long long) * steps * m->mk_grid, st));
     const unsigned tag0 = mk_next_tags(&m->mk_tag, steps, static_cast<int>(c.layers), m->mk_vec, m->mk_vec_n,
                                        m->mk_part, m->mk_part_n, st);
-    MKParams p = mk_params(m, kv, seq, start, steps, d_ids, logits, eos, S, m->mk_vec, m->mk_part, m->mk_best, tag0);
+    MKParams p =
+        mk_params(m, kv, seq, start, steps, d_ids, logits, eos, S, group, m->mk_vec, m->mk_part, m->mk_best, tag0);
     // Optional phase trace (SOC_B200_MK_TRACE=<file>): raw u64 %globaltimer stamps of the first step.
     const char* trace_path = std::getenv("SOC_B200_MK_TRACE");
     unsigned long long* trace = nullptr;
@@ -2064,7 +2068,8 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         if (pos == 0) throw Error(SOC_B200_ERR_INVALID, "GenerationContext decode requires a prefilled KV cache");
         if (pos + 1 > m->rope_len) throw Error(SOC_B200_ERR_CAPACITY, "decode position beyond the RoPE table");
 
-        const int S = mk_att_splits(pos + 1, hkv, grid);
+        int group = 1;
+        const int S = mk_att_plan(pos + 1, hq, hkv, grid, &group);
         // carve the array (256-byte aligned pieces); every check comes before any side effect
         char* base = static_cast<char*>(noalloc_scratch(m->ctx->device));
         size_t off = 0;
@@ -2091,7 +2096,7 @@ extern "C" int soc_b200_decode_noalloc(soc_model* m, soc_kv* kv, int seq, int32_
         // tags keep growing across calls on this device's array (whatever model made them), so a
         // word left by an earlier call never carries a tag this call waits for
         const unsigned tag0 = noalloc_tags(m->ctx->device, 1, static_cast<int>(c.layers), vec, nvec, part, npart, st);
-        MKParams p = mk_params(m, kv, seq, pos, 1, ids, lg, -1, S, vec, part, best, tag0);
+        MKParams p = mk_params(m, kv, seq, pos, 1, ids, lg, -1, S, group, vec, part, best, tag0);
         mk_launch(p, grid, st);
         count_launches(1);
         if (logits) SOCB_CUDA(cudaMemcpyAsync(logits, lg, sizeof(float) * V, cudaMemcpyDeviceToHost, st));

@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(AP_THREADS) k_attn_pages(const float* __restri
                                                           const int* __restrict__ row_pos, int hq, int hkv,
                                                           KVLayerView kv, int n_splits, float* __restrict__ out,
                                                           float* __restrict__ part, int* err) {
+    pdl_enter();
     constexpr int PT = 16;                    // tokens per page
     constexpr int PAGE_B = PT * D * 2;        // bytes of one kv head's K (or V) page
     constexpr int LPK = (G >= 4 && D >= 128) ? 16 : 8, DPL = D / LPK, NV = DPL / 8;
@@ -277,6 +278,7 @@ __global__ void __launch_bounds__(AP_THREADS) k_attn_pages_mma(const float* __re
                                                               float* __restrict__ part,
                                                               const __grid_constant__ CUtensorMap tk,
                                                               const __grid_constant__ CUtensorMap tv, int* err) {
+    pdl_enter();
     constexpr int PT = 16, PAGE_B = PT * D * 2, KS = D / 16;
     // Page i goes to slot i % NSLOT and warp i % CW; NSLOT a multiple of CW keeps every slot
     // with one warp, so no warp can wait on a slot's phase parity two phases ahead.
@@ -528,8 +530,8 @@ void pages_dg(dim3 grid, const float* q, const Rows& rows, int hq, int hkv, cons
             SOCB_CUDA(cudaFuncSetAttribute(k_attn_pages_mma<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_m));
             set_m = true;
         }
-        k_attn_pages_mma<D, G><<<grid, AP_THREADS, smem_m, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out,
-                                                                 scratch, *kv.tmk, *kv.tmv, err);
+        launch_pdl(k_attn_pages_mma<D, G>, dim3(grid), dim3(AP_THREADS), smem_m, st, q, rows.seq, rows.pos, hq, hkv,
+                   kv, splits, out, scratch, *kv.tmk, *kv.tmv, err);
         return;
     }
     constexpr int LPK = (G >= 4 && D >= 128) ? 16 : 8;
@@ -540,7 +542,8 @@ void pages_dg(dim3 grid, const float* q, const Rows& rows, int hq, int hkv, cons
         SOCB_CUDA(cudaFuncSetAttribute(k_attn_pages<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         set = true;
     }
-    k_attn_pages<D, G><<<grid, AP_THREADS, smem, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out, scratch, err);
+    launch_pdl(k_attn_pages<D, G>, dim3(grid), dim3(AP_THREADS), smem, st, q, rows.seq, rows.pos, hq, hkv, kv, splits,
+               out, scratch, err);
 }
 
 template <int D>

@@ -50,6 +50,7 @@ template <int D>
 __global__ void __launch_bounds__(FW * 32) k_flash_prefill(const float* __restrict__ q, int n, int hq, int hkv,
                                                            int seq, int start, KVLayerView kv, float qscale,
                                                            float* __restrict__ out) {
+    pdl_enter();
     constexpr int CH = D / 8;              // 16-byte chunks per key row
     constexpr int TILE = FK * D * 2;       // bytes of one K (or V) block
     extern __shared__ __align__(128) uint8_t fsm[];
@@ -239,7 +240,7 @@ void flash_d(const float* q, int n, int hq, int hkv, int seq, int start, const K
     }
     const float qscale = 1.4426950408889634f / sqrtf(static_cast<float>(D));
     dim3 grid((n + FQ - 1) / FQ, hq);
-    k_flash_prefill<D><<<grid, FW * 32, smem, st>>>(q, n, hq, hkv, seq, start, kv, qscale, out);
+    launch_pdl(k_flash_prefill<D>, dim3(grid), dim3(FW * 32), smem, st, q, n, hq, hkv, seq, start, kv, qscale, out);
 }
 
 }  // namespace

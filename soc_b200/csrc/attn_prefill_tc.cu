@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
     k_flash_prefill_tc(const float* __restrict__ q, int n, int hq, int hkv, int seq, int start, KVLayerView kv,
                        float qscale, float* __restrict__ out, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, int* err) {
+    pdl_enter();
     constexpr int QR = D / 64;                // regions of a Q / K / V row
     constexpr int KV_BYTES = QR * REGION;     // one K (or V) block of 128 keys
     constexpr int O_COL = TBN;                // O accumulator columns [128, 128 + D)
@@ -369,8 +370,8 @@ void flash_tc_d(const float* q, int n, int hq, int hkv, int seq, int start, cons
     }
     const float qscale = 1.4426950408889634f / sqrtf(static_cast<float>(D));
     dim3 grid(hq, (n + TBM - 1) / TBM);
-    k_flash_prefill_tc<D><<<grid, T_THREADS, smem, st>>>(q, n, hq, hkv, seq, start, kv, qscale, out, *kv.tmk,
-                                                          *kv.tmv, err);
+    launch_pdl(k_flash_prefill_tc<D>, dim3(grid), dim3(T_THREADS), smem, st, q, n, hq, hkv, seq, start, kv, qscale,
+               out, *kv.tmk, *kv.tmv, err);
 }
 
 }  // namespace

@@ -28,6 +28,34 @@ void set_last_error(const std::string& message);
                                     __FILE__ + ":" + std::to_string(__LINE__) + " (" #expr ")");  \
     } while (0)
 
+// Programmatic dependent launch.  The modular kernels start with pdl_enter(): they wait until the
+// kernel before them in the stream has completed and its memory is visible (before touching any
+// memory), then let the next kernel launch.  Launched with launch_pdl, a kernel's launch and CTA
+// scheduling overlap the tail of the one before it; launched normally, the wait returns at once.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Whether launch_pdl asks for programmatic serialization (SOC_B200_PDL=0 turns it off).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SOCB_CUDA(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 // Weight element formats of the linear layers.
 enum WFmt : int { WF_F16 = 1, WF_BF16 = 2, WF_I8G64 = 3, WF_I4G32 = 4 };
 

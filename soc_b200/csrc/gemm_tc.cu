@@ -244,6 +244,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               const __grid_constant__ CUtensorMap tw, int M, int N, int K, void* __restrict__ y,
               void* __restrict__ y_lo, int ldy, int mode, int out_half, int ksplit,
               const __grid_constant__ CUtensorMap ty, int out_tma, int* err) {
+    pdl_enter();
     using Cfg = TcCfg<SPLIT>;
     constexpr int STAGES = Cfg::STAGES, STAGE_BYTES = Cfg::STAGE_BYTES, W_OFF = Cfg::A_TILES * A_BYTES;
     extern __shared__ uint8_t smem_raw[];
@@ -414,6 +415,7 @@ template <typename T>
 __global__ void __launch_bounds__(1024) k_rows_to_half(const float* __restrict__ x, int ldx, int cols,
                                                        const float* __restrict__ w, float eps, T* __restrict__ out,
                                                        T* __restrict__ out_lo, int ldo) {
+    pdl_enter();
     __shared__ float red[32];
     __shared__ float scale;
     const float* xr = x + static_cast<size_t>(blockIdx.x) * ldx;
@@ -473,6 +475,7 @@ __global__ void __launch_bounds__(1024) k_rows_to_half(const float* __restrict__
 template <int F, typename T>
 __global__ void k_dequant(const uint8_t* __restrict__ W, const __half* __restrict__ S, size_t rows, int cols,
                           T* __restrict__ out) {
+    pdl_enter();
     using C = Codec<F>;
     const size_t vpr = static_cast<size_t>(cols) / C::EPV, total = rows * vpr;
     const int ng = cols / C::GROUP;
@@ -504,6 +507,7 @@ __global__ void k_dequant(const uint8_t* __restrict__ W, const __half* __restric
 template <typename T>
 __global__ void k_splitk_reduce(const float* __restrict__ ws, int ksplit, int M, int N, void* __restrict__ y,
                                 void* __restrict__ y_lo, int ldy, int mode, int out_half) {
+    pdl_enter();
     const size_t pairs = static_cast<size_t>(M) * (N / 2);
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < pairs;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -639,16 +643,17 @@ static void gemm_t(const CUtensorMap& a, const CUtensorMap& a_lo, const CUtensor
     CUtensorMap ty{};
     if (ksplit <= 1) {
         const bool tma = !out_half && mode != LIN_SWIGLU && tc_out_tma() && make_out_map(&ty, y, M, N, ldy, 1);
-        k_gemm_tc<T, SPLIT><<<grid, TC_THREADS, TC_SMEM, st>>>(a, a_lo, w, M, N, K, y, y_lo, ldy, mode,
-                                                               out_half ? 1 : 0, 1, ty, tma ? 1 : 0, err);
+        launch_pdl(k_gemm_tc<T, SPLIT>, dim3(grid), dim3(TC_THREADS), TC_SMEM, st, a, a_lo, w, M, N, K, y, y_lo, ldy,
+                   mode, out_half ? 1 : 0, 1, ty, tma ? 1 : 0, err);
         return;
     }
     const bool tma = tc_out_tma() && make_out_map(&ty, ws, M, N, N, ksplit);
-    k_gemm_tc<T, SPLIT><<<grid, TC_THREADS, TC_SMEM, st>>>(a, a_lo, w, M, N, K, ws, nullptr, N, LIN_STORE, 0, ksplit,
-                                                           ty, tma ? 1 : 0, err);
+    launch_pdl(k_gemm_tc<T, SPLIT>, dim3(grid), dim3(TC_THREADS), TC_SMEM, st, a, a_lo, w, M, N, K, ws, nullptr, N,
+               LIN_STORE, 0, ksplit, ty, tma ? 1 : 0, err);
     const size_t pairs = static_cast<size_t>(M) * (N / 2);
     const int rgrid = static_cast<int>(std::min<size_t>((pairs + 255) / 256, 148 * 16));
-    k_splitk_reduce<T><<<rgrid, 256, 0, st>>>(ws, ksplit, M, N, y, y_lo, ldy, mode, out_half ? 1 : 0);
+    launch_pdl(k_splitk_reduce<T>, dim3(rgrid), dim3(256), 0, st, ws, ksplit, M, N, y, y_lo, ldy, mode,
+               out_half ? 1 : 0);
 }
 
 void launch_gemm_tc(int wfmt, const CUtensorMap& a, const CUtensorMap* a_lo, const CUtensorMap& w, int M, int N,
@@ -704,12 +709,12 @@ void launch_rows_to_half(int wfmt, const float* x, int ldx, int rows, int cols, 
     if (threads > 1024) throw Error(-1, "row conversion supports at most 16384 columns");
     if (threads < 32) threads = 32;
     if (wfmt == WF_BF16)
-        k_rows_to_half<__nv_bfloat16><<<rows, threads, 0, st>>>(x, ldx, cols, norm_w, eps,
+        launch_pdl(k_rows_to_half<__nv_bfloat16>, dim3(rows), dim3(threads), 0, st, x, ldx, cols, norm_w, eps,
                                                                 static_cast<__nv_bfloat16*>(out),
                                                                 static_cast<__nv_bfloat16*>(out_lo), ldo);
     else
-        k_rows_to_half<__half><<<rows, threads, 0, st>>>(x, ldx, cols, norm_w, eps, static_cast<__half*>(out),
-                                                         static_cast<__half*>(out_lo), ldo);
+        launch_pdl(k_rows_to_half<__half>, dim3(rows), dim3(threads), 0, st, x, ldx, cols, norm_w, eps,
+                   static_cast<__half*>(out), static_cast<__half*>(out_lo), ldo);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }
@@ -719,11 +724,11 @@ void launch_dequant(int wfmt, const void* W, const void* scales, int rows, int c
     const int grid = 148 * 8;
     if (out_fmt != WF_F16) throw Error(-1, "dequantisation writes fp16");
     if (wfmt == WF_I8G64)
-        k_dequant<WF_I8G64, __half><<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(W),
+        launch_pdl(k_dequant<WF_I8G64, __half>, dim3(grid), dim3(256), 0, st, static_cast<const uint8_t*>(W),
                                                           static_cast<const __half*>(scales), rows, cols,
                                                           static_cast<__half*>(out));
     else if (wfmt == WF_I4G32)
-        k_dequant<WF_I4G32, __half><<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(W),
+        launch_pdl(k_dequant<WF_I4G32, __half>, dim3(grid), dim3(256), 0, st, static_cast<const uint8_t*>(W),
                                                           static_cast<const __half*>(scales), rows, cols,
                                                           static_cast<__half*>(out));
     else

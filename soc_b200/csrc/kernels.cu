@@ -23,6 +23,14 @@ static std::atomic<long long> g_launches{0};
 void count_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 long long launches_so_far() { return g_launches.load(std::memory_order_relaxed); }
 
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("SOC_B200_PDL");
+        return !(e && std::string(e) == "0");
+    }();
+    return on;
+}
+
 // ------------------------------------------------------------------------ helpers
 __device__ __forceinline__ uint4 ld_nc16(const void* p) {
     uint4 r;
@@ -44,6 +52,7 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&w)[8]) {
 template <typename T>
 __global__ void k_embed(const T* __restrict__ table, int H, int V, const int* __restrict__ tokens,
                         float* __restrict__ h, int* err) {
+    pdl_enter();
     const int row = blockIdx.x;
     const int tok = tokens[row];
     float* out = h + static_cast<size_t>(row) * H;
@@ -65,10 +74,11 @@ void launch_embed(int wfmt, const void* table, int hidden, int vocab, const int*
                   int* err, cudaStream_t st) {
     if (rows <= 0) return;
     if (wfmt == WF_BF16)
-        k_embed<__nv_bfloat16><<<rows, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(table), hidden, vocab,
-                                                      tokens, h, err);
+        launch_pdl(k_embed<__nv_bfloat16>, dim3(rows), dim3(128), 0, st, static_cast<const __nv_bfloat16*>(table),
+                   hidden, vocab, tokens, h, err);
     else
-        k_embed<__half><<<rows, 128, 0, st>>>(static_cast<const __half*>(table), hidden, vocab, tokens, h, err);
+        launch_pdl(k_embed<__half>, dim3(rows), dim3(128), 0, st, static_cast<const __half*>(table), hidden, vocab,
+                   tokens, h, err);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }
@@ -76,6 +86,7 @@ void launch_embed(int wfmt, const void* table, int hidden, int vocab, const int*
 // ----------------------------------------------------------------------- RMSNorm
 __global__ void k_rmsnorm(const float* __restrict__ x, int n, const float* __restrict__ w, float eps,
                           float* __restrict__ y) {
+    pdl_enter();
     __shared__ float red[32];
     const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
     float* yr = y + static_cast<size_t>(blockIdx.x) * n;
@@ -96,7 +107,7 @@ __global__ void k_rmsnorm(const float* __restrict__ x, int n, const float* __res
 
 void launch_rmsnorm(const float* x, int rows, int n, const float* w, float eps, float* y, cudaStream_t st) {
     if (rows <= 0) return;
-    k_rmsnorm<<<rows, 256, 0, st>>>(x, n, w, eps, y);
+    launch_pdl(k_rmsnorm, dim3(rows), dim3(256), 0, st, x, n, w, eps, y);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }
@@ -131,6 +142,7 @@ __global__ void __launch_bounds__(LIN_THREADS) k_linear(const uint8_t* __restric
                                                         int out_f, int in_f, const float* __restrict__ x, int ldx,
                                                         int rows, const float* __restrict__ norm_w, float eps,
                                                         float* __restrict__ y, int ldy, int mode) {
+    pdl_enter();
     using C = Codec<F>;
     constexpr int EPV = C::EPV, NP = EPV / 8, G = C::GROUP;
     extern __shared__ float4 xs4[];
@@ -297,7 +309,7 @@ static void linear_rb(const void* W, const void* S, int out_f, int in_f, const f
     }
     const int groups = (out_f + NWR - 1) / NWR;
     dim3 grid((groups + LIN_WARPS - 1) / LIN_WARPS, (rows + RB - 1) / RB);
-    k_linear<F, RB, NWR><<<grid, LIN_THREADS, smem, st>>>(static_cast<const uint8_t*>(W),
+    launch_pdl(k_linear<F, RB, NWR>, dim3(grid), dim3(LIN_THREADS), smem, st, static_cast<const uint8_t*>(W),
                                                           static_cast<const __half*>(S), out_f, in_f, x, ldx, rows,
                                                           norm_w, eps, y, ldy, mode);
     SOCB_CUDA(cudaGetLastError());
@@ -351,6 +363,7 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope_kv(const float* __restrict
                                                          const int* __restrict__ row_seq,
                                                          const int* __restrict__ row_pos, KVLayerView kv,
                                                          float* __restrict__ q_out, int* err) {
+    pdl_enter();
     constexpr int DL = D / 32;
     constexpr int HALF = D / 2;
     const int row = blockIdx.x;
@@ -417,11 +430,11 @@ void launch_qk_norm_rope_kv(const float* qkv, const Rows& rows, int hq, int hkv,
                             float* q_out, int* err, cudaStream_t st) {
     if (rows.n <= 0) return;
     if (head_dim == 128)
-        k_qk_norm_rope_kv<128><<<rows.n, 256, 0, st>>>(qkv, hq, hkv, qn_w, kn_w, eps, rope_cs, rope_len, rows.seq,
-                                                       rows.pos, kv, q_out, err);
+        launch_pdl(k_qk_norm_rope_kv<128>, dim3(rows.n), dim3(256), 0, st, qkv, hq, hkv, qn_w, kn_w, eps, rope_cs,
+                   rope_len, rows.seq, rows.pos, kv, q_out, err);
     else if (head_dim == 64)
-        k_qk_norm_rope_kv<64><<<rows.n, 256, 0, st>>>(qkv, hq, hkv, qn_w, kn_w, eps, rope_cs, rope_len, rows.seq,
-                                                      rows.pos, kv, q_out, err);
+        launch_pdl(k_qk_norm_rope_kv<64>, dim3(rows.n), dim3(256), 0, st, qkv, hq, hkv, qn_w, kn_w, eps, rope_cs,
+                   rope_len, rows.seq, rows.pos, kv, q_out, err);
     else
         throw Error(-1, "head_dim must be 64 or 128");
     SOCB_CUDA(cudaGetLastError());
@@ -442,6 +455,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attention(const float* __res
                                                               const int* __restrict__ row_pos, int hq, int hkv,
                                                               KVLayerView kv, int n_splits,
                                                               float* __restrict__ out, float* __restrict__ part) {
+    pdl_enter();
     constexpr int DL = D / 32;
     __shared__ float sm_m[ATT_WARPS][ATT_MAXG], sm_l[ATT_WARPS][ATT_MAXG];
     __shared__ float sm_o[ATT_WARPS][ATT_MAXG][D];
@@ -540,6 +554,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attention(const float* __res
 
 template <int D>
 __global__ void k_attn_combine(const float* __restrict__ part, int hq, int n_splits, float* __restrict__ out) {
+    pdl_enter();
     const int row = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
     const float* pp = part + (static_cast<size_t>(row) * hq + h) * n_splits * (D + 2);
     float M = -INFINITY;
@@ -567,6 +582,7 @@ template <int D, int G>
 __global__ void __launch_bounds__(128) k_attn_rows(const float* __restrict__ q, const int* __restrict__ row_seq,
                                                    const int* __restrict__ row_pos, int hq, int hkv, KVLayerView kv,
                                                    int n_splits, float* __restrict__ out, float* __restrict__ part) {
+    pdl_enter();
     constexpr int LPK = (G >= 4 && D >= 128) ? 16 : 8, DPL = D / LPK, KPW = 32 / LPK, NW = 4, NS = NW * KPW;
     constexpr int NV = DPL / 8;  // 16-byte vectors per lane per key row
     __shared__ float sm_m[NS][G], sm_l[NS][G];
@@ -709,10 +725,14 @@ template <int D>
 static bool attn_rows_d(int G, dim3 grid, const float* q, const Rows& rows, int hq, int hkv, const KVLayerView& kv,
                         int splits, float* out, float* scratch, cudaStream_t st) {
     switch (G) {
-        case 1: k_attn_rows<D, 1><<<grid, 128, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out, scratch); return true;
-        case 2: k_attn_rows<D, 2><<<grid, 128, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out, scratch); return true;
-        case 4: k_attn_rows<D, 4><<<grid, 128, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out, scratch); return true;
-        case 8: k_attn_rows<D, 8><<<grid, 128, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out, scratch); return true;
+        case 1: launch_pdl(k_attn_rows<D, 1>, dim3(grid), dim3(128), 0, st, q, rows.seq, rows.pos, hq, hkv, kv, splits,
+                           out, scratch); return true;
+        case 2: launch_pdl(k_attn_rows<D, 2>, dim3(grid), dim3(128), 0, st, q, rows.seq, rows.pos, hq, hkv, kv, splits,
+                           out, scratch); return true;
+        case 4: launch_pdl(k_attn_rows<D, 4>, dim3(grid), dim3(128), 0, st, q, rows.seq, rows.pos, hq, hkv, kv, splits,
+                           out, scratch); return true;
+        case 8: launch_pdl(k_attn_rows<D, 8>, dim3(grid), dim3(128), 0, st, q, rows.seq, rows.pos, hq, hkv, kv, splits,
+                           out, scratch); return true;
         default: return false;
     }
 }
@@ -752,17 +772,20 @@ void launch_attention(const float* q, const Rows& rows, int splits, int hq, int 
     else if (!done && head_dim == 64) done = attn_rows_d<64>(G, grid, q, rows, hq, hkv, kv, splits, out, scratch, st);
     if (done) {
         if (splits > 1) {
-            if (head_dim == 128) k_attn_combine<128><<<dim3(rows.n, hq), 128, 0, st>>>(scratch, hq, splits, out);
-            else k_attn_combine<64><<<dim3(rows.n, hq), 64, 0, st>>>(scratch, hq, splits, out);
+            if (head_dim == 128) launch_pdl(k_attn_combine<128>, dim3(dim3(rows.n, hq)), dim3(128), 0, st, scratch, hq,
+                                            splits, out);
+            else launch_pdl(k_attn_combine<64>, dim3(dim3(rows.n, hq)), dim3(64), 0, st, scratch, hq, splits, out);
         }
     } else if (head_dim == 128) {
-        k_attention<128><<<grid, ATT_WARPS * 32, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out,
-                                                          scratch);
-        if (splits > 1) k_attn_combine<128><<<dim3(rows.n, hq), 128, 0, st>>>(scratch, hq, splits, out);
+        launch_pdl(k_attention<128>, dim3(grid), dim3(ATT_WARPS * 32), 0, st, q, rows.seq, rows.pos, hq, hkv, kv,
+                   splits, out, scratch);
+        if (splits > 1) launch_pdl(k_attn_combine<128>, dim3(dim3(rows.n, hq)), dim3(128), 0, st, scratch, hq, splits,
+                                   out);
     } else if (head_dim == 64) {
-        k_attention<64><<<grid, ATT_WARPS * 32, 0, st>>>(q, rows.seq, rows.pos, hq, hkv, kv, splits, out,
-                                                         scratch);
-        if (splits > 1) k_attn_combine<64><<<dim3(rows.n, hq), 64, 0, st>>>(scratch, hq, splits, out);
+        launch_pdl(k_attention<64>, dim3(grid), dim3(ATT_WARPS * 32), 0, st, q, rows.seq, rows.pos, hq, hkv, kv,
+                   splits, out, scratch);
+        if (splits > 1) launch_pdl(k_attn_combine<64>, dim3(dim3(rows.n, hq)), dim3(64), 0, st, scratch, hq, splits,
+                                   out);
     } else {
         throw Error(-1, "head_dim must be 64 or 128");
     }
@@ -852,6 +875,7 @@ constexpr int ARGMAX_COLS = ARGMAX_THREADS * 16;
 
 __global__ void __launch_bounds__(ARGMAX_THREADS) k_argmax(const float* __restrict__ logits, int V, int ld, int v_off,
                                                          float temp, unsigned long long* __restrict__ keys) {
+    pdl_enter();
     __shared__ unsigned long long red[ARGMAX_THREADS / 32];
     const float* row = logits + static_cast<size_t>(blockIdx.y) * ld;
     const int c0 = blockIdx.x * ARGMAX_COLS;
@@ -899,6 +923,7 @@ __global__ void __launch_bounds__(ARGMAX_THREADS) k_argmax(const float* __restri
 // keys_all [shards][rows] -> id of the largest key per row (ties: lowest global index).
 __global__ void k_argmax_merge(const unsigned long long* __restrict__ keys_all, int shards, int rows,
                                int* __restrict__ next_ids) {
+    pdl_enter();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     unsigned long long b = 0ull;
@@ -910,6 +935,7 @@ __global__ void k_argmax_merge(const unsigned long long* __restrict__ keys_all, 
 }
 
 __global__ void k_zero_keys(unsigned long long* keys, int n) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) keys[i] = 0ull;
 }
@@ -918,9 +944,9 @@ void launch_argmax_keys(const float* logits, int vocab, int ld, int rows, int v_
                         unsigned long long* keys, cudaStream_t st) {
     if (rows <= 0) return;
     // a kernel rather than a memset node, so that the step stays a graph of kernels only
-    k_zero_keys<<<(rows + 255) / 256, 256, 0, st>>>(keys, rows);
+    launch_pdl(k_zero_keys, dim3((rows + 255) / 256), dim3(256), 0, st, keys, rows);
     const dim3 grid((vocab + ARGMAX_COLS - 1) / ARGMAX_COLS, rows);
-    k_argmax<<<grid, ARGMAX_THREADS, 0, st>>>(logits, vocab, ld, v_off, temperature, keys);
+    launch_pdl(k_argmax, dim3(grid), dim3(ARGMAX_THREADS), 0, st, logits, vocab, ld, v_off, temperature, keys);
     SOCB_CUDA(cudaGetLastError());
     count_launches(2);
 }
@@ -934,7 +960,7 @@ void launch_argmax(const float* logits, int vocab, int ld, int rows, float tempe
 
 void launch_argmax_merge(const unsigned long long* keys_all, int shards, int rows, int* next_ids, cudaStream_t st) {
     if (rows <= 0) return;
-    k_argmax_merge<<<(rows + 127) / 128, 128, 0, st>>>(keys_all, shards, rows, next_ids);
+    launch_pdl(k_argmax_merge, dim3((rows + 127) / 128), dim3(128), 0, st, keys_all, shards, rows, next_ids);
     SOCB_CUDA(cudaGetLastError());
     count_launches(1);
 }
@@ -1013,6 +1039,7 @@ __device__ void bitonic1024_desc(unsigned long long& a0, unsigned long long& a1,
 __global__ void __launch_bounds__(TOPK_THREADS) k_topk_chunks(const float* __restrict__ base, int V, int seg_len,
                                                               size_t seg_stride, float temp, int k,
                                                               unsigned long long* __restrict__ cand) {
+    pdl_enter();
     __shared__ unsigned long long s[TOPK_CHUNK];
     const int first = blockIdx.x * TOPK_CHUNK;
     unsigned long long a[2];
@@ -1038,6 +1065,7 @@ __global__ void __launch_bounds__(TOPK_THREADS) k_topk_merge(const unsigned long
                                                              const float* __restrict__ base, int seg_len,
                                                              size_t seg_stride, float* __restrict__ top_logits,
                                                              int* __restrict__ top_ids) {
+    pdl_enter();
     __shared__ unsigned long long s[TOPK_CHUNK];
     const int l0 = blockIdx.x * TOPK_GROUP, nl = min(TOPK_GROUP, lists - l0);
     const int n = nl * k;  // <= 1,024; the rest of the 1,024 sorted keys are zero
@@ -1072,19 +1100,22 @@ void launch_topk(const float* base, int V, int seg_len, size_t seg_stride, float
                  unsigned long long* cand, float* top_logits, int* top_ids, cudaStream_t st) {
     if (k < 1 || k > TOPK_MAX || V < 1) throw Error(-2, "top-k: k out of range");
     int lists = (V + TOPK_CHUNK - 1) / TOPK_CHUNK;
-    k_topk_chunks<<<lists, TOPK_THREADS, 0, st>>>(base, V, seg_len, seg_stride, temperature, k, cand);
+    launch_pdl(k_topk_chunks, dim3(lists), dim3(TOPK_THREADS), 0, st, base, V, seg_len, seg_stride, temperature, k,
+               cand);
     int launches = 1;
     unsigned long long* in = cand;
     unsigned long long* out = cand + static_cast<size_t>(lists) * k;
     while (lists > TOPK_GROUP) {
         const int groups = (lists + TOPK_GROUP - 1) / TOPK_GROUP;
-        k_topk_merge<<<groups, TOPK_THREADS, 0, st>>>(in, lists, k, out, base, seg_len, seg_stride, nullptr, nullptr);
+        launch_pdl(k_topk_merge, dim3(groups), dim3(TOPK_THREADS), 0, st, in, lists, k, out, base, seg_len, seg_stride,
+                   nullptr, nullptr);
         ++launches;
         // the next round reads this one's lists and writes over the ones it just read
         std::swap(in, out);
         lists = groups;
     }
-    k_topk_merge<<<1, TOPK_THREADS, 0, st>>>(in, lists, k, nullptr, base, seg_len, seg_stride, top_logits, top_ids);
+    launch_pdl(k_topk_merge, dim3(1), dim3(TOPK_THREADS), 0, st, in, lists, k, nullptr, base, seg_len, seg_stride,
+               top_logits, top_ids);
     SOCB_CUDA(cudaGetLastError());
     count_launches(launches + 1);
 }

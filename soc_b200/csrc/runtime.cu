@@ -910,6 +910,15 @@ void logits_to_host(soc_model* m, int rows, float* host, cudaStream_t st) {
 constexpr int kPrefillChunk = 4096;
 constexpr int kPrefillGraphRows = 64;  // prefill chunks up to this many rows run as a cached graph
 
+// SOC_B200_PREFILL_GRAPH=0 launches short prefill chunks directly instead of through a cached graph.
+bool prefill_graph_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("SOC_B200_PREFILL_GRAPH");
+        return !(e && std::string(e) == "0");
+    }();
+    return on;
+}
+
 // One prefill chunk (rows in m->d_tokens / d_seq / d_pos already) through a CUDA graph of its
 // whole forward, captured on first use and replayed while the chunk's shape, cache slot,
 // position and buffers stay the same (a generation job's prompt, over and over).  The values the
@@ -970,7 +979,7 @@ void prefill_impl(soc_model* m, soc_kv* kv, int seq, const int32_t* ids, int n, 
         SOCB_CUDA(cudaMemcpyAsync(m->d_pos, ps.data(), sizeof(int) * cn, cudaMemcpyHostToDevice, st));
         const bool last = off + cn == n;
         // (the pageable host vectors are staged by the driver before cudaMemcpyAsync returns)
-        if (m->tp_size == 1 && cn <= kPrefillGraphRows && !m->pf_graph_broken)
+        if (m->tp_size == 1 && cn <= kPrefillGraphRows && !m->pf_graph_broken && prefill_graph_enabled())
             prefill_graph(m, kv, seq, start + off, cn, last);
         else
             forward_rows(m, kv, cn, start + off + cn, last ? cn - 1 : 0, last ? 1 : 0, 1, seq, start + off);

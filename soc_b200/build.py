@@ -22,7 +22,7 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxe
          "-Xcompiler", "-fvisibility=hidden"]
 
 SOURCES = ["runtime.cu", "kernels.cu", "decode_mk.cu", "gemm_tc.cu", "attn_prefill.cu", "nccl_rt.cu", "attn_decode.cu", "tokenizer.cu",
-           "attn_prefill_tc.cu", "tp_allreduce.cu"]
+           "attn_prefill_tc.cu", "tp_allreduce.cu", "linear_mma.cu"]
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:

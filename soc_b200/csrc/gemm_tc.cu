@@ -571,10 +571,12 @@ bool tc_rows_ok(int rows, long long out_f, long long in_f, bool quant) {
         const int t = std::atoi(e);
         return t > 0 && rows >= (quant ? 2 * t : t);
     }
-    // measured crossovers against the CUDA-core GEMV: at 4-15 rows a matrix of 32 M weights
-    // or more already streams faster through the tensor-core GEMM, smaller ones do not
-    const bool big = out_f * in_f >= (32ll << 20);
-    return quant ? (rows >= 32 || (rows >= 16 && big)) : (rows >= 16 || (rows >= 4 && big));
+    // measured crossovers against the small-batch kernels (k_linear_mma): below 16 rows (fp16)
+    // or 32 rows (int8 / int4, whose GEMM route first expands the weights to fp16) those stream
+    // every Qwen3-0.6B shape faster, the lm_head included
+    (void)out_f;
+    (void)in_f;
+    return quant ? rows >= 32 : rows >= 16;
 }
 
 // SOC_B200_TC_OUT=registers keeps the fp32 GEMM outputs on the register-store epilogue.

@@ -341,6 +341,7 @@ void launch_linear(int wfmt, const void* W, const void* scales, int out_f, int i
                    int rows, const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
     if (rows <= 0 || out_f <= 0) return;
     if (ldx % 4 != 0) throw Error(-1, "linear: ldx must be a multiple of 4");
+    if (launch_linear_mma(wfmt, W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st)) return;
     switch (wfmt) {
         case WF_F16: linear_f<WF_F16>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
         case WF_BF16: linear_f<WF_BF16>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;

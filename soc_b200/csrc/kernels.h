@@ -40,6 +40,12 @@ void launch_embed(int wfmt, const void* table, int hidden, int vocab, const int*
 void launch_linear(int wfmt, const void* W, const void* scales, int out_f, int in_f, const float* x, int ldx,
                    int rows, const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st);
 
+// Tensor-core variant for fp16 / int8 g64 / int4 g32 weights and up to 16 input rows per
+// row block (linear_mma.cu); false when the shape or format is outside it (launch_linear then
+// runs the CUDA-core GEMV).  SOC_B200_LINEAR_MMA=0 turns it off.
+bool launch_linear_mma(int wfmt, const void* W, const void* scales, int out_f, int in_f, const float* x, int ldx,
+                       int rows, const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st);
+
 void launch_qk_norm_rope_kv(const float* qkv, const Rows& rows, int hq, int hkv, int head_dim, const float* qn_w,
                             const float* kn_w, float eps, const float2* rope_cs, int rope_len, const KVLayerView& kv,
                             float* q_out, int* err, cudaStream_t st);

@@ -1,0 +1,581 @@
+// Small-batch linear layers on the tensor cores: y[r, o] (mode)= sum_i x'[r, i] * W[o, i] for a
+// handful of input rows r, with W in fp16, int8 group-64 or int4 group-32 (fp16 group scales).
+// It replaces the per-element fp32 FMAs of the CUDA-core GEMV (k_linear), whose integer formats
+// are bound by instruction issue rather than by HBM: here the decode of a weight byte into fp16
+// is 1-2 logic/half2 instructions and the multiply-adds run as mma.sync.m16n8k16 (fp32
+// accumulation).  The reference computes the same products in fp32 on the CPU
+// (src/ops/linear.cpp, src/ops/qmm.cpp); the group-quantised layout is the one its exporter
+// writes (tools/export_qwen3.py).
+//
+// Exactness.  Integer weights are exact in fp16 (|q| <= 127).  An input row is scaled by a power
+// of two 2^e chosen from its largest magnitude and split into two fp16 parts hi + lo, which keep
+// about 22 significant bits; the parts are two B columns of the same MMA, so the fp32 accumulator
+// sees w*hi + w*lo.  Group scales multiply the fp32 result of each group, never a weight.
+//
+// Tiling.  A warp owns 16 output rows (a tile).  Lane (g = lane/4, t = lane%4) streams 16 bytes of
+// rows g and g+8 per chunk: byte offset 64*c + 16*t of the row, so the four lanes of a row read
+// 64 contiguous bytes and a chunk of 16 rows is 1 KB in every format (32 fp16, 64 int8 or 128
+// int4 elements per row).  The k order inside an MMA is a free permutation: the decoded pairs
+// sit in the A registers in whatever order the decode produces them, and the input row is stored
+// in shared memory in the same permuted order, so every B fragment is one 16-byte shared load.
+//
+// Columns.  fp16/int8: column n = 2b + part (b = input row of the CTA's row block, part = hi/lo),
+// four input rows per n8 tile; for int8 the four lanes of a row cover one 64-element group, so one
+// chunk is one group.  int4: the four lanes of a row hold four different 32-element groups, so
+// column n = 2*t' + part takes input values only from lane t' = n/2 (the other B entries are
+// zero): D[row][2t' + part] is then lane t''s group alone and gets that group's scale.  One input
+// row per tile.
+//
+// K split.  When the matrix has too few tiles to give every SM several warps, the 8 warps of a
+// CTA share fewer tiles and each takes every ks-th chunk; the partial sums meet in shared memory.
+#include <algorithm>
+#include <cstdlib>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace socb {
+namespace {
+
+constexpr int LM_WARPS = 8;
+constexpr int LM_THREADS = LM_WARPS * 32;
+constexpr int LM_ZERO_HALVES = 64;  // zero area read by lanes whose B column is empty
+
+template <int F>
+struct MmaFmt;
+template <>
+struct MmaFmt<WF_F16> {
+    static constexpr int KC = 32, GROUP = 0;
+    static constexpr bool PER_T = false;
+    // fp16 weights are their own A pairs: natural k order.
+    static __host__ __device__ __forceinline__ int slot(int k) { return k; }
+};
+template <>
+struct MmaFmt<WF_I8G64> {
+    static constexpr int KC = 64, GROUP = 64;
+    static constexpr bool PER_T = false;
+    // a word (4 int8) decodes to the pairs (k0, k2), (k1, k3)
+    static __host__ __device__ __forceinline__ int slot(int k) {
+        return (k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1);
+    }
+};
+template <>
+struct MmaFmt<WF_I4G32> {
+    static constexpr int KC = 128, GROUP = 32;
+    static constexpr bool PER_T = true;
+    // a word (8 int4) decodes to the pairs (k0, k4), (k1, k5), (k2, k6), (k3, k7)
+    static __host__ __device__ __forceinline__ int slot(int k) { return (k & ~7) | ((k & 3) << 1) | ((k >> 2) & 1); }
+};
+
+// Input rows per n8 tile and tiles for NB input rows.
+template <int F>
+constexpr int rows_per_tile() {
+    return MmaFmt<F>::PER_T ? 1 : 4;
+}
+template <int F, int NB>
+constexpr int tiles_for() {
+    return (NB + rows_per_tile<F>() - 1) / rows_per_tile<F>();
+}
+
+__device__ __forceinline__ uint4 ld_w16(const uint8_t* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ float ld_scale(const __half* p) {
+    unsigned short u;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(u) : "l"(p));
+    return __half2float(__ushort_as_half(u));
+}
+__device__ __forceinline__ uint4 lds16(uint32_t addr) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
+    return r;
+}
+__device__ __forceinline__ uint32_t lop_and_xor(uint32_t v, uint32_t mask, uint32_t flip) {
+    return (v & mask) ^ flip;  // one LOP3
+}
+__device__ __forceinline__ uint32_t h2_add(uint32_t a, uint32_t b) {
+    __half2 r = __hadd2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    __half2 r = __hfma2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b),
+                        *reinterpret_cast<__half2*>(&c));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// D += A * B, m16n8k16, fp16 inputs, fp32 accumulation.  a = {row g k-lo, row g+8 k-lo,
+// row g k-hi, row g+8 k-hi}, b = {k-lo, k-hi}.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// fp16 constants as packed pairs
+constexpr uint32_t H2_M1152 = 0xE480E480u;  // -1152 = -(1024 + 128)
+constexpr uint32_t H2_M1032 = 0xE408E408u;  // -1032 = -(1024 + 8)
+constexpr uint32_t H2_1_16 = 0x2C002C00u;   // 1/16
+constexpr uint32_t H2_M72 = 0xD480D480u;    // -72 = -(1024/16 + 8)
+
+// Decode one 16-byte weight vector of a row into the A pairs of the chunk's MMA steps:
+// p[s][0] = logical k 2t..2t+1 of step s, p[s][1] = logical k 2t+8..2t+9.
+template <int F>
+struct Decode;
+template <>
+struct Decode<WF_F16> {
+    static constexpr int STEPS = 2;
+    static __device__ __forceinline__ void run(const uint4& u, uint32_t (&p)[STEPS][2]) {
+        p[0][0] = u.x; p[0][1] = u.y; p[1][0] = u.z; p[1][1] = u.w;
+    }
+};
+template <>
+struct Decode<WF_I8G64> {
+    static constexpr int STEPS = 4;
+    // (v & 0x00ff00ff) ^ 0x64806480 puts the biased bytes 0 and 2 in the mantissas of 1024:
+    // 1024 + (q + 128); adding -1152 leaves q exactly.
+    static __device__ __forceinline__ void run(const uint4& u, uint32_t (&p)[STEPS][2]) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const uint32_t v = u4_word(u, w);
+            p[w][0] = h2_add(lop_and_xor(v, 0x00FF00FFu, 0x64806480u), H2_M1152);
+            p[w][1] = h2_add(lop_and_xor(v >> 8, 0x00FF00FFu, 0x64806480u), H2_M1152);
+        }
+    }
+};
+template <>
+struct Decode<WF_I4G32> {
+    static constexpr int STEPS = 8;
+    // Nibbles 0/4 land in the low mantissa bits of 1024 (+ (q + 8)); nibbles 1/5 in bits 4-7,
+    // i.e. 1024 + 16 (q + 8), which one fma by 1/16 and -72 brings back to q.  Shifting the word by
+    // 8 does the same for nibbles 2/6 and 3/7.  Every intermediate is exact in fp16.
+    static __device__ __forceinline__ void run(const uint4& u, uint32_t (&p)[STEPS][2]) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const uint32_t v = u4_word(u, w), v8 = v >> 8;
+            p[2 * w][0] = h2_add(lop_and_xor(v, 0x000F000Fu, 0x64086408u), H2_M1032);
+            p[2 * w][1] = h2_fma(lop_and_xor(v, 0x00F000F0u, 0x64806480u), H2_1_16, H2_M72);
+            p[2 * w + 1][0] = h2_add(lop_and_xor(v8, 0x000F000Fu, 0x64086408u), H2_M1032);
+            p[2 * w + 1][1] = h2_fma(lop_and_xor(v8, 0x00F000F0u, 0x64806480u), H2_1_16, H2_M72);
+        }
+    }
+};
+
+// 2^e for |e| <= 126 (exact)
+__device__ __forceinline__ float pow2i_f(int e) { return __int_as_float((e + 127) << 23); }
+
+// Exponent that scales a row whose largest magnitude is mx into [2^14, 2^15).
+__device__ __forceinline__ int row_exponent(float mx) {
+    if (!(mx > 0.0f) || !(mx < 3.0e38f)) return 0;
+    const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xffu) - 127;
+    return max(-100, min(100, 14 - ex));
+}
+
+}  // namespace
+
+// Per-warp work stream.  Big matrices (ks == 1): warp gw of the grid takes tiles gw, gw + NW, ...
+// (NW = warps of one row block) and streams all chunks of each.  Small ones (ks > 1): warp
+// (wt, kp) of a CTA takes chunks kp, kp + ks, ... of its one tile.  The weight chunks run through a
+// ring of UNR register slots, each refilled as soon as it is consumed, so a warp always has UNR
+// chunk loads in flight; the first UNR loads are issued before the wait on the previous kernel
+// (weights are never written by the kernel before this one in the stream).
+template <int F, int NB>
+struct Stream {
+    using M = MmaFmt<F>;
+    static constexpr int NT = tiles_for<F, NB>();
+    static constexpr int UNR = NT <= 2 ? 4 : 2;
+    int tile, c;  // next chunk to load
+    int tstride, kp, ks, nch, tiles, out_f, ng;
+    size_t row_bytes;
+    const uint8_t* W;
+    const __half* S;
+    int g, t;
+    uint4 a[UNR][2];
+    float s0[UNR], s8[UNR];
+
+    __device__ __forceinline__ void load(int u) {
+        if (tile >= tiles) return;
+        const int rg = min(tile * 16 + g, out_f - 1), rg8 = min(tile * 16 + g + 8, out_f - 1);
+        const size_t off = static_cast<size_t>(c) * 64 + 16 * t;
+        a[u][0] = ld_w16(W + static_cast<size_t>(rg) * row_bytes + off);
+        a[u][1] = ld_w16(W + static_cast<size_t>(rg8) * row_bytes + off);
+        if (M::GROUP) {
+            const int gi = M::PER_T ? 4 * c + t : c;
+            s0[u] = ld_scale(S + static_cast<size_t>(rg) * ng + gi);
+            s8[u] = ld_scale(S + static_cast<size_t>(rg8) * ng + gi);
+        }
+        c += ks;
+        if (c >= nch) {
+            c = kp;
+            tile += tstride;
+        }
+    }
+};
+
+// Per-lane results of a tile: rows g and g+8 for input row b(j) of tile j.
+template <int F, int NT>
+__device__ __forceinline__ void tile_results(const float (&acc)[NT][4], float (&res)[NT][2]) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        res[j][0] = acc[j][0] + acc[j][1];
+        res[j][1] = acc[j][2] + acc[j][3];
+        if (MmaFmt<F>::PER_T) {  // the four groups of a chunk sit in the four lanes of the row
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                res[j][h] += __shfl_xor_sync(0xffffffffu, res[j][h], 1);
+                res[j][h] += __shfl_xor_sync(0xffffffffu, res[j][h], 2);
+            }
+        }
+    }
+}
+
+template <int F, int NT>
+__device__ __forceinline__ void tile_store(const float (&res)[NT][2], int o0, int g, int t, int nr, const int* ex_s,
+                                           float* __restrict__ y, int ldy, int r0, int out_f, int mode) {
+    using M = MmaFmt<F>;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const int b = M::PER_T ? j : 4 * j + t;
+        const bool writer = M::PER_T ? t == 0 : true;
+        const float unscale = b < nr ? pow2i_f(-ex_s[b]) : 0.0f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int o = o0 + g + 8 * h;
+            const float v = res[j][h] * unscale;
+            if (mode == LIN_SWIGLU) {
+                const float up = __shfl_down_sync(0xffffffffu, v, 4);  // row o + 1 sits in lane + 4
+                if (writer && b < nr && (g & 1) == 0 && o + 1 < out_f)
+                    y[static_cast<size_t>(r0 + b) * ldy + o / 2] = silu_f(v) * up;
+            } else if (writer && b < nr && o < out_f) {
+                float* dst = y + static_cast<size_t>(r0 + b) * ldy + o;
+                if (mode == LIN_RESIDUAL)
+                    *dst += v;
+                else
+                    *dst = v;
+            }
+        }
+    }
+}
+
+// One CTA: 8 warps, NB input rows (row block yb).  Dynamic shared memory: 2*NB part rows of padk
+// halves (row 2b + part), LM_ZERO_HALVES zeros, then the k-split partials (8 warps x tiles x 2 x 32
+// floats).
+template <int F, int NB>
+__global__ void __launch_bounds__(LM_THREADS, 2)
+    k_linear_mma(const uint8_t* __restrict__ W, const __half* __restrict__ S, int out_f, int in_f,
+                 const float* __restrict__ x, int ldx, int rows, const float* __restrict__ norm_w, float eps,
+                 float* __restrict__ y, int ldy, int mode, int ks, int ny) {
+    using M = MmaFmt<F>;
+    using St = Stream<F, NB>;
+    constexpr int KC = M::KC, G = M::GROUP, NT = St::NT, UNR = St::UNR;
+    constexpr int STEPS = Decode<F>::STEPS;
+    extern __shared__ uint4 lm_smem[];
+    __shared__ float red_s[NB][LM_WARPS][2];
+    __shared__ float rs_s[NB];
+    __shared__ int ex_s[NB];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    // Row blocks that share weight tiles are neighbours in launch order (the second read of the
+    // weights hits L2).
+    const int yb = blockIdx.x % ny, xb = blockIdx.x / ny;
+    const int nxb = gridDim.x / ny;
+    const int r0 = yb * NB;
+    const int nr = min(NB, rows - r0);
+    const int tiles = (out_f + 15) / 16;
+
+    St sr;
+    sr.W = W;
+    sr.S = S;
+    sr.g = g;
+    sr.t = t;
+    sr.ks = ks;
+    sr.nch = in_f / KC;
+    sr.tiles = tiles;
+    sr.out_f = out_f;
+    sr.ng = G ? in_f / G : 0;
+    sr.row_bytes = static_cast<size_t>(in_f) * 64 / KC;
+    if (ks == 1) {
+        sr.tile = xb * LM_WARPS + warp;
+        sr.tstride = nxb * LM_WARPS;
+        sr.kp = 0;
+    } else {
+        sr.tile = xb * (LM_WARPS / ks) + warp / ks;
+        sr.tstride = tiles;  // one tile
+        sr.kp = warp % ks;
+    }
+    sr.c = sr.kp;
+    int pt = sr.tile, pc = sr.kp;  // next chunk to consume
+    const int tstride = sr.tstride;
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) sr.load(u);
+
+    pdl_enter();
+    const int padk = in_f + 8;  // halves; the 16-byte pad spreads the part rows over the banks
+    __half* xs = reinterpret_cast<__half*>(lm_smem);
+    __half* zero = xs + static_cast<size_t>(2 * NB) * padk;
+    float* part = reinterpret_cast<float*>(zero + LM_ZERO_HALVES);
+    // ---- stage the input rows: rmsnorm (optional), power-of-two scale, fp16 hi/lo, permuted k
+    for (int i = tid; i < LM_ZERO_HALVES / 2; i += LM_THREADS) reinterpret_cast<uint32_t*>(zero)[i] = 0u;
+    for (int r = 0; r < nr; ++r) {
+        const float* xr = x + static_cast<size_t>(r0 + r) * ldx;
+        float ss = 0.0f, mx = 0.0f;
+        for (int i = tid * 4; i < in_f; i += LM_THREADS * 4) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + i);
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            float4 nw = make_float4(1.f, 1.f, 1.f, 1.f);
+            if (norm_w != nullptr) nw = *reinterpret_cast<const float4*>(norm_w + i);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * nw.x), fabsf(v.y * nw.y)), fmaxf(fabsf(v.z * nw.z), fabsf(v.w * nw.w))));
+        }
+        ss = warp_sum(ss);
+        mx = warp_max(mx);
+        if (lane == 0) {
+            red_s[r][warp][0] = ss;
+            red_s[r][warp][1] = mx;
+        }
+    }
+    __syncthreads();
+    if (tid < nr) {
+        float ss = 0.0f, mx = 0.0f;
+        for (int w = 0; w < LM_WARPS; ++w) {
+            ss += red_s[tid][w][0];
+            mx = fmaxf(mx, red_s[tid][w][1]);
+        }
+        const float rs = norm_w != nullptr ? 1.0f / sqrtf(ss / static_cast<float>(in_f) + eps) : 1.0f;
+        const int e = row_exponent(mx * rs);
+        rs_s[tid] = rs;
+        ex_s[tid] = e;
+    }
+    __syncthreads();
+    for (int r = 0; r < nr; ++r) {
+        const float* xr = x + static_cast<size_t>(r0 + r) * ldx;
+        const float sc = rs_s[r] * pow2i_f(ex_s[r]);
+        for (int i = tid * 8; i < in_f; i += LM_THREADS * 8) {
+            float v[8];
+            *reinterpret_cast<float4*>(v) = *reinterpret_cast<const float4*>(xr + i);
+            *reinterpret_cast<float4*>(v + 4) = *reinterpret_cast<const float4*>(xr + i + 4);
+            if (norm_w != nullptr) {
+                const float4 a = *reinterpret_cast<const float4*>(norm_w + i);
+                const float4 b = *reinterpret_cast<const float4*>(norm_w + i + 4);
+                v[0] *= a.x; v[1] *= a.y; v[2] *= a.z; v[3] *= a.w;
+                v[4] *= b.x; v[5] *= b.y; v[6] *= b.z; v[7] *= b.w;
+            }
+            __align__(16) __half hi[8], lo[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float s = v[j] * sc;
+                const __half h = __float2half_rn(s);
+                hi[M::slot(j)] = h;  // slot() permutes within aligned groups of 8 (i is a multiple of 8)
+                lo[M::slot(j)] = __float2half_rn(s - __half2float(h));
+            }
+            *reinterpret_cast<uint4*>(xs + static_cast<size_t>(2 * r) * padk + i) = *reinterpret_cast<uint4*>(hi);
+            *reinterpret_cast<uint4*>(xs + static_cast<size_t>(2 * r + 1) * padk + i) = *reinterpret_cast<uint4*>(lo);
+        }
+    }
+    __syncthreads();
+
+    // B source of this lane per tile: shared address of chunk 0 and whether the column has data.
+    uint32_t bbase[NT];
+    bool bval[NT];
+    const uint32_t zaddr = static_cast<uint32_t>(__cvta_generic_to_shared(zero));
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        int b, koff;
+        if (M::PER_T) {
+            b = j;
+            bval[j] = (g >> 1) == t && b < nr;
+            koff = 32 * t;  // lane t's 32-element group inside a chunk
+        } else {
+            b = 4 * j + (g >> 1);
+            bval[j] = b < nr;
+            koff = (KC / 4) * t;
+        }
+        const int row = 2 * min(b, NB - 1) + (g & 1);
+        bbase[j] = static_cast<uint32_t>(__cvta_generic_to_shared(xs + static_cast<size_t>(row) * padk + koff));
+    }
+
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[j][q] = 0.0f;
+
+    constexpr int BV = STEPS / 2;  // 16-byte B loads per chunk and tile (two steps each)
+    const int nch = sr.nch;
+    while (pt < tiles) {
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+            if (pt >= tiles) break;
+            const int c = pc;
+            uint32_t p0[STEPS][2], p8[STEPS][2];
+            Decode<F>::run(sr.a[u][0], p0);
+            Decode<F>::run(sr.a[u][1], p8);
+            const float sc0 = G ? sr.s0[u] : 1.0f, sc8 = G ? sr.s8[u] : 1.0f;
+            sr.load(u);  // refill the slot with the chunk UNR ahead
+            float d[NT][4];
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) d[j][q] = G ? 0.0f : acc[j][q];
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const uint32_t addr = bval[j] ? bbase[j] + static_cast<uint32_t>(c * KC * 2) : zaddr;
+#pragma unroll
+                for (int v = 0; v < BV; ++v) {
+                    const uint4 bb = lds16(addr + 16 * v);
+                    mma16816(d[j], p0[2 * v][0], p8[2 * v][0], p0[2 * v][1], p8[2 * v][1], bb.x, bb.y);
+                    mma16816(d[j], p0[2 * v + 1][0], p8[2 * v + 1][0], p0[2 * v + 1][1], p8[2 * v + 1][1], bb.z,
+                             bb.w);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                if (G) {
+                    acc[j][0] = fmaf(sc0, d[j][0], acc[j][0]);
+                    acc[j][1] = fmaf(sc0, d[j][1], acc[j][1]);
+                    acc[j][2] = fmaf(sc8, d[j][2], acc[j][2]);
+                    acc[j][3] = fmaf(sc8, d[j][3], acc[j][3]);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) acc[j][q] = d[j][q];
+                }
+            }
+            pc += ks;
+            if (pc >= nch) {
+                if (ks == 1) {  // whole tile done: store it and start the next
+                    float res[NT][2];
+                    tile_results<F, NT>(acc, res);
+                    tile_store<F, NT>(res, pt * 16, g, t, nr, ex_s, y, ldy, r0, out_f, mode);
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) acc[j][q] = 0.0f;
+                }
+                pc = sr.kp;
+                pt += tstride;
+            }
+        }
+    }
+    if (ks == 1) return;
+
+    // ---- k split: the ks warps of a tile add their partial sums
+    float res[NT][2];
+    tile_results<F, NT>(acc, res);
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) part[((warp * NT + j) * 2 + h) * 32 + lane] = res[j][h];
+    __syncthreads();
+    const int my_tile = xb * (LM_WARPS / ks) + warp / ks;
+    if (warp % ks != 0 || my_tile >= tiles) return;
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float s = 0.0f;
+            for (int k = 0; k < ks; ++k) s += part[(((warp + k) * NT + j) * 2 + h) * 32 + lane];
+            res[j][h] = s;
+        }
+    tile_store<F, NT>(res, my_tile * 16, g, t, nr, ex_s, y, ldy, r0, out_f, mode);
+}
+
+namespace {
+
+constexpr size_t LM_SMEM_CAP = 110 * 1024;  // two CTAs per SM
+constexpr int LM_TARGET_WARPS = 148 * 16;   // two 8-warp CTAs on every SM
+
+template <int F>
+constexpr int max_nb() {
+    return MmaFmt<F>::PER_T ? 4 : 16;
+}
+
+size_t lm_smem_bytes(int nb, int nt, int in_f) {
+    return static_cast<size_t>(2 * nb) * (in_f + 8) * 2 + LM_ZERO_HALVES * 2 +
+           static_cast<size_t>(LM_WARPS) * nt * 2 * 32 * 4;
+}
+
+bool linear_mma_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("SOC_B200_LINEAR_MMA");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <int F, int NB>
+void linear_mma_nb(const void* W, const void* S, int out_f, int in_f, const float* x, int ldx, int rows,
+                   const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    constexpr int NT = tiles_for<F, NB>();
+    const size_t smem = lm_smem_bytes(NB, NT, in_f);
+    static bool attr_set = false;  // one attribute set per template instance
+    if (!attr_set) {
+        SOCB_CUDA(cudaFuncSetAttribute(k_linear_mma<F, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       200 * 1024));
+        attr_set = true;
+    }
+    const int tiles = (out_f + 15) / 16;
+    const int ny = (rows + NB - 1) / NB;
+    const int nch = in_f / MmaFmt<F>::KC;
+    int ks = 1;
+    while (ks < LM_WARPS && 2 * ks <= nch && static_cast<long long>(tiles) * ny * ks < LM_TARGET_WARPS) ks *= 2;
+    const int tpc = LM_WARPS / ks;
+    int nx = (tiles + tpc - 1) / tpc;
+    // ks == 1: persistent warps, at most two CTAs per SM over all row blocks
+    if (ks == 1) nx = std::max(1, std::min(nx, LM_TARGET_WARPS / LM_WARPS / ny));
+    launch_pdl(k_linear_mma<F, NB>, dim3(nx * ny), dim3(LM_THREADS), smem, st, static_cast<const uint8_t*>(W),
+               static_cast<const __half*>(S), out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, ks, ny);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+template <int F>
+bool linear_mma_f(const void* W, const void* S, int out_f, int in_f, const float* x, int ldx, int rows,
+                  const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    if (in_f % MmaFmt<F>::KC != 0) return false;
+    if (MmaFmt<F>::GROUP && S == nullptr) return false;
+    if (mode == LIN_SWIGLU && out_f % 2 != 0) return false;
+    // Smallest row block that holds all rows, else the largest whose staging fits the budget.
+    int nb = 1;
+    while (nb < rows && nb < max_nb<F>()) nb *= 2;
+    auto fits = [&](int b) {
+        const int nt = (b + rows_per_tile<F>() - 1) / rows_per_tile<F>();
+        return lm_smem_bytes(b, nt, in_f) <= LM_SMEM_CAP;
+    };
+    while (nb > 1 && !fits(nb)) nb /= 2;
+    if (!fits(nb)) return false;
+    switch (nb) {
+        case 1: linear_mma_nb<F, 1>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        case 2: linear_mma_nb<F, 2>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        case 4: linear_mma_nb<F, 4>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        case 8:
+            if constexpr (max_nb<F>() >= 8)
+                linear_mma_nb<F, 8>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+            break;
+        default:
+            if constexpr (max_nb<F>() >= 16)
+                linear_mma_nb<F, 16>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+            break;
+    }
+    return true;
+}
+
+}  // namespace
+
+bool launch_linear_mma(int wfmt, const void* W, const void* scales, int out_f, int in_f, const float* x, int ldx,
+                       int rows, const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    if (!linear_mma_enabled() || rows <= 0 || out_f <= 0 || ldx % 4 != 0) return false;
+    switch (wfmt) {
+        case WF_F16: return linear_mma_f<WF_F16>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+        case WF_I8G64:
+            return linear_mma_f<WF_I8G64>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+        case WF_I4G32:
+            return linear_mma_f<WF_I4G32>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
+        default: return false;
+    }
+}
+
+}  // namespace socb

@@ -43,6 +43,38 @@ def test_quant_linear_kernel_against_fp64(gpu_ctx, fmt, rows, shape):
     assert err <= 1e-4 * (in_f ** 0.5), err
 
 
+@pytest.mark.parametrize("rows", [3, 5, 13])
+@pytest.mark.parametrize("shape", [(1000, 384), (1000, 320), (40, 256)], ids=["ragged_tile", "off_chunk", "tiny"])
+@pytest.mark.parametrize("fmt", ["fp16", "int8_g64", "int4_g32"])
+def test_small_batch_linear_ragged_shapes(gpu_ctx, fmt, rows, shape):
+    """Row counts that leave row blocks part-empty, output counts that leave the last 16-row tile
+    part-empty, and an in_features (320) that is not a whole number of int4 chunks (128): the
+    tensor-core small-batch kernel or the CUDA-core GEMV, whichever takes the shape, against an
+    fp64 product."""
+    import torch
+    out_f, in_f = shape
+    rng = np.random.default_rng(out_f * 7 + in_f + rows)
+    w = rng.standard_normal((out_f, in_f), dtype=np.float32) * np.float32(0.02)
+    x = (rng.standard_normal((rows, in_f), dtype=np.float32) * np.float32(30.0)).astype(np.float32)
+    if fmt == "fp16":
+        wh = w.astype(np.float16)
+        wd, code, sc = wh.astype(np.float64), R.WEIGHTS_F16, None
+        qt = torch.from_numpy(wh).cuda()
+    else:
+        q, s = quantize_groupwise(w, fmt)
+        wd, code = dequantize_groupwise(q, s, fmt).astype(np.float64), FORMATS[fmt]
+        qt = torch.from_numpy(np.ascontiguousarray(q).view(np.uint8)).cuda()
+        sc = torch.from_numpy(np.ascontiguousarray(s)).cuda()
+    ref = x.astype(np.float64) @ wd.T
+    xt = torch.from_numpy(x).cuda()
+    y = torch.full((rows, out_f), float("nan"), device="cuda")
+    gpu_ctx.linear(code, qt.data_ptr(), sc.data_ptr() if sc is not None else None, out_f, in_f, xt.data_ptr(),
+                   rows, y.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    err = np.abs(y.cpu().numpy().astype(np.float64) - ref).max()
+    assert err <= 1e-4 * 30.0 * (in_f ** 0.5), err
+
+
 def test_quant_linear_rejects_missing_scales(gpu_ctx):
     import torch
     w = torch.zeros(64, 256, dtype=torch.uint8, device="cuda")

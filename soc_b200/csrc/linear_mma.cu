@@ -46,14 +46,12 @@ struct MmaFmt;
 template <>
 struct MmaFmt<WF_F16> {
     static constexpr int KC = 32, GROUP = 0;
-    static constexpr bool PER_T = false;
     // fp16 weights are their own A pairs: natural k order.
     static __host__ __device__ __forceinline__ int slot(int k) { return k; }
 };
 template <>
 struct MmaFmt<WF_I8G64> {
     static constexpr int KC = 64, GROUP = 64;
-    static constexpr bool PER_T = false;
     // a word (4 int8) decodes to the pairs (k0, k2), (k1, k3)
     static __host__ __device__ __forceinline__ int slot(int k) {
         return (k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1);
@@ -62,20 +60,21 @@ struct MmaFmt<WF_I8G64> {
 template <>
 struct MmaFmt<WF_I4G32> {
     static constexpr int KC = 128, GROUP = 32;
-    static constexpr bool PER_T = true;
     // a word (8 int4) decodes to the pairs (k0, k4), (k1, k5), (k2, k6), (k3, k7)
     static __host__ __device__ __forceinline__ int slot(int k) { return (k & ~7) | ((k & 3) << 1) | ((k >> 2) & 1); }
 };
 
-// Input rows per n8 tile and tiles for NB input rows.
-template <int F>
-constexpr int rows_per_tile() {
-    return MmaFmt<F>::PER_T ? 1 : 4;
-}
+// Column scheme for NB input rows.  PER_T (int4, one input row): column 2t' + part holds lane t''s
+// group only.  XPOSE (int4, two or more input rows): the four lanes of a row first swap words so
+// that lane t holds word t of each of the chunk's four groups; a group is then two MMA steps over
+// all four lanes and the columns are 2b + part as for int8.  RPT = input rows per n8 tile.
 template <int F, int NB>
-constexpr int tiles_for() {
-    return (NB + rows_per_tile<F>() - 1) / rows_per_tile<F>();
-}
+struct Sch {
+    static constexpr bool PER_T = F == WF_I4G32 && NB == 1;
+    static constexpr bool XPOSE = F == WF_I4G32 && NB > 1;
+    static constexpr int RPT = PER_T ? 1 : 4;
+    static constexpr int NT = (NB + RPT - 1) / RPT;
+};
 
 __device__ __forceinline__ uint4 ld_w16(const uint8_t* p) {
     uint4 r;
@@ -88,6 +87,11 @@ __device__ __forceinline__ float ld_scale(const __half* p) {
     unsigned short u;
     asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(u) : "l"(p));
     return __half2float(__ushort_as_half(u));
+}
+__device__ __forceinline__ uint2 ld_scale4(const __half* p) {  // four consecutive fp16 scales (8-byte aligned)
+    uint2 r;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
 }
 __device__ __forceinline__ uint4 lds16(uint32_t addr) {
     uint4 r;
@@ -130,7 +134,8 @@ struct Decode;
 template <>
 struct Decode<WF_F16> {
     static constexpr int STEPS = 2;
-    static __device__ __forceinline__ void run(const uint4& u, uint32_t (&p)[STEPS][2]) {
+    // steps 2v and 2v+1 of the chunk (v = 0 only)
+    static __device__ __forceinline__ void pair(const uint4& u, int, uint32_t (&p)[2][2]) {
         p[0][0] = u.x; p[0][1] = u.y; p[1][0] = u.z; p[1][1] = u.w;
     }
 };
@@ -139,12 +144,13 @@ struct Decode<WF_I8G64> {
     static constexpr int STEPS = 4;
     // (v & 0x00ff00ff) ^ 0x64806480 puts the biased bytes 0 and 2 in the mantissas of 1024:
     // 1024 + (q + 128); adding -1152 leaves q exactly.
-    static __device__ __forceinline__ void run(const uint4& u, uint32_t (&p)[STEPS][2]) {
+    // steps 2v and 2v+1 of the chunk: words 2v and 2v+1
+    static __device__ __forceinline__ void pair(const uint4& u, int v, uint32_t (&p)[2][2]) {
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            const uint32_t v = u4_word(u, w);
-            p[w][0] = h2_add(lop_and_xor(v, 0x00FF00FFu, 0x64806480u), H2_M1152);
-            p[w][1] = h2_add(lop_and_xor(v >> 8, 0x00FF00FFu, 0x64806480u), H2_M1152);
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t w = u4_word(u, 2 * v + k);
+            p[k][0] = h2_add(lop_and_xor(w, 0x00FF00FFu, 0x64806480u), H2_M1152);
+            p[k][1] = h2_add(lop_and_xor(w >> 8, 0x00FF00FFu, 0x64806480u), H2_M1152);
         }
     }
 };
@@ -154,17 +160,43 @@ struct Decode<WF_I4G32> {
     // Nibbles 0/4 land in the low mantissa bits of 1024 (+ (q + 8)); nibbles 1/5 in bits 4-7,
     // i.e. 1024 + 16 (q + 8), which one fma by 1/16 and -72 brings back to q.  Shifting the word by
     // 8 does the same for nibbles 2/6 and 3/7.  Every intermediate is exact in fp16.
-    static __device__ __forceinline__ void run(const uint4& u, uint32_t (&p)[STEPS][2]) {
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            const uint32_t v = u4_word(u, w), v8 = v >> 8;
-            p[2 * w][0] = h2_add(lop_and_xor(v, 0x000F000Fu, 0x64086408u), H2_M1032);
-            p[2 * w][1] = h2_fma(lop_and_xor(v, 0x00F000F0u, 0x64806480u), H2_1_16, H2_M72);
-            p[2 * w + 1][0] = h2_add(lop_and_xor(v8, 0x000F000Fu, 0x64086408u), H2_M1032);
-            p[2 * w + 1][1] = h2_fma(lop_and_xor(v8, 0x00F000F0u, 0x64806480u), H2_1_16, H2_M72);
-        }
+    static __device__ __forceinline__ void word(uint32_t v, uint32_t (&p)[2][2]) {
+        const uint32_t v8 = v >> 8;
+        p[0][0] = h2_add(lop_and_xor(v, 0x000F000Fu, 0x64086408u), H2_M1032);
+        p[0][1] = h2_fma(lop_and_xor(v, 0x00F000F0u, 0x64806480u), H2_1_16, H2_M72);
+        p[1][0] = h2_add(lop_and_xor(v8, 0x000F000Fu, 0x64086408u), H2_M1032);
+        p[1][1] = h2_fma(lop_and_xor(v8, 0x00F000F0u, 0x64806480u), H2_1_16, H2_M72);
     }
+    // steps 2v and 2v+1 of the chunk: word v
+    static __device__ __forceinline__ void pair(const uint4& u, int v, uint32_t (&p)[2][2]) { word(u4_word(u, v), p); }
 };
+
+// 4 x 4 word transpose across the four lanes of a row (lanes t = 0..3 of one g): on entry lane t
+// holds words 0..3 of its own 16 bytes, on exit word t of lane 0..3's 16 bytes.  Two butterfly
+// stages; each sends the two words that the lane gives up and takes the partner's two.
+__device__ __forceinline__ void quad_transpose(uint4& u, int t) {
+    const bool odd = t & 1, hi = t & 2;
+    uint32_t s0 = odd ? u.x : u.y, s1 = odd ? u.z : u.w;
+    uint32_t r0 = __shfl_xor_sync(0xffffffffu, s0, 1), r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
+    if (odd) {
+        u.x = r0;
+        u.z = r1;
+    } else {
+        u.y = r0;
+        u.w = r1;
+    }
+    s0 = hi ? u.x : u.z;
+    s1 = hi ? u.y : u.w;
+    r0 = __shfl_xor_sync(0xffffffffu, s0, 2);
+    r1 = __shfl_xor_sync(0xffffffffu, s1, 2);
+    if (hi) {
+        u.x = r0;
+        u.y = r1;
+    } else {
+        u.z = r0;
+        u.w = r1;
+    }
+}
 
 // 2^e for |e| <= 126 (exact)
 __device__ __forceinline__ float pow2i_f(int e) { return __int_as_float((e + 127) << 23); }
@@ -178,6 +210,17 @@ __device__ __forceinline__ int row_exponent(float mx) {
 
 }  // namespace
 
+// Weight chunks in flight per warp (8 registers per lane each).  A shared-memory ring filled by
+// cp.async (8 slots of 1 KB per warp) measured slower on every shape: lm_head fp16 b=1 73.5 against
+// 53.2 us.
+#ifndef LM_RING1
+#define LM_RING1 4
+#endif
+template <int F, int NB>
+__host__ __device__ constexpr int ring_depth() {
+    return Sch<F, NB>::XPOSE ? (Sch<F, NB>::NT >= 4 ? 2 : 3) : NB == 1 ? LM_RING1 : Sch<F, NB>::NT <= 2 ? 4 : 2;
+}
+
 // Per-warp work stream.  Big matrices (ks == 1): warp gw of the grid takes tiles gw, gw + NW, ...
 // (NW = warps of one row block) and streams all chunks of each.  Small ones (ks > 1): warp
 // (wt, kp) of a CTA takes chunks kp, kp + ks, ... of its one tile.  The weight chunks run through a
@@ -187,8 +230,9 @@ __device__ __forceinline__ int row_exponent(float mx) {
 template <int F, int NB>
 struct Stream {
     using M = MmaFmt<F>;
-    static constexpr int NT = tiles_for<F, NB>();
-    static constexpr int UNR = NT <= 2 ? 4 : 2;
+    using Z = Sch<F, NB>;
+    static constexpr int NT = Z::NT;
+    static constexpr int UNR = ring_depth<F, NB>();
     int tile, c;  // next chunk to load
     int tstride, kp, ks, nch, tiles, out_f, ng;
     size_t row_bytes;
@@ -197,15 +241,26 @@ struct Stream {
     int g, t;
     uint4 a[UNR][2];
     float s0[UNR], s8[UNR];
+    uint2 v0[UNR], v8[UNR];  // XPOSE: the chunk's four group scales of rows g and g+8
 
+    // The 16-byte vectors of rows g and g+8 of the chunk in slot u.
+    __device__ __forceinline__ void fetch(int u, uint4& a0, uint4& a8) {
+        a0 = a[u][0];
+        a8 = a[u][1];
+    }
+
+    // Refill slot u with the next chunk of the stream.
     __device__ __forceinline__ void load(int u) {
         if (tile >= tiles) return;
         const int rg = min(tile * 16 + g, out_f - 1), rg8 = min(tile * 16 + g + 8, out_f - 1);
         const size_t off = static_cast<size_t>(c) * 64 + 16 * t;
         a[u][0] = ld_w16(W + static_cast<size_t>(rg) * row_bytes + off);
         a[u][1] = ld_w16(W + static_cast<size_t>(rg8) * row_bytes + off);
-        if (M::GROUP) {
-            const int gi = M::PER_T ? 4 * c + t : c;
+        if (Z::XPOSE) {
+            v0[u] = ld_scale4(S + static_cast<size_t>(rg) * ng + 4 * c);
+            v8[u] = ld_scale4(S + static_cast<size_t>(rg8) * ng + 4 * c);
+        } else if (M::GROUP) {
+            const int gi = Z::PER_T ? 4 * c + t : c;
             s0[u] = ld_scale(S + static_cast<size_t>(rg) * ng + gi);
             s8[u] = ld_scale(S + static_cast<size_t>(rg8) * ng + gi);
         }
@@ -218,13 +273,13 @@ struct Stream {
 };
 
 // Per-lane results of a tile: rows g and g+8 for input row b(j) of tile j.
-template <int F, int NT>
+template <int F, int NB, int NT>
 __device__ __forceinline__ void tile_results(const float (&acc)[NT][4], float (&res)[NT][2]) {
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
         res[j][0] = acc[j][0] + acc[j][1];
         res[j][1] = acc[j][2] + acc[j][3];
-        if (MmaFmt<F>::PER_T) {  // the four groups of a chunk sit in the four lanes of the row
+        if (Sch<F, NB>::PER_T) {  // the four groups of a chunk sit in the four lanes of the row
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 res[j][h] += __shfl_xor_sync(0xffffffffu, res[j][h], 1);
@@ -234,14 +289,14 @@ __device__ __forceinline__ void tile_results(const float (&acc)[NT][4], float (&
     }
 }
 
-template <int F, int NT>
+template <int F, int NB, int NT>
 __device__ __forceinline__ void tile_store(const float (&res)[NT][2], int o0, int g, int t, int nr, const int* ex_s,
                                            float* __restrict__ y, int ldy, int r0, int out_f, int mode) {
-    using M = MmaFmt<F>;
+    using Z = Sch<F, NB>;
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
-        const int b = M::PER_T ? j : 4 * j + t;
-        const bool writer = M::PER_T ? t == 0 : true;
+        const int b = Z::PER_T ? j : 4 * j + t;
+        const bool writer = Z::PER_T ? t == 0 : true;
         const float unscale = b < nr ? pow2i_f(-ex_s[b]) : 0.0f;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -311,14 +366,14 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
     sr.c = sr.kp;
     int pt = sr.tile, pc = sr.kp;  // next chunk to consume
     const int tstride = sr.tstride;
-#pragma unroll
-    for (int u = 0; u < UNR; ++u) sr.load(u);
-
-    pdl_enter();
     const int padk = in_f + 8;  // halves; the 16-byte pad spreads the part rows over the banks
     __half* xs = reinterpret_cast<__half*>(lm_smem);
     __half* zero = xs + static_cast<size_t>(2 * NB) * padk;
     float* part = reinterpret_cast<float*>(zero + LM_ZERO_HALVES);
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) sr.load(u);
+
+    pdl_enter();
     // ---- stage the input rows: rmsnorm (optional), power-of-two scale, fp16 hi/lo, permuted k
     for (int i = tid; i < LM_ZERO_HALVES / 2; i += LM_THREADS) reinterpret_cast<uint32_t*>(zero)[i] = 0u;
     for (int r = 0; r < nr; ++r) {
@@ -385,14 +440,14 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
         int b, koff;
-        if (M::PER_T) {
+        if (Sch<F, NB>::PER_T) {
             b = j;
             bval[j] = (g >> 1) == t && b < nr;
             koff = 32 * t;  // lane t's 32-element group inside a chunk
         } else {
             b = 4 * j + (g >> 1);
             bval[j] = b < nr;
-            koff = (KC / 4) * t;
+            koff = Sch<F, NB>::XPOSE ? 8 * t : (KC / 4) * t;  // XPOSE: word t of each group
         }
         const int row = 2 * min(b, NB - 1) + (g & 1);
         bbase[j] = static_cast<uint32_t>(__cvta_generic_to_shared(xs + static_cast<size_t>(row) * padk + koff));
@@ -411,9 +466,38 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
         for (int u = 0; u < UNR; ++u) {
             if (pt >= tiles) break;
             const int c = pc;
-            uint32_t p0[STEPS][2], p8[STEPS][2];
-            Decode<F>::run(sr.a[u][0], p0);
-            Decode<F>::run(sr.a[u][1], p8);
+            if constexpr (Sch<F, NB>::XPOSE) {
+                uint4 w0, w8;
+                sr.fetch(u, w0, w8);
+                const uint2 sv0 = sr.v0[u], sv8 = sr.v8[u];
+                quad_transpose(w0, t);
+                quad_transpose(w8, t);
+                sr.load(u);  // refill the slot with the chunk UNR ahead
+                const float2 sa = h2_to_f2(sv0.x), sb = h2_to_f2(sv0.y);
+                const float2 ta = h2_to_f2(sv8.x), tb = h2_to_f2(sv8.y);
+                const float sg[4] = {sa.x, sa.y, sb.x, sb.y}, sg8[4] = {ta.x, ta.y, tb.x, tb.y};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {  // group 4c + q: word t of it in every lane
+                    uint32_t e0[2][2], e8[2][2];
+                    Decode<WF_I4G32>::word(u4_word(w0, q), e0);
+                    Decode<WF_I4G32>::word(u4_word(w8, q), e8);
+#pragma unroll
+                    for (int j = 0; j < NT; ++j) {
+                        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        const uint32_t addr =
+                            bval[j] ? bbase[j] + static_cast<uint32_t>(c * KC * 2 + 64 * q) : zaddr;
+                        const uint4 bb = lds16(addr);
+                        mma16816(d, e0[0][0], e8[0][0], e0[0][1], e8[0][1], bb.x, bb.y);
+                        mma16816(d, e0[1][0], e8[1][0], e0[1][1], e8[1][1], bb.z, bb.w);
+                        acc[j][0] = fmaf(sg[q], d[0], acc[j][0]);
+                        acc[j][1] = fmaf(sg[q], d[1], acc[j][1]);
+                        acc[j][2] = fmaf(sg8[q], d[2], acc[j][2]);
+                        acc[j][3] = fmaf(sg8[q], d[3], acc[j][3]);
+                    }
+                }
+            } else {
+            uint4 a0, a8;
+            sr.fetch(u, a0, a8);
             const float sc0 = G ? sr.s0[u] : 1.0f, sc8 = G ? sr.s8[u] : 1.0f;
             sr.load(u);  // refill the slot with the chunk UNR ahead
             float d[NT][4];
@@ -421,15 +505,20 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
             for (int j = 0; j < NT; ++j)
 #pragma unroll
                 for (int q = 0; q < 4; ++q) d[j][q] = G ? 0.0f : acc[j][q];
+            uint32_t addr[NT];
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                const uint32_t addr = bval[j] ? bbase[j] + static_cast<uint32_t>(c * KC * 2) : zaddr;
+            for (int j = 0; j < NT; ++j) addr[j] = bval[j] ? bbase[j] + static_cast<uint32_t>(c * KC * 2) : zaddr;
+            // decode two steps at a time right before their MMAs (fewer live registers)
 #pragma unroll
-                for (int v = 0; v < BV; ++v) {
-                    const uint4 bb = lds16(addr + 16 * v);
-                    mma16816(d[j], p0[2 * v][0], p8[2 * v][0], p0[2 * v][1], p8[2 * v][1], bb.x, bb.y);
-                    mma16816(d[j], p0[2 * v + 1][0], p8[2 * v + 1][0], p0[2 * v + 1][1], p8[2 * v + 1][1], bb.z,
-                             bb.w);
+            for (int v = 0; v < BV; ++v) {
+                uint32_t q0[2][2], q8[2][2];
+                Decode<F>::pair(a0, v, q0);
+                Decode<F>::pair(a8, v, q8);
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    const uint4 bb = lds16(addr[j] + 16 * v);
+                    mma16816(d[j], q0[0][0], q8[0][0], q0[0][1], q8[0][1], bb.x, bb.y);
+                    mma16816(d[j], q0[1][0], q8[1][0], q0[1][1], q8[1][1], bb.z, bb.w);
                 }
             }
 #pragma unroll
@@ -444,12 +533,13 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
                     for (int q = 0; q < 4; ++q) acc[j][q] = d[j][q];
                 }
             }
+            }
             pc += ks;
             if (pc >= nch) {
                 if (ks == 1) {  // whole tile done: store it and start the next
                     float res[NT][2];
-                    tile_results<F, NT>(acc, res);
-                    tile_store<F, NT>(res, pt * 16, g, t, nr, ex_s, y, ldy, r0, out_f, mode);
+                    tile_results<F, NB, NT>(acc, res);
+                    tile_store<F, NB, NT>(res, pt * 16, g, t, nr, ex_s, y, ldy, r0, out_f, mode);
 #pragma unroll
                     for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -464,7 +554,7 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
 
     // ---- k split: the ks warps of a tile add their partial sums
     float res[NT][2];
-    tile_results<F, NT>(acc, res);
+    tile_results<F, NB, NT>(acc, res);
 #pragma unroll
     for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -480,7 +570,7 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
             for (int k = 0; k < ks; ++k) s += part[(((warp + k) * NT + j) * 2 + h) * 32 + lane];
             res[j][h] = s;
         }
-    tile_store<F, NT>(res, my_tile * 16, g, t, nr, ex_s, y, ldy, r0, out_f, mode);
+    tile_store<F, NB, NT>(res, my_tile * 16, g, t, nr, ex_s, y, ldy, r0, out_f, mode);
 }
 
 namespace {
@@ -490,7 +580,7 @@ constexpr int LM_TARGET_WARPS = 148 * 16;   // two 8-warp CTAs on every SM
 
 template <int F>
 constexpr int max_nb() {
-    return MmaFmt<F>::PER_T ? 4 : 16;
+    return 16;
 }
 
 size_t lm_smem_bytes(int nb, int nt, int in_f) {
@@ -509,7 +599,7 @@ bool linear_mma_enabled() {
 template <int F, int NB>
 void linear_mma_nb(const void* W, const void* S, int out_f, int in_f, const float* x, int ldx, int rows,
                    const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
-    constexpr int NT = tiles_for<F, NB>();
+    constexpr int NT = Sch<F, NB>::NT;
     const size_t smem = lm_smem_bytes(NB, NT, in_f);
     static bool attr_set = false;  // one attribute set per template instance
     if (!attr_set) {
@@ -542,7 +632,7 @@ bool linear_mma_f(const void* W, const void* S, int out_f, int in_f, const float
     int nb = 1;
     while (nb < rows && nb < max_nb<F>()) nb *= 2;
     auto fits = [&](int b) {
-        const int nt = (b + rows_per_tile<F>() - 1) / rows_per_tile<F>();
+        const int nt = (F == WF_I4G32 && b == 1) ? 1 : (b + 3) / 4;
         return lm_smem_bytes(b, nt, in_f) <= LM_SMEM_CAP;
     };
     while (nb > 1 && !fits(nb)) nb /= 2;

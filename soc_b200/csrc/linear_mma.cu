@@ -121,6 +121,15 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D = A * B (zero accumulator input).
+__device__ __forceinline__ void mma16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
 // fp16 constants as packed pairs
 constexpr uint32_t H2_M1152 = 0xE480E480u;  // -1152 = -(1024 + 128)
 constexpr uint32_t H2_M1032 = 0xE408E408u;  // -1032 = -(1024 + 8)
@@ -218,7 +227,9 @@ __device__ __forceinline__ int row_exponent(float mx) {
 #endif
 template <int F, int NB>
 __host__ __device__ constexpr int ring_depth() {
-    return Sch<F, NB>::XPOSE ? (Sch<F, NB>::NT >= 4 ? 2 : 3) : NB == 1 ? LM_RING1 : Sch<F, NB>::NT <= 2 ? 4 : 2;
+    return Sch<F, NB>::XPOSE ? (Sch<F, NB>::NT >= 4 ? 2 : 3)
+           : NB == 1         ? LM_RING1
+                             : (Sch<F, NB>::NT == 1 ? 4 : Sch<F, NB>::NT == 2 ? 3 : 2);
 }
 
 // Per-warp work stream.  Big matrices (ks == 1): warp gw of the grid takes tiles gw, gw + NW, ...
@@ -227,18 +238,25 @@ __host__ __device__ constexpr int ring_depth() {
 // ring of UNR register slots, each refilled as soon as it is consumed, so a warp always has UNR
 // chunk loads in flight; the first UNR loads are issued before the wait on the previous kernel
 // (weights are never written by the kernel before this one in the stream).
-template <int F, int NB>
+template <int F, int NB, int DEPTH = ring_depth<F, NB>()>
 struct Stream {
     using M = MmaFmt<F>;
     using Z = Sch<F, NB>;
     static constexpr int NT = Z::NT;
-    static constexpr int UNR = ring_depth<F, NB>();
+    static constexpr int UNR = DEPTH;
+    // scale index step per chunk: one int8 group, four int4 groups
+    static constexpr int SSTEP = F == WF_I4G32 ? 4 : 1;
     int tile, c;  // next chunk to load
     int tstride, kp, ks, nch, tiles, out_f, ng;
     size_t row_bytes;
     const uint8_t* W;
     const __half* S;
     int g, t;
+    // addresses of the next load (rows g and g+8), set per tile and advanced per chunk
+    const uint8_t* wp0;
+    const uint8_t* wp8;
+    const __half* sp0;
+    const __half* sp8;
     uint4 a[UNR][2];
     float s0[UNR], s8[UNR];
     uint2 v0[UNR], v8[UNR];  // XPOSE: the chunk's four group scales of rows g and g+8
@@ -249,25 +267,43 @@ struct Stream {
         a8 = a[u][1];
     }
 
+    // Addresses of chunk c of the current tile.
+    __device__ __forceinline__ void set_tile() {
+        const int rg = min(tile * 16 + g, out_f - 1), rg8 = min(tile * 16 + g + 8, out_f - 1);
+        const size_t off = static_cast<size_t>(c) * 64 + 16 * t;
+        wp0 = W + static_cast<size_t>(rg) * row_bytes + off;
+        wp8 = W + static_cast<size_t>(rg8) * row_bytes + off;
+        if (M::GROUP) {
+            const int gi = SSTEP * c + (Z::PER_T ? t : 0);
+            sp0 = S + static_cast<size_t>(rg) * ng + gi;
+            sp8 = S + static_cast<size_t>(rg8) * ng + gi;
+        }
+    }
+
     // Refill slot u with the next chunk of the stream.
     __device__ __forceinline__ void load(int u) {
         if (tile >= tiles) return;
-        const int rg = min(tile * 16 + g, out_f - 1), rg8 = min(tile * 16 + g + 8, out_f - 1);
-        const size_t off = static_cast<size_t>(c) * 64 + 16 * t;
-        a[u][0] = ld_w16(W + static_cast<size_t>(rg) * row_bytes + off);
-        a[u][1] = ld_w16(W + static_cast<size_t>(rg8) * row_bytes + off);
+        a[u][0] = ld_w16(wp0);
+        a[u][1] = ld_w16(wp8);
         if (Z::XPOSE) {
-            v0[u] = ld_scale4(S + static_cast<size_t>(rg) * ng + 4 * c);
-            v8[u] = ld_scale4(S + static_cast<size_t>(rg8) * ng + 4 * c);
+            v0[u] = ld_scale4(sp0);
+            v8[u] = ld_scale4(sp8);
         } else if (M::GROUP) {
-            const int gi = Z::PER_T ? 4 * c + t : c;
-            s0[u] = ld_scale(S + static_cast<size_t>(rg) * ng + gi);
-            s8[u] = ld_scale(S + static_cast<size_t>(rg8) * ng + gi);
+            s0[u] = ld_scale(sp0);
+            s8[u] = ld_scale(sp8);
         }
         c += ks;
-        if (c >= nch) {
+        if (c < nch) {
+            wp0 += 64 * ks;
+            wp8 += 64 * ks;
+            if (M::GROUP) {
+                sp0 += SSTEP * ks;
+                sp8 += SSTEP * ks;
+            }
+        } else {
             c = kp;
             tile += tstride;
+            if (tile < tiles) set_tile();
         }
     }
 };
@@ -364,6 +400,7 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
         sr.kp = warp % ks;
     }
     sr.c = sr.kp;
+    if (sr.tile < tiles) sr.set_tile();
     int pt = sr.tile, pc = sr.kp;  // next chunk to consume
     const int tstride = sr.tstride;
     const int padk = in_f + 8;  // halves; the 16-byte pad spreads the part rows over the banks
@@ -483,11 +520,11 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
                     Decode<WF_I4G32>::word(u4_word(w8, q), e8);
 #pragma unroll
                     for (int j = 0; j < NT; ++j) {
-                        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        float d[4];
                         const uint32_t addr =
                             bval[j] ? bbase[j] + static_cast<uint32_t>(c * KC * 2 + 64 * q) : zaddr;
                         const uint4 bb = lds16(addr);
-                        mma16816(d, e0[0][0], e8[0][0], e0[0][1], e8[0][1], bb.x, bb.y);
+                        mma16816_z(d, e0[0][0], e8[0][0], e0[0][1], e8[0][1], bb.x, bb.y);
                         mma16816(d, e0[1][0], e8[1][0], e0[1][1], e8[1][1], bb.z, bb.w);
                         acc[j][0] = fmaf(sg[q], d[0], acc[j][0]);
                         acc[j][1] = fmaf(sg[q], d[1], acc[j][1]);
@@ -501,10 +538,12 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
             const float sc0 = G ? sr.s0[u] : 1.0f, sc8 = G ? sr.s8[u] : 1.0f;
             sr.load(u);  // refill the slot with the chunk UNR ahead
             float d[NT][4];
+            if (!G) {
 #pragma unroll
-            for (int j = 0; j < NT; ++j)
+                for (int j = 0; j < NT; ++j)
 #pragma unroll
-                for (int q = 0; q < 4; ++q) d[j][q] = G ? 0.0f : acc[j][q];
+                    for (int q = 0; q < 4; ++q) d[j][q] = acc[j][q];
+            }
             uint32_t addr[NT];
 #pragma unroll
             for (int j = 0; j < NT; ++j) addr[j] = bval[j] ? bbase[j] + static_cast<uint32_t>(c * KC * 2) : zaddr;
@@ -517,7 +556,10 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
 #pragma unroll
                 for (int j = 0; j < NT; ++j) {
                     const uint4 bb = lds16(addr[j] + 16 * v);
-                    mma16816(d[j], q0[0][0], q8[0][0], q0[0][1], q8[0][1], bb.x, bb.y);
+                    if (G && v == 0)  // a group starts here: zero accumulator input
+                        mma16816_z(d[j], q0[0][0], q8[0][0], q0[0][1], q8[0][1], bb.x, bb.y);
+                    else
+                        mma16816(d[j], q0[0][0], q8[0][0], q0[0][1], q8[0][1], bb.x, bb.y);
                     mma16816(d[j], q0[1][0], q8[1][0], q0[1][1], q8[1][1], bb.z, bb.w);
                 }
             }
@@ -571,6 +613,276 @@ __global__ void __launch_bounds__(LM_THREADS, 2)
             res[j][h] = s;
         }
     tile_store<F, NB, NT>(res, my_tile * 16, g, t, nr, ex_s, y, ldy, r0, out_f, mode);
+}
+
+// ------------------------------------------------------------ int8 weights on the integer MMA
+// int8 g64 weights enter mma.sync.m16n8k32.s8.s8 as they are (no decode).  An input row is scaled
+// by 2^e so that its largest magnitude lies in [2^21, 2^22), rounded to an integer and split into
+// three balanced base-256 limbs (each in [-128, 127]); limb l of input row 2j + bl is B column
+// 3 bl + l of tile j (two input rows per n8 tile, columns 6 and 7 empty).  The int32 products are
+// exact; a chunk is one 64-element group, whose int32 result times the group scale is accumulated
+// in fp32 per column, and the limbs are recombined (x 2^(8 l)) when the tile is stored.  Lane
+// (g, t) holds k 16t..16t+15 of the chunk for rows g and g+8: words 0/1 are the two k quarters of
+// MMA step 0 and words 2/3 those of step 1, the natural k order, so the limbs are staged as they are.
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma16832_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Exponent that scales a row whose largest magnitude is mx into [2^21, 2^22).
+__device__ __forceinline__ int row_exponent_i(float mx) {
+    if (!(mx > 0.0f) || !(mx < 3.0e38f)) return 0;
+    const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xffu) - 127;
+    return max(-100, min(100, 21 - ex));
+}
+
+// Lane (g, t): columns 2t and 2t+1 of rows g and g+8.  Weighted by 2^(8 l) and summed per input row
+// (columns 0-2 row 0, 3-5 row 1) over the four lanes of the row, then stored like tile_store.
+template <int NB, int NT>
+__device__ __forceinline__ void imma_tile_store(const float (&acc)[NT][4], int o0, int g, int t, int nr,
+                                                const int* ex_s, float* __restrict__ y, int ldy, int r0, int out_f,
+                                                int mode) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        float p[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};  // [input row of the tile][h]
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int col = 2 * t + k;
+            const float w = col % 3 == 0 ? 1.0f : col % 3 == 1 ? 256.0f : 65536.0f;
+            if (col < 3) {
+                p[0][0] = fmaf(w, acc[j][k], p[0][0]);
+                p[0][1] = fmaf(w, acc[j][2 + k], p[0][1]);
+            } else if (col < 6) {
+                p[1][0] = fmaf(w, acc[j][k], p[1][0]);
+                p[1][1] = fmaf(w, acc[j][2 + k], p[1][1]);
+            }
+        }
+#pragma unroll
+        for (int bl = 0; bl < 2; ++bl)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                p[bl][h] += __shfl_xor_sync(0xffffffffu, p[bl][h], 1);
+                p[bl][h] += __shfl_xor_sync(0xffffffffu, p[bl][h], 2);
+            }
+#pragma unroll
+        for (int bl = 0; bl < 2; ++bl) {
+            const int b = 2 * j + bl;
+            const bool writer = t == bl;
+            const float unscale = b < nr ? pow2i_f(-ex_s[b]) : 0.0f;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int o = o0 + g + 8 * h;
+                const float v = p[bl][h] * unscale;
+                if (mode == LIN_SWIGLU) {
+                    const float up = __shfl_down_sync(0xffffffffu, v, 4);  // row o + 1 sits in lane + 4
+                    if (writer && b < nr && (g & 1) == 0 && o + 1 < out_f)
+                        y[static_cast<size_t>(r0 + b) * ldy + o / 2] = silu_f(v) * up;
+                } else if (writer && b < nr && o < out_f) {
+                    float* dst = y + static_cast<size_t>(r0 + b) * ldy + o;
+                    if (mode == LIN_RESIDUAL)
+                        *dst += v;
+                    else
+                        *dst = v;
+                }
+            }
+        }
+    }
+}
+
+// int8 g64, NB input rows (1, 2, 4 or 8).  Dynamic shared memory: 3*NB limb rows of padk bytes (row
+// 3b + l), 64 zero bytes, then the k-split partials (8 warps x tiles x 4 x 32 floats).
+template <int NB>
+__global__ void __launch_bounds__(LM_THREADS, 2)
+    k_linear_imma(const uint8_t* __restrict__ W, const __half* __restrict__ S, int out_f, int in_f,
+                  const float* __restrict__ x, int ldx, int rows, const float* __restrict__ norm_w, float eps,
+                  float* __restrict__ y, int ldy, int mode, int ks, int ny) {
+    using St = Stream<WF_I8G64, NB, NB <= 2 ? 4 : NB == 4 ? 3 : 2>;
+    constexpr int KC = 64, G = 64, NT = (NB + 1) / 2, UNR = St::UNR;
+    extern __shared__ uint4 lm_smem[];
+    __shared__ float red_s[NB][LM_WARPS][2];
+    __shared__ float rs_s[NB];
+    __shared__ int ex_s[NB];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int yb = blockIdx.x % ny, xb = blockIdx.x / ny;
+    const int nxb = gridDim.x / ny;
+    const int r0 = yb * NB;
+    const int nr = min(NB, rows - r0);
+    const int tiles = (out_f + 15) / 16;
+
+    St sr;
+    sr.W = W;
+    sr.S = S;
+    sr.g = g;
+    sr.t = t;
+    sr.ks = ks;
+    sr.nch = in_f / KC;
+    sr.tiles = tiles;
+    sr.out_f = out_f;
+    sr.ng = in_f / G;
+    sr.row_bytes = static_cast<size_t>(in_f);
+    if (ks == 1) {
+        sr.tile = xb * LM_WARPS + warp;
+        sr.tstride = nxb * LM_WARPS;
+        sr.kp = 0;
+    } else {
+        sr.tile = xb * (LM_WARPS / ks) + warp / ks;
+        sr.tstride = tiles;  // one tile
+        sr.kp = warp % ks;
+    }
+    sr.c = sr.kp;
+    if (sr.tile < tiles) sr.set_tile();
+    int pt = sr.tile, pc = sr.kp;  // next chunk to consume
+    const int tstride = sr.tstride;
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) sr.load(u);
+
+    pdl_enter();
+    const int padk = in_f % 128 == 0 ? in_f + 64 : in_f;  // bytes; limb rows alternate 64-byte bank halves
+    int8_t* xs = reinterpret_cast<int8_t*>(lm_smem);
+    int8_t* zero = xs + static_cast<size_t>(3 * NB) * padk;
+    float* part = reinterpret_cast<float*>(zero + 64);
+    if (tid < 16) reinterpret_cast<uint32_t*>(zero)[tid] = 0u;
+    for (int r = 0; r < nr; ++r) {
+        const float* xr = x + static_cast<size_t>(r0 + r) * ldx;
+        float ss = 0.0f, mx = 0.0f;
+        for (int i = tid * 4; i < in_f; i += LM_THREADS * 4) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + i);
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            float4 nw = make_float4(1.f, 1.f, 1.f, 1.f);
+            if (norm_w != nullptr) nw = *reinterpret_cast<const float4*>(norm_w + i);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * nw.x), fabsf(v.y * nw.y)), fmaxf(fabsf(v.z * nw.z), fabsf(v.w * nw.w))));
+        }
+        ss = warp_sum(ss);
+        mx = warp_max(mx);
+        if (lane == 0) {
+            red_s[r][warp][0] = ss;
+            red_s[r][warp][1] = mx;
+        }
+    }
+    __syncthreads();
+    if (tid < nr) {
+        float ss = 0.0f, mx = 0.0f;
+        for (int w = 0; w < LM_WARPS; ++w) {
+            ss += red_s[tid][w][0];
+            mx = fmaxf(mx, red_s[tid][w][1]);
+        }
+        const float rs = norm_w != nullptr ? 1.0f / sqrtf(ss / static_cast<float>(in_f) + eps) : 1.0f;
+        rs_s[tid] = rs;
+        ex_s[tid] = row_exponent_i(mx * rs);
+    }
+    __syncthreads();
+    for (int r = 0; r < nr; ++r) {
+        const float* xr = x + static_cast<size_t>(r0 + r) * ldx;
+        const float sc = rs_s[r] * pow2i_f(ex_s[r]);
+        for (int i = tid * 4; i < in_f; i += LM_THREADS * 4) {
+            float4 v = *reinterpret_cast<const float4*>(xr + i);
+            if (norm_w != nullptr) {
+                const float4 nw = *reinterpret_cast<const float4*>(norm_w + i);
+                v.x *= nw.x; v.y *= nw.y; v.z *= nw.z; v.w *= nw.w;
+            }
+            const float e4[4] = {v.x, v.y, v.z, v.w};
+            uint32_t lw[3] = {0u, 0u, 0u};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int xi = __float2int_rn(e4[k] * sc);
+                const int l0 = ((xi + 128) & 255) - 128;
+                const int rr = (xi - l0) >> 8;
+                const int l1 = ((rr + 128) & 255) - 128;
+                const int l2 = (rr - l1) >> 8;
+                lw[0] |= (static_cast<uint32_t>(l0) & 255u) << (8 * k);
+                lw[1] |= (static_cast<uint32_t>(l1) & 255u) << (8 * k);
+                lw[2] |= (static_cast<uint32_t>(l2) & 255u) << (8 * k);
+            }
+#pragma unroll
+            for (int l = 0; l < 3; ++l) *reinterpret_cast<uint32_t*>(xs + static_cast<size_t>(3 * r + l) * padk + i) = lw[l];
+        }
+    }
+    __syncthreads();
+
+    // B source of this lane per tile: column g = limb g % 3 of input row 2j + g / 3 (g < 6)
+    uint32_t bbase[NT];
+    bool bval[NT];
+    const uint32_t zaddr = static_cast<uint32_t>(__cvta_generic_to_shared(zero));
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const int b = 2 * j + g / 3, l = g % 3;
+        bval[j] = g < 6 && b < nr;
+        const int row = 3 * min(b, NB - 1) + l;
+        bbase[j] = static_cast<uint32_t>(__cvta_generic_to_shared(xs + static_cast<size_t>(row) * padk + 16 * t));
+    }
+
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[j][q] = 0.0f;
+
+    const int nch = sr.nch;
+    while (pt < tiles) {
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+            if (pt >= tiles) break;
+            const int c = pc;
+            uint4 a0, a8;
+            sr.fetch(u, a0, a8);
+            const float sc0 = sr.s0[u], sc8 = sr.s8[u];
+            sr.load(u);  // refill the slot with the chunk UNR ahead
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const uint32_t addr = bval[j] ? bbase[j] + static_cast<uint32_t>(c * KC) : zaddr;
+                const uint4 bb = lds16(addr);
+                int d[4];
+                imma16832_z(d, a0.x, a8.x, a0.y, a8.y, bb.x, bb.y);
+                imma16832(d, a0.z, a8.z, a0.w, a8.w, bb.z, bb.w);
+                acc[j][0] = fmaf(sc0, static_cast<float>(d[0]), acc[j][0]);
+                acc[j][1] = fmaf(sc0, static_cast<float>(d[1]), acc[j][1]);
+                acc[j][2] = fmaf(sc8, static_cast<float>(d[2]), acc[j][2]);
+                acc[j][3] = fmaf(sc8, static_cast<float>(d[3]), acc[j][3]);
+            }
+            pc += ks;
+            if (pc >= nch) {
+                if (ks == 1) {  // whole tile done: store it and start the next
+                    imma_tile_store<NB, NT>(acc, pt * 16, g, t, nr, ex_s, y, ldy, r0, out_f, mode);
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) acc[j][q] = 0.0f;
+                }
+                pc = sr.kp;
+                pt += tstride;
+            }
+        }
+    }
+    if (ks == 1) return;
+
+    // ---- k split: the ks warps of a tile add their partial sums
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) part[((warp * NT + j) * 4 + q) * 32 + lane] = acc[j][q];
+    __syncthreads();
+    const int my_tile = xb * (LM_WARPS / ks) + warp / ks;
+    if (warp % ks != 0 || my_tile >= tiles) return;
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float s = 0.0f;
+            for (int k = 0; k < ks; ++k) s += part[(((warp + k) * NT + j) * 4 + q) * 32 + lane];
+            acc[j][q] = s;
+        }
+    imma_tile_store<NB, NT>(acc, my_tile * 16, g, t, nr, ex_s, y, ldy, r0, out_f, mode);
 }
 
 namespace {
@@ -653,6 +965,62 @@ bool linear_mma_f(const void* W, const void* S, int out_f, int in_f, const float
     return true;
 }
 
+size_t imma_smem_bytes(int nb, int in_f) {
+    const size_t padk = in_f % 128 == 0 ? in_f + 64 : in_f;
+    return static_cast<size_t>(3 * nb) * padk + 64 + static_cast<size_t>(LM_WARPS) * ((nb + 1) / 2) * 4 * 32 * 4;
+}
+
+bool linear_imma_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("SOC_B200_LINEAR_IMMA");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <int NB>
+void linear_imma_nb(const void* W, const void* S, int out_f, int in_f, const float* x, int ldx, int rows,
+                    const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    const size_t smem = imma_smem_bytes(NB, in_f);
+    static bool attr_set = false;  // one attribute set per template instance
+    if (!attr_set) {
+        SOCB_CUDA(cudaFuncSetAttribute(k_linear_imma<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr_set = true;
+    }
+    const int tiles = (out_f + 15) / 16;
+    const int ny = (rows + NB - 1) / NB;
+    const int nch = in_f / 64;
+    int ks = 1;
+    while (ks < LM_WARPS && 2 * ks <= nch && static_cast<long long>(tiles) * ny * ks < LM_TARGET_WARPS) ks *= 2;
+    const int tpc = LM_WARPS / ks;
+    int nx = (tiles + tpc - 1) / tpc;
+    if (ks == 1) nx = std::max(1, std::min(nx, LM_TARGET_WARPS / LM_WARPS / ny));
+    launch_pdl(k_linear_imma<NB>, dim3(nx * ny), dim3(LM_THREADS), smem, st, static_cast<const uint8_t*>(W),
+               static_cast<const __half*>(S), out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, ks, ny);
+    SOCB_CUDA(cudaGetLastError());
+    count_launches(1);
+}
+
+// int8 g64 on the integer MMA for one or two input rows (measured: lm_head b=1 29.2 against 31.8 us on
+// the fp16 MMA; at 4 rows it loses, 36.7 against 33.9 us); false when the shape is outside it.
+constexpr int IMMA_MAX_ROWS = 2;
+bool linear_imma(const void* W, const void* S, int out_f, int in_f, const float* x, int ldx, int rows,
+                 const float* norm_w, float eps, float* y, int ldy, int mode, cudaStream_t st) {
+    if (!linear_imma_enabled() || rows > IMMA_MAX_ROWS || in_f % 64 != 0 || S == nullptr) return false;
+    if (mode == LIN_SWIGLU && out_f % 2 != 0) return false;
+    int nb = 1;
+    while (nb < rows) nb *= 2;
+    while (nb > 1 && imma_smem_bytes(nb, in_f) > LM_SMEM_CAP) nb /= 2;
+    if (imma_smem_bytes(nb, in_f) > LM_SMEM_CAP) return false;
+    switch (nb) {
+        case 1: linear_imma_nb<1>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        case 2: linear_imma_nb<2>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        case 4: linear_imma_nb<4>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+        default: linear_imma_nb<8>(W, S, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st); break;
+    }
+    return true;
+}
+
 }  // namespace
 
 bool launch_linear_mma(int wfmt, const void* W, const void* scales, int out_f, int in_f, const float* x, int ldx,
@@ -661,6 +1029,7 @@ bool launch_linear_mma(int wfmt, const void* W, const void* scales, int out_f, i
     switch (wfmt) {
         case WF_F16: return linear_mma_f<WF_F16>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
         case WF_I8G64:
+            if (linear_imma(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st)) return true;
             return linear_mma_f<WF_I8G64>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);
         case WF_I4G32:
             return linear_mma_f<WF_I4G32>(W, scales, out_f, in_f, x, ldx, rows, norm_w, eps, y, ldy, mode, st);

@@ -565,18 +565,20 @@ int tc_min_rows() {
     return e && *e ? std::atoi(e) : 16;
 }
 
-bool tc_rows_ok(int rows, long long out_f, long long in_f, bool quant) {
+bool tc_rows_ok(int rows, long long out_f, long long in_f, int wfmt) {
+    const bool quant = wfmt == WF_I8G64 || wfmt == WF_I4G32;
     const char* e = std::getenv("SOC_B200_TC_MIN_ROWS");
     if (e && *e) {
         const int t = std::atoi(e);
         return t > 0 && rows >= (quant ? 2 * t : t);
     }
-    // measured crossovers against the small-batch kernels (k_linear_mma): below 16 rows (fp16)
-    // or 32 rows (int8 / int4, whose GEMM route first expands the weights to fp16) those stream
-    // every Qwen3-0.6B shape faster, the lm_head included
+    // measured crossovers against the small-batch kernels (linear_mma.cu: fp16, int8, int4): below
+    // 32 rows those stream every Qwen3-0.6B shape faster, the lm_head included (fp16 at 16 rows:
+    // 7.0 against 12.6 us for 2048 x 1024, 71.8 against 77.1 us for the lm_head); at 64 rows the GEMM
+    // wins.  bf16 has only the CUDA-core GEMV below the GEMM, which the GEMM beats from 16 rows.
     (void)out_f;
     (void)in_f;
-    return quant ? rows >= 32 : rows >= 16;
+    return rows >= (wfmt == WF_BF16 ? 16 : 32);
 }
 
 // SOC_B200_TC_OUT=registers keeps the fp32 GEMM outputs on the register-store epilogue.

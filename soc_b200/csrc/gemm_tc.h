@@ -14,9 +14,9 @@ bool tc_available();
 // SOC_B200_TC_MIN_ROWS overrides it, 0 disables the path); group-quantised linears use it
 // from 2 * that many rows (their weights are expanded to fp16 first).
 int tc_min_rows();
-// Whether a linear of `rows` input rows and an out_f x in_f matrix runs on the tensor-core
-// GEMM (SOC_B200_TC_MIN_ROWS, when set, is a plain row threshold).
-bool tc_rows_ok(int rows, long long out_f, long long in_f, bool quant);
+// Whether a linear of `rows` input rows and an out_f x in_f matrix of weight format wfmt runs on
+// the tensor-core GEMM (SOC_B200_TC_MIN_ROWS, when set, is a plain row threshold).
+bool tc_rows_ok(int rows, long long out_f, long long in_f, int wfmt);
 // Up to this many rows (default 512, SOC_B200_TC_SPLIT_MAX_ROWS) the GEMM input rows are
 // carried as hi + lo halves (two MMAs per K step, about 22 significand bits); above it as
 // one half (prefill-sized GEMMs, tensor-throughput bound).

@@ -770,7 +770,7 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
     // Tensor-core GEMMs for the block linears once there are enough rows (group-quantised
     // weights are first expanded to fp16, one matrix at a time, into m->wdq).
     const bool quant = m->wfmt == WF_I8G64 || m->wfmt == WF_I4G32;
-    const bool tc = m->tc_ok && tc_rows_ok(n, static_cast<long long>(2 * I), H, quant);
+    const bool tc = m->tc_ok && tc_rows_ok(n, static_cast<long long>(2 * I), H, m->wfmt);
     const bool split = n <= tc_split_max_rows();
     const int gf = m->gfmt;
     CUtensorMap a_h{}, a_att{}, a_act{}, a_h_lo{}, a_att_lo{}, a_act_lo{};
@@ -851,7 +851,7 @@ void forward_rows(soc_model* m, soc_kv* kv, int n, int max_visible, int lm_first
     }
     if (lm_rows > 0) {
         ensure_logits(m, lm_rows);
-        if (m->tc_ok && tc_rows_ok(lm_rows, m->v_loc, H, false)) {
+        if (m->tc_ok && tc_rows_ok(lm_rows, m->v_loc, H, m->efmt)) {
             // many rows (batched decode): tensor-core GEMM over the vocab rows
             const bool lsplit = lm_rows <= tc_split_max_rows();
             CUtensorMap a_lm{}, a_lm_lo{};
@@ -1925,7 +1925,7 @@ int soc_b200_linear(soc_ctx* ctx, int weight_format, const void* w, const void* 
         if (f < 0) throw Error(SOC_B200_ERR_INVALID, "linear: weight format not supported by this build");
         cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
         const bool quant = f == WF_I8G64 || f == WF_I4G32;
-        const bool tc = tc_rows_ok(rows, out_features, in_features, quant) && in_features % 64 == 0 && tc_available();
+        const bool tc = tc_rows_ok(rows, out_features, in_features, f) && in_features % 64 == 0 && tc_available();
         if (!tc) {
             launch_linear(f, w, scales, out_features, in_features, x, in_features, rows, nullptr, 0.0f, y,
                           out_features, LIN_STORE, st);

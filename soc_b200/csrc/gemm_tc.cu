@@ -573,12 +573,14 @@ bool tc_rows_ok(int rows, long long out_f, long long in_f, int wfmt) {
         return t > 0 && rows >= (quant ? 2 * t : t);
     }
     // measured crossovers against the small-batch kernels (linear_mma.cu: fp16, int8, int4): below
-    // 32 rows those stream every Qwen3-0.6B shape faster, the lm_head included (fp16 at 16 rows:
-    // 7.0 against 12.6 us for 2048 x 1024, 71.8 against 77.1 us for the lm_head); at 64 rows the GEMM
-    // wins.  bf16 has only the CUDA-core GEMV below the GEMM, which the GEMM beats from 16 rows.
+    // 32 rows (fp16) those stream every Qwen3-0.6B shape faster, the lm_head included (fp16 at 16
+    // rows: 7.0 against 12.6 us for 2048 x 1024, 71.8 against 77.1 us for the lm_head); int8 / int4,
+    // whose GEMM route first expands the matrix to fp16, stay on them up to 63 rows (at 32 rows the
+    // int8 lm_head takes 92.5 against 178.8 us, the 1-6 M-weight matrices 6-14 against 13-17 us).
+    // bf16 has only the CUDA-core GEMV below the GEMM, which the GEMM beats from 16 rows.
     (void)out_f;
     (void)in_f;
-    return rows >= (wfmt == WF_BF16 ? 16 : 32);
+    return rows >= (wfmt == WF_BF16 ? 16 : quant ? 64 : 32);
 }
 
 // SOC_B200_TC_OUT=registers keeps the fp32 GEMM outputs on the register-store epilogue.

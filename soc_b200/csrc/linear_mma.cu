@@ -4,8 +4,9 @@
 // are bound by instruction issue rather than by HBM: here the decode of a weight byte into fp16
 // is 1-2 logic/half2 instructions and the multiply-adds run as mma.sync.m16n8k16 (fp32
 // accumulation).  The reference computes the same products in fp32 on the CPU
-// (src/ops/linear.cpp, src/ops/qmm.cpp); the group-quantised layout is the one its exporter
-// writes (tools/export_qwen3.py).
+// (Mac/cpu/src/linear.cpp:51-84, Linear::Forward; its int8 matmul Mac/cpu/header/matrix_ops.h:308-350
+// over the per-column rule of QuantizeMatMulRhs8, matrix_ops.h:42-73); the group-wise int8 g64 / int4 g32
+// layout with fp16 scales is this build's bundle format, which keeps that rule inside each group.
 //
 // Exactness.  Integer weights are exact in fp16 (|q| <= 127).  An input row is scaled by a power
 // of two 2^e chosen from its largest magnitude and split into two fp16 parts hi + lo, which keep

@@ -43,7 +43,7 @@ def test_quant_linear_kernel_against_fp64(gpu_ctx, fmt, rows, shape):
     assert err <= 1e-4 * (in_f ** 0.5), err
 
 
-@pytest.mark.parametrize("rows", [2, 3, 5, 13])
+@pytest.mark.parametrize("rows", [2, 3, 5, 13, 37])
 @pytest.mark.parametrize("shape", [(1000, 384), (1000, 320), (40, 256)], ids=["ragged_tile", "off_chunk", "tiny"])
 @pytest.mark.parametrize("fmt", ["fp16", "int8_g64", "int4_g32"])
 def test_small_batch_linear_ragged_shapes(gpu_ctx, fmt, rows, shape):

@@ -998,12 +998,13 @@ bool linear_mma_f(const void* W, const void* S, int out_f, int in_f, const float
     if (MmaFmt<F>::GROUP && S == nullptr) return false;
     if (mode == LIN_SWIGLU && out_f % 2 != 0) return false;
     // Smallest row block that holds all rows, else the largest whose staging fits the budget.
-    // Matrices under 32 M weights take at most 8 rows per row block (two blocks at 16 rows: half the
-    // staging per CTA, twice the CTAs): measured 7.0 -> 5.2 us for 2048 x 1024 at 16 rows, 9.3 against
-    // 8.0 us for 3072 x 1024, and the config-0 16-token prefill 1.85 -> 1.79 ms.
+    // Matrices under 32 M weights take at most 4 rows per row block (four blocks at 16 rows: a quarter
+    // of the staging per CTA, four times the CTAs): the config-0 16-token prefill measured 1.85 ms with
+    // 16-row blocks, 1.79 with 8-row and 1.77 with 4-row ones (2048 x 1024 at 16 rows: 7.0 -> 5.2 us at
+    // 8-row blocks).
     const bool big = static_cast<long long>(out_f) * in_f >= (32ll << 20);
     int nb = 1;
-    while (nb < rows && nb < max_nb<F>() && (nb < 8 || big)) nb *= 2;
+    while (nb < rows && nb < max_nb<F>() && (nb < 4 || big)) nb *= 2;
     auto fits = [&](int b) {
         const int nt = (F == WF_I4G32 && b == 1) ? 1 : (b + 3) / 4;
         return lm_smem_bytes(b, nt, in_f) <= LM_SMEM_CAP;
